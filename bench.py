@@ -1,0 +1,382 @@
+#!/usr/bin/env python
+"""GLM-4-9B decode benchmark: tok/s and HBM-roofline MBU on 1..8 B200s (TP=N).
+
+Workload: the full GLM-4-9B-shaped dense model (40 layers, hidden 4096,
+32 q / 2 kv heads, head_dim 128, SwiGLU 13696, vocab 151552), random-init
+bf16 weights generated on the device (seed 0), KV cache pre-filled by running
+the seeded uniform-random prompt (context 1024) through the model, then greedy
+decode steps at batch B (default 1).  One step = one token per sequence.
+
+    python bench.py [--gpus N --steps K --warmup W --batch B --ctx C]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (TP = N, one rank per GPU)
+    python bench.py --impl reference                          (CPU arm, see below)
+
+value:  B / step time, whole job (the TP ranks cooperate on the same tokens:
+        total work is fixed as N grows, scaling "strong"); step time is the
+        CUDA-event time of K CUDA-graph replays with device-resident inputs,
+        max over ranks.
+e2e:    the same metric through the public API with host buffers: every step
+        copies the fed token ids from pinned host memory, replays the step and
+        reads the greedy ids back (the reference's per-step host sync).
+--impl reference: the reference's algorithm on the host cores.  JAX/Flax (the
+        reference's runtime) is not installable on this image, so this times
+        the numpy restatement under oracle/ (kind "port") on a bounded sample
+        (one GLM-4-9B decoder layer at context C plus the LM head, scaled to 40
+        layers), rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "GLM-4-9B decode tok/s & HBM-roofline MBU at TP=1/2/4/8, batch 1 and 32"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--ctx", type=int, default=1024)
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--impl", choices=["jsx", "reference"], default="jsx")
+    ap.add_argument("--no-pdl", action="store_true", help="disable programmatic dependent launch")
+    ap.add_argument("--layers", type=int, default=40, help=argparse.SUPPRESS)
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# CPU arm (oracle restatement, host cores)
+# ---------------------------------------------------------------------------
+
+def blas_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return int(max(n)) if n else 1
+    except Exception:
+        return 1
+
+
+def cpu_decode_sample(ctx: int, reps: int = 2) -> dict:
+    """One GLM-4-9B decoder layer (batch 1, KV cache of ctx rows) and the final
+    norm + LM head, timed with the oracle; tok/s = 1 / (40 * t_layer + t_head)."""
+    ref = importlib.import_module("oracle.glm4_ref")
+    cfg = ref.GLMConfig(num_hidden_layers=1)
+    p = ref.init_params(ref.GLMConfig(num_hidden_layers=1, vocab_size=8), seed=0)  # one layer's shapes
+    lp = p.layers[0]
+    rng = np.random.default_rng(0)
+    lm_head = ref.bf16(rng.standard_normal((cfg.vocab_size, cfg.hidden_size), dtype=np.float32) * 0.02)
+    norm = np.ones(cfg.hidden_size, np.float32)
+    L = ctx + 1
+    kc = ref.bf16(rng.standard_normal((1, L, cfg.num_key_value_heads, cfg.head_dim), dtype=np.float32))
+    vc = ref.bf16(rng.standard_normal((1, L, cfg.num_key_value_heads, cfg.head_dim), dtype=np.float32))
+    h = ref.bf16(rng.standard_normal((1, 1, cfg.hidden_size), dtype=np.float32))
+    inv = ref.rope_inv_freq(cfg.head_dim)
+    pos = np.full((1, 1), ctx, np.int32)
+    mask = ref.make_decode_mask(ctx, L)
+    t_layer, t_head = [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        y = ref.decoder_layer(lp, cfg, h, pos, mask, (kc, vc), np.array([ctx]), inv)
+        t1 = time.perf_counter()
+        logits = ref.bf16(ref.rmsnorm(y, norm, cfg.rms_norm_eps) @ lm_head.T)
+        ref.argmax_first(logits[:, -1])
+        t2 = time.perf_counter()
+        t_layer.append(t1 - t0)
+        t_head.append(t2 - t1)
+    tl, th = min(t_layer), min(t_head)
+    per_tok = 40 * tl + th
+    return {"value": 1.0 / per_tok, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
+            "sample": (f"numpy oracle (oracle/glm4_ref.py), batch 1: one GLM-4-9B decoder layer at "
+                       f"context {ctx} ({tl * 1e3:.1f} ms) x 40 + final norm/LM head/argmax "
+                       f"({th * 1e3:.1f} ms), best of {reps}; reference JAX runtime not installable")}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cb = cpu_decode_sample(args.ctx)
+    v = cb["value"]
+    line = {
+        "metric": METRIC, "impl": "reference", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 / v, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(args),
+        "cpu_baseline": cb,
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(args) -> dict:
+    return {"workload": (f"GLM-4-9B-shaped dense decode (40 layers, random-init bf16), batch {args.batch}, "
+                         f"KV cache pre-filled to context {args.ctx}, TP={args.gpus}"),
+            "batch": args.batch, "context": args.ctx, "tp": args.gpus, "parallelism": f"tp{args.gpus}",
+            "l2": "inputs larger than L2: every step streams all weights (>= 2.2 GB per GPU)"}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+
+FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASON_NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+
+class ClockSampler:
+    def __init__(self, device_index):
+        import torch
+        self.path = tempfile.mktemp(prefix="jsx_clocks_", suffix=".csv")
+        sel = str(device_index)
+        try:
+            uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+            sel = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+        except Exception:
+            pass
+        self.proc = None
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", sel], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(REASON_NAMES, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def measured_hbm_peak() -> tuple[float, str]:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(key: str):
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(key)
+    except Exception:
+        return None
+
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    jsx = importlib.import_module("e2e-jaxscale_b200")
+    K = jsx.kernels
+    K.set_pdl(not args.no_pdl)
+    dev = torch.device("cuda", local)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    mesh = jsx.create_mesh(tp=args.gpus)
+    cfg = jsx.ModelConfig(num_hidden_layers=args.layers)
+    model = jsx.GLM4ForCausalLM(cfg, mesh)
+    model.init_random(seed=args.seed)
+    B, C = args.batch, args.ctx
+    e2e_steps = max(16, args.steps // 2)
+    L = C + 2 * args.warmup + args.steps + e2e_steps + 8
+    st = jsx.DecodeState(model, B, L)
+    graph = jsx.DecodeGraph(model, st)
+    barrier()
+
+    # prefill the context with seeded uniform prompt ids (one graph replay per position)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab_size, (B, C)).astype(np.int32)
+    prompt_dev = torch.from_numpy(prompt).to(dev)
+    st.pos.zero_()
+    for s in range(C):
+        st.ids.copy_(prompt_dev[:, s])
+        if s < C - 1:
+            graph.prefill()
+        else:
+            graph.decode()
+    for _ in range(args.warmup):
+        graph.decode()
+    torch.cuda.synchronize()
+    barrier()
+
+    clocks = ClockSampler(local)
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(args.steps):
+        graph.decode()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    # end to end through the public API, host buffers
+    host_in = torch.empty(B, dtype=torch.int32).pin_memory()
+    host_out = torch.empty(B, dtype=torch.int32).pin_memory()
+    host_in.copy_(st.ids.cpu())
+    for _ in range(args.warmup):
+        st.ids.copy_(host_in, non_blocking=True)
+        graph.decode()
+        host_out.copy_(st.ids, non_blocking=True)
+        stream.synchronize()
+        host_in.copy_(host_out)
+    barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        st.ids.copy_(host_in, non_blocking=True)
+        graph.decode()
+        host_out.copy_(st.ids, non_blocking=True)
+        stream.synchronize()
+        host_in.copy_(host_out)
+    t1 = time.perf_counter()
+    barrier()
+    e2e_ms = max_over_ranks((t1 - t0) * 1e3 / e2e_steps)
+    clk = clocks.stop()
+
+    # dominant kernel: fused gate/up + SwiGLU GEMV, one launch per layer's weights
+    m = min(B, K.MAX_DECODE_TOKENS)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in model.layers]
+    torch.cuda.synchronize()
+    for (a, b), lp in zip(ev, model.layers):
+        a.record(stream)
+        K.gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m])
+        b.record(stream)
+    torch.cuda.synchronize()
+    dur = [a.elapsed_time(b) for a, b in ev]
+    kern_ms = statistics.mean(dur)
+    lp0 = model.layers[0]
+    kern_bytes = lp0.w_gu.numel() * 2 + m * cfg.hidden_size * 2 + m * model.I_l * 2 + cfg.hidden_size * 2
+    peak, peak_kind = measured_hbm_peak()
+    achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
+    trafkey = f"gate_up_swiglu_tp{args.gpus}_m{m}"
+
+    # step bytes: weights streamed + KV rows read/written + embedding rows
+    c = cfg
+    kv_bytes = B * c.num_hidden_layers * 2 * (C + args.warmup + args.steps) * model.nkv_l * c.head_dim * 2
+    step_bytes = model.weight_bytes() + kv_bytes + B * c.hidden_size * 2
+    mbu = step_bytes / (ms * 1e-3) / (peak * 1e9)
+    ref_model_bytes = 2 * (c.num_hidden_layers * (
+        c.hidden_size * c.num_attention_heads * c.head_dim * 2 + c.hidden_size * c.num_key_value_heads * c.head_dim * 2
+        + c.num_attention_heads * c.head_dim + 2 * c.num_key_value_heads * c.head_dim
+        + 3 * c.hidden_size * c.intermediate_size + 2 * c.hidden_size) + 2 * c.vocab_size * c.hidden_size + c.hidden_size)
+    mbu_ref = ref_model_bytes / (ms * 1e-3) / (peak * 1e9 * args.gpus)
+
+    launches = model.kernels_per_step(B, head=True) * args.steps
+    cpu = cpu_decode_sample(C) if (rank == 0 and world == 1) else None
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": B / (ms * 1e-3), "unit": "tok/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init N(0,0.02) bf16 weights (device RNG seed 0), uniform prompt ids seed 1",
+            "config": workload_config(args),
+            "mbu": mbu, "bytes_per_step_per_gpu": step_bytes,
+            "mbu_reference_formula": mbu_ref,
+            "roofline": {"bound": "hbm", "kernel": "jsx_gate_up_swiglu (k_gemv<M,EPI_SWIGLU>)",
+                         "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"{peak_kind} hbm_gbs (burst, kernel timed alone)",
+                         "traffic": ncu_traffic(trafkey), "algorithmic_bytes_per_launch": kern_bytes,
+                         "launch_ms": kern_ms},
+            "cpu_baseline": cpu,
+            "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
+            "gpu_launches": launches,
+            "pdl": K.pdl_enabled(),
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    graph.release()
+    torch.cuda.synchronize()
+    barrier()
+    mesh.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,73 @@
+// Tensor-parallel group: device view of the symmetric NVLink buffers.
+//
+// Every rank owns one buffer with the same layout; peers write into it with
+// plain P2P stores (CUDA IPC mappings), then publish with a release store of
+// the call's epoch into a flag.  Waiters acquire-load their own flags.
+//
+// Epochs come from a per-rank device counter (`state[kCalls]`) that the last
+// CTA of every collective kernel advances, so the protocol needs no host
+// argument per call and survives CUDA-graph replay.  Data slots alternate by
+// epoch parity: a peer can be at most one call ahead (it cannot finish call
+// e+1 before this rank has pushed call e+1, which happens after this rank
+// finished reading call e), so parity e&1 is never overwritten while read.
+// Flags compare with (int)(flag - epoch) >= 0 so a peer that already moved to
+// the next epoch still satisfies the wait.
+#pragma once
+
+#include "common.cuh"
+
+namespace jsx {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxCtas = 1024;  // flag rows for per-CTA publication; row kMaxCtas is the LM-head row
+
+enum { kCalls = 0, kDone = 1, kError = 2, kStateWords = 8 };
+
+struct CommDev {
+  char* base[kMaxRanks];  // symmetric buffer of every rank, as mapped in this process
+  uint32_t* state;        // local, not shared: calls, done, error
+  int rank;
+  int world;
+  int max_tokens;
+  int hidden;
+  size_t off_data;        // float [2][world][max_tokens][hidden]
+  size_t off_keys;        // u64   [2][world][max_tokens]
+  unsigned long long timeout_ns;
+};
+
+__device__ __forceinline__ uint32_t* flag_ptr(const CommDev& c, int r, int row, int src) {
+  return reinterpret_cast<uint32_t*>(c.base[r]) + (size_t)row * c.world + src;
+}
+__device__ __forceinline__ float* data_ptr(const CommDev& c, int r, int par, int src, int m) {
+  return reinterpret_cast<float*>(c.base[r] + c.off_data) +
+         ((size_t)(par * c.world + src) * c.max_tokens + m) * c.hidden;
+}
+__device__ __forceinline__ unsigned long long* key_ptr(const CommDev& c, int r, int par, int src) {
+  return reinterpret_cast<unsigned long long*>(c.base[r] + c.off_keys) +
+         (size_t)(par * c.world + src) * c.max_tokens;
+}
+
+__device__ __forceinline__ uint32_t read_epoch(const CommDev& c) {
+  return *reinterpret_cast<volatile uint32_t*>(c.state + kCalls) + 1u;
+}
+
+// Bounded wait until this rank's flag (row, src) reaches `epoch`.  On timeout
+// the error word is set and the caller proceeds (its output is then garbage
+// and the host reports JSX_ETIMEDOUT through jsx_comm_check).
+__device__ __forceinline__ void wait_flag(const CommDev& c, int row, int src, uint32_t epoch) {
+  const uint32_t* f = flag_ptr(c, c.rank, row, src);
+  const uint64_t t0 = globaltimer();
+  uint32_t it = 0;
+  while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+    ++it;
+    if ((it & 63u) == 0) {
+      if (globaltimer() - t0 > c.timeout_ns || it > (1u << 28)) {
+        atomicOr(c.state + kError, 1u);
+        return;
+      }
+    }
+    __nanosleep(32);
+  }
+}
+
+}  // namespace jsx

@@ -1,0 +1,581 @@
+// Decode GEMV family (M <= 8 tokens): the weight-streaming kernels of one
+// GLM-4 decoder step, each with its prologue/epilogue fused.
+//
+//   jsx_linear                 LinearBase (layers/linear.py:57-82), optional RMSNorm prologue
+//   jsx_qkv_rope_cache         input_layernorm + q/k/v + bias + RoPE + KV-cache write
+//   jsx_gate_up_swiglu         post_attention_layernorm + gate/up + SwiGLU
+//   jsx_row_linear_allreduce   o_proj/down_proj + TP all-reduce (NVLink P2P) + residual
+//   jsx_lmhead_argmax          final norm + LM head + greedy argmax (+ cross-rank argmax)
+//
+// Layout: weights are packed row-major [N_rows][K] (each output row's K inputs
+// contiguous), so a warp streams whole 512-byte lines with 16-byte
+// non-allocating loads.  The activations (M x K bf16, optionally RMS-
+// normalised) are staged once per CTA in shared memory.
+//
+// Work split: rows are processed in groups of kRows by one warp; group g goes
+// to CTA g % grid so that every SM gets work even when the row count is small
+// (o_proj/down at N = 4096).  The grid is persistent (<= resident CTAs), which
+// the peer protocol of the row-parallel kernel relies on: every CTA of every
+// rank is resident, so a CTA that waits for its peers never blocks a CTA they
+// wait for.
+//
+// Programmatic dependent launch: each kernel issues its first weight loads
+// BEFORE griddepcontrol.wait (weights never depend on the previous kernel) and
+// performs every activation read and every global write after it.
+#include <stdio.h>
+
+#include "comm.cuh"
+#include "common.cuh"
+#include "launch.cuh"
+
+namespace jsx {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRows = 2;    // rows per warp group (the qkv / gate_up packings assume 2)
+constexpr int kUnroll = 8;  // 16-byte vectors per lane per row in flight
+constexpr int kMaxM = 8;
+
+enum Epi { EPI_LINEAR = 0, EPI_QKV = 1, EPI_SWIGLU = 2, EPI_ROWAR = 3, EPI_LMHEAD = 4 };
+
+struct GemvArgs {
+  const bf16* x;      // [M][K]
+  const bf16* gamma;  // RMSNorm gain [K] or null
+  float eps;
+  const bf16* w;      // packed [N][K]
+  int M, K, N;        // N = packed rows
+  // EPI_LINEAR
+  const bf16* bias;
+  bf16* y;            // [M][N] (linear), q_out [M][nq*hd] (qkv), act [M][N/2] (swiglu)
+  // EPI_QKV
+  const float* inv_freq;
+  const int32_t* pos;
+  bf16* kc;
+  bf16* vc;
+  int nq, nkv, hd, rot, max_seq, tps;
+  // EPI_ROWAR
+  bf16* h;            // residual [M][N]
+  // EPI_LMHEAD
+  int vocab_offset;
+  unsigned long long* keys;  // [M] workspace (zero on entry, left zero)
+  uint32_t* done;            // workspace counter (zero on entry, left zero)
+  int32_t* ids;              // [M]
+};
+
+// ---- activations -> shared memory (optionally RMS-normalised) --------------
+// layers/normalization.py:31-37: y = bf16((x * rsqrt(mean(x^2) + eps)) * g), fp32 inside.
+template <int M>
+__device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
+  const int nvec = a.K >> 3;
+  const uint4* xv = reinterpret_cast<const uint4*>(a.x);
+  uint4* sv = reinterpret_cast<uint4*>(xs);
+  if (a.gamma == nullptr) {
+    for (int i = threadIdx.x; i < M * nvec; i += blockDim.x) sv[i] = xv[i];
+    __syncthreads();
+    return;
+  }
+  __shared__ float red[M][kWarps];
+  __shared__ float rstd[M];
+  float ss[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) ss[m] = 0.f;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      float f[8];
+      unpack8(xv[m * nvec + v], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss[m] = fmaf(f[j], f[j], ss[m]);
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    float s = warp_sum(ss[m]);
+    if (lane == 0) red[m][warp] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < M) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t += red[threadIdx.x][w];
+    rstd[threadIdx.x] = 1.0f / sqrtf(t / (float)a.K + a.eps);
+  }
+  __syncthreads();
+  const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
+  for (int i = threadIdx.x; i < M * nvec; i += blockDim.x) {
+    const int m = i / nvec, v = i - m * nvec;
+    float f[8], g[8];
+    unpack8(xv[i], f);
+    unpack8(gv[v], g);
+    const float r = rstd[m];
+    uint4 o;
+    o.x = pack2((f[0] * r) * g[0], (f[1] * r) * g[1]);
+    o.y = pack2((f[2] * r) * g[2], (f[3] * r) * g[3]);
+    o.z = pack2((f[4] * r) * g[4], (f[5] * r) * g[5]);
+    o.w = pack2((f[6] * r) * g[6], (f[7] * r) * g[7]);
+    sv[i] = o;
+  }
+  __syncthreads();
+}
+
+// ---- weight batches -----------------------------------------------------------
+struct Batch {
+  uint4 w[kUnroll][kRows];
+};
+
+__device__ __forceinline__ void load_batch(Batch& b, const uint4* __restrict__ wv, int nvec,
+                                           int base, int lane) {
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int v = base + u * 32 + lane;
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+      b.w[u][r] = (v < nvec) ? ld_stream(wv + (size_t)r * nvec + v) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int M>
+__device__ __forceinline__ void fma_batch(const Batch& b, const uint4* __restrict__ xv, int nvec,
+                                          int base, int lane, float (&acc)[kRows][M]) {
+#pragma unroll
+  for (int u = 0; u < kUnroll; ++u) {
+    const int v = base + u * 32 + lane;
+    if (v < nvec) {
+      float wf[kRows][8];
+#pragma unroll
+      for (int r = 0; r < kRows; ++r) unpack8(b.w[u][r], wf[r]);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float xf[8];
+        unpack8(xv[m * nvec + v], xf);
+#pragma unroll
+        for (int r = 0; r < kRows; ++r)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[r][m] = fmaf(wf[r][j], xf[j], acc[r][m]);
+      }
+    }
+  }
+}
+
+// Value (r, m) of a warp-reduced accumulator tile, selected without dynamic
+// register indexing.
+template <int M>
+__device__ __forceinline__ float pick(const float (&acc)[kRows][M], int r, int m) {
+  float v = 0.f;
+#pragma unroll
+  for (int rr = 0; rr < kRows; ++rr)
+#pragma unroll
+    for (int mm = 0; mm < M; ++mm)
+      if (rr == r && mm == m) v = acc[rr][mm];
+  return v;
+}
+
+// ---- epilogues ------------------------------------------------------------------
+// qkv packing (jsx_pack_qkv): per head hd/2 groups; group j < rot/2 holds rows
+// (j, j + rot/2) (a neox rotary pair), group j >= rot/2 holds the pass-through
+// pair (rot + 2(j - rot/2), +1).  Heads: q (nq), then k (nkv), then v (nkv).
+template <int M>
+__device__ __forceinline__ void epi_qkv(const GemvArgs& a, int g, const float (&acc)[kRows][M],
+                                        int lane) {
+  if (lane >= M) return;
+  const int m = lane;
+  const int gph = a.hd >> 1;
+  const int head = g / gph, j = g - head * gph;
+  const int rh = a.rot >> 1;
+  int d0, d1;
+  bool rotary;
+  if (j < rh) { d0 = j; d1 = j + rh; rotary = true; }
+  else { d0 = a.rot + 2 * (j - rh); d1 = d0 + 1; rotary = false; }
+  const int col0 = head * a.hd + d0, col1 = head * a.hd + d1;  // index into q|k|v
+  float x1 = rbf(pick<M>(acc, 0, m));
+  float x2 = rbf(pick<M>(acc, 1, m));
+  if (a.bias) {
+    x1 = rbf(x1 + ldbf(a.bias + col0));
+    x2 = rbf(x2 + ldbf(a.bias + col1));
+  }
+  const int p = a.pos[m];
+  const bool is_v = head >= a.nq + a.nkv;
+  if (rotary && !is_v) {
+    // layers/rotary.py:56-58 (fp32 angle, bf16 cos/sin) and :88-91 (half split)
+    float s, c;
+    sincosf((float)p * a.inv_freq[j], &s, &c);
+    c = rbf(c);
+    s = rbf(s);
+    const float o1 = rbf(rbf(x1 * c) - rbf(x2 * s));
+    const float o2 = rbf(rbf(x2 * c) + rbf(x1 * s));
+    x1 = o1;
+    x2 = o2;
+  }
+  if (head < a.nq) {
+    bf16* q = a.y + (size_t)m * a.nq * a.hd + head * a.hd;
+    q[d0] = __float2bfloat16_rn(x1);
+    q[d1] = __float2bfloat16_rn(x2);
+  } else {
+    const int kvh = is_v ? head - a.nq - a.nkv : head - a.nq;
+    const int b = m / a.tps;
+    // dynamic_update_slice clamps the start row into [0, max_seq - 1] (layers/attention.py:127-133)
+    const int slot = p < 0 ? 0 : (p >= a.max_seq ? a.max_seq - 1 : p);
+    bf16* dst = (is_v ? a.vc : a.kc) + (((size_t)b * a.max_seq + slot) * a.nkv + kvh) * a.hd;
+    dst[d0] = __float2bfloat16_rn(x1);
+    dst[d1] = __float2bfloat16_rn(x2);
+  }
+}
+
+// gate/up packing (jsx_pack_gate_up): group j holds rows (gate_j, up_j).
+// models/glm4.py:47-49 with jax.nn.silu(x) = x * sigmoid(x) on bf16 arrays.
+template <int M>
+__device__ __forceinline__ void epi_swiglu(const GemvArgs& a, int g, const float (&acc)[kRows][M],
+                                           int lane) {
+  if (lane >= M) return;
+  const int m = lane;
+  const float gate = rbf(pick<M>(acc, 0, m));
+  const float up = rbf(pick<M>(acc, 1, m));
+  const float sig = rbf(1.0f / (1.0f + expf(-gate)));
+  const float act = rbf(rbf(gate * sig) * up);
+  a.y[(size_t)m * (a.N >> 1) + g] = __float2bfloat16_rn(act);
+}
+
+// ---- the kernel ------------------------------------------------------------------
+template <int M, int EPI>
+__global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = a.K >> 3;
+  const int ngroups = a.N / kRows;
+  const int grid = gridDim.x;
+  const uint4* wbase = reinterpret_cast<const uint4*>(a.w);
+  const size_t group_vecs = (size_t)kRows * nvec;
+
+  int g = blockIdx.x + grid * warp;
+  Batch bt;
+  if (g < ngroups) load_batch(bt, wbase + (size_t)g * group_vecs, nvec, 0, lane);
+
+  pdl_wait();
+  pdl_launch_dependents();
+
+  const bool multi = (EPI == EPI_ROWAR || EPI == EPI_LMHEAD) && c.world > 1;
+  uint32_t epoch = 0;
+  int par = 0;
+  if (EPI == EPI_ROWAR && multi) {
+    epoch = read_epoch(c);
+    par = epoch & 1;
+  }
+
+  stage_x<M>(a, xs);
+  const uint4* xv = reinterpret_cast<const uint4*>(xs);
+
+  unsigned long long best[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) best[m] = 0ull;
+
+  for (; g < ngroups; g += grid * kWarps) {
+    const uint4* wv = wbase + (size_t)g * group_vecs;
+    float acc[kRows][M];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
+
+    for (int base = 0; base < nvec; base += 32 * kUnroll) {
+      if (base > 0) load_batch(bt, wv, nvec, base, lane);
+      fma_batch<M>(bt, xv, nvec, base, lane, acc);
+    }
+    // Prefetch the next group's first batch before the reductions/epilogue.
+    const int gn = g + grid * kWarps;
+    if (gn < ngroups) load_batch(bt, wbase + (size_t)gn * group_vecs, nvec, 0, lane);
+
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+
+    if constexpr (EPI == EPI_LINEAR) {
+      if (lane < kRows * M) {
+        const int r = lane / M, m = lane - (lane / M) * M;
+        const int row = g * kRows + r;
+        float v = rbf(pick<M>(acc, r, m));
+        if (a.bias) v = rbf(v + ldbf(a.bias + row));
+        a.y[(size_t)m * a.N + row] = __float2bfloat16_rn(v);
+      }
+    } else if constexpr (EPI == EPI_QKV) {
+      epi_qkv<M>(a, g, acc, lane);
+    } else if constexpr (EPI == EPI_SWIGLU) {
+      epi_swiglu<M>(a, g, acc, lane);
+    } else if constexpr (EPI == EPI_ROWAR) {
+      if (lane < kRows * M) {
+        const int r = lane / M, m = lane - (lane / M) * M;
+        const int row = g * kRows + r;
+        const float v = pick<M>(acc, r, m);
+        if (!multi) {
+          bf16* hp = a.h + (size_t)m * a.N + row;
+          *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(v));
+        } else {
+          for (int d = 0; d < c.world; ++d) data_ptr(c, d, par, c.rank, m)[row] = v;
+        }
+      }
+    } else if constexpr (EPI == EPI_LMHEAD) {
+      // logits are bf16 in the reference (layers/embedding.py:88-92)
+      unsigned long long key = 0ull;
+      int mine = -1;
+      if (lane < kRows * M) {
+        const int r = lane / M, m = lane - (lane / M) * M;
+        const int row = g * kRows + r;
+        const float v = rbf(pick<M>(acc, r, m));
+        if (a.y) a.y[(size_t)m * a.N + row] = __float2bfloat16_rn(v);
+        key = argmax_key(v, (uint32_t)(a.vocab_offset + row));
+        mine = m;
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        unsigned long long k = warp_max_u64(mine == m ? key : 0ull);
+        best[m] = k > best[m] ? k : best[m];
+      }
+    }
+  }
+
+  if constexpr (EPI == EPI_ROWAR) {
+    if (multi) {
+      // publish this CTA's partial tile to every rank, then gather
+      __threadfence_system();
+      __syncthreads();
+      if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
+      if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
+      __syncthreads();
+      const int my_groups = (ngroups - (int)blockIdx.x + grid - 1) / grid;
+      const int entries = my_groups * kRows * M;
+      for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+        const int gl = e / (kRows * M);
+        const int rem = e - gl * kRows * M;
+        const int r = rem / M, m = rem - (rem / M) * M;
+        const int row = (blockIdx.x + grid * gl) * kRows + r;
+        float s = 0.f;
+        for (int src = 0; src < c.world; ++src) s += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+        bf16* hp = a.h + (size_t)m * a.N + row;
+        *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(s));
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        if (atomicAdd(c.state + kDone, 1u) == gridDim.x - 1) {
+          c.state[kDone] = 0u;
+          __threadfence();
+          c.state[kCalls] = epoch;
+        }
+      }
+    }
+  }
+
+  if constexpr (EPI == EPI_LMHEAD) {
+    __shared__ unsigned long long cta_best[kWarps][M];
+    __shared__ bool is_last;
+    if (lane == 0) {
+#pragma unroll
+      for (int m = 0; m < M; ++m) cta_best[warp][m] = best[m];
+    }
+    __syncthreads();
+    if (threadIdx.x < M) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < kWarps; ++w) b = cta_best[w][threadIdx.x] > b ? cta_best[w][threadIdx.x] : b;
+      atomicMax(a.keys + threadIdx.x, b);
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (is_last) {
+      __threadfence();
+      __shared__ unsigned long long fin[M];
+      if (threadIdx.x < M) fin[threadIdx.x] = atomicAdd(a.keys + threadIdx.x, 0ull);
+      __syncthreads();
+      if (multi) {
+        const uint32_t ep = read_epoch(c);
+        const int pr = ep & 1;
+        if (threadIdx.x < M)
+          for (int d = 0; d < c.world; ++d) key_ptr(c, d, pr, c.rank)[threadIdx.x] = fin[threadIdx.x];
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, kMaxCtas, c.rank), ep);
+        if (threadIdx.x < c.world) wait_flag(c, kMaxCtas, threadIdx.x, ep);
+        __syncthreads();
+        if (threadIdx.x < M) {
+          unsigned long long b = 0ull;
+          for (int s = 0; s < c.world; ++s) {
+            const unsigned long long k = __ldcg(key_ptr(c, c.rank, pr, s) + threadIdx.x);
+            b = k > b ? k : b;
+          }
+          fin[threadIdx.x] = b;
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) c.state[kCalls] = ep;
+      }
+      if (threadIdx.x < M) {
+        a.ids[threadIdx.x] = (int32_t)argmax_key_index(fin[threadIdx.x]);
+        a.keys[threadIdx.x] = 0ull;
+      }
+      if (threadIdx.x == 0) *a.done = 0u;
+    }
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------
+template <int EPI>
+static int launch_gemv(const GemvArgs& a, const CommDev& c, cudaStream_t s, int max_grid) {
+  const size_t smem = (size_t)a.M * a.K * sizeof(bf16);
+  JSX_REQUIRE(smem <= 200 * 1024, "activations of %d x %d bf16 exceed the shared-memory stage", a.M, a.K);
+  const int ngroups = a.N / kRows;
+#define JSX_GEMV_CASE(MM)                                                                   \
+  case MM: {                                                                                \
+    auto kern = k_gemv<MM, EPI>;                                                            \
+    JSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,        \
+                                  (int)smem));                                              \
+    int occ = 0;                                                                            \
+    JSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem));    \
+    JSX_REQUIRE(occ > 0, "gemv kernel does not fit on an SM (M=%d K=%d)", a.M, a.K);       \
+    int grid = sm_count() * occ;                                                            \
+    const int need = (ngroups + kWarps - 1) / kWarps;                                       \
+    if (grid > need) grid = need;                                                           \
+    if (grid > max_grid) grid = max_grid;                                                   \
+    if (grid < 1) grid = 1;                                                                 \
+    JSX_CUDA(launch_kernel(kern, dim3(grid), dim3(kThreads), smem, s, a, c));              \
+    return JSX_OK;                                                                          \
+  }
+  switch (a.M) {
+    JSX_GEMV_CASE(1)
+    JSX_GEMV_CASE(2)
+    JSX_GEMV_CASE(3)
+    JSX_GEMV_CASE(4)
+    JSX_GEMV_CASE(5)
+    JSX_GEMV_CASE(6)
+    JSX_GEMV_CASE(7)
+    JSX_GEMV_CASE(8)
+    default:
+      set_error("M=%d outside the decode GEMV range 1..%d", a.M, kMaxM);
+      return JSX_ENOTSUP;
+  }
+#undef JSX_GEMV_CASE
+}
+
+static int check_common(const void* x, const void* w, int M, int K, int N) {
+  JSX_REQUIRE(x && w, "null activation or weight pointer");
+  JSX_REQUIRE(M >= 1 && M <= kMaxM, "M=%d outside 1..%d", M, kMaxM);
+  JSX_REQUIRE(K >= 8 && K % 8 == 0, "K=%d must be a positive multiple of 8", K);
+  JSX_REQUIRE(N >= kRows && N % kRows == 0, "N=%d must be a positive multiple of %d", N, kRows);
+  JSX_REQUIRE(aligned16(x) && aligned16(w), "activation and weight must be 16-byte aligned");
+  return JSX_OK;
+}
+
+CommDev comm_view(jsx_comm* comm);  // comm.cu
+
+}  // namespace jsx
+
+using namespace jsx;
+
+extern "C" int jsx_linear(const void* x, const void* gamma, float eps, const void* w_nk,
+                          const void* bias, void* y, int M, int K, int N, void* stream) {
+  int st = check_common(x, w_nk, M, K, N);
+  if (st) return st;
+  JSX_REQUIRE(y != nullptr, "null output");
+  JSX_REQUIRE(gamma == nullptr || aligned16(gamma), "gamma must be 16-byte aligned");
+  GemvArgs a = {};
+  a.x = (const bf16*)x; a.gamma = (const bf16*)gamma; a.eps = eps; a.w = (const bf16*)w_nk;
+  a.M = M; a.K = K; a.N = N; a.bias = (const bf16*)bias; a.y = (bf16*)y;
+  CommDev c = {};
+  c.world = 1;
+  return launch_gemv<EPI_LINEAR>(a, c, (cudaStream_t)stream, 1 << 30);
+}
+
+extern "C" int jsx_qkv_rope_cache(const void* h, const void* ln_gamma, float eps, const void* w_qkv,
+                                  const void* b_qkv, const float* inv_freq,
+                                  const int32_t* positions, void* q_out, void* k_cache,
+                                  void* v_cache, int M, int tokens_per_seq, int K, int nq, int nkv,
+                                  int head_dim, int rotary_dim, int max_seq, void* stream) {
+  const int N = (nq + 2 * nkv) * head_dim;
+  int st = check_common(h, w_qkv, M, K, N);
+  if (st) return st;
+  JSX_REQUIRE(q_out && k_cache && v_cache && positions && inv_freq, "null q/k/v/positions/inv_freq");
+  JSX_REQUIRE(nq >= 1 && nkv >= 1, "bad head counts nq=%d nkv=%d", nq, nkv);
+  JSX_REQUIRE(head_dim >= 2 && head_dim % 2 == 0, "head_dim=%d must be even", head_dim);
+  JSX_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0 &&
+                  (head_dim - rotary_dim) % 2 == 0,
+              "rotary_dim=%d incompatible with head_dim=%d", rotary_dim, head_dim);
+  JSX_REQUIRE(tokens_per_seq >= 1 && M % tokens_per_seq == 0, "tokens_per_seq=%d must divide M=%d",
+              tokens_per_seq, M);
+  JSX_REQUIRE(max_seq >= 1, "max_seq=%d", max_seq);
+  JSX_REQUIRE(ln_gamma == nullptr || aligned16(ln_gamma), "gamma must be 16-byte aligned");
+  GemvArgs a = {};
+  a.x = (const bf16*)h; a.gamma = (const bf16*)ln_gamma; a.eps = eps; a.w = (const bf16*)w_qkv;
+  a.M = M; a.K = K; a.N = N; a.bias = (const bf16*)b_qkv; a.y = (bf16*)q_out;
+  a.inv_freq = inv_freq; a.pos = positions; a.kc = (bf16*)k_cache; a.vc = (bf16*)v_cache;
+  a.nq = nq; a.nkv = nkv; a.hd = head_dim; a.rot = rotary_dim; a.max_seq = max_seq;
+  a.tps = tokens_per_seq;
+  CommDev c = {};
+  c.world = 1;
+  return launch_gemv<EPI_QKV>(a, c, (cudaStream_t)stream, 1 << 30);
+}
+
+extern "C" int jsx_gate_up_swiglu(const void* h, const void* ln_gamma, float eps, const void* w_gu,
+                                  void* act, int M, int K, int I, void* stream) {
+  int st = check_common(h, w_gu, M, K, 2 * I);
+  if (st) return st;
+  JSX_REQUIRE(act != nullptr, "null output");
+  JSX_REQUIRE(ln_gamma == nullptr || aligned16(ln_gamma), "gamma must be 16-byte aligned");
+  GemvArgs a = {};
+  a.x = (const bf16*)h; a.gamma = (const bf16*)ln_gamma; a.eps = eps; a.w = (const bf16*)w_gu;
+  a.M = M; a.K = K; a.N = 2 * I; a.y = (bf16*)act;
+  CommDev c = {};
+  c.world = 1;
+  return launch_gemv<EPI_SWIGLU>(a, c, (cudaStream_t)stream, 1 << 30);
+}
+
+extern "C" int jsx_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h,
+                                        int M, int K_local, int N, void* stream) {
+  int st = check_common(x, w_nk, M, K_local, N);
+  if (st) return st;
+  JSX_REQUIRE(h != nullptr, "null residual");
+  GemvArgs a = {};
+  a.x = (const bf16*)x; a.w = (const bf16*)w_nk; a.M = M; a.K = K_local; a.N = N; a.h = (bf16*)h;
+  CommDev c = {};
+  c.world = 1;
+  if (comm) {
+    c = comm_view(comm);
+    JSX_REQUIRE(c.base[0] != nullptr || c.world == 1, "comm peers not opened");
+    JSX_REQUIRE(M <= c.max_tokens && N <= c.hidden,
+                "M=%d N=%d exceed the comm buffer (%d tokens x %d)", M, N, c.max_tokens, c.hidden);
+  }
+  return launch_gemv<EPI_ROWAR>(a, c, (cudaStream_t)stream, kMaxCtas);
+}
+
+extern "C" int jsx_lmhead_workspace_size(int M, size_t* bytes) {
+  JSX_REQUIRE(bytes && M >= 1 && M <= kMaxM, "bad arguments");
+  *bytes = 256 + (size_t)kMaxM * sizeof(unsigned long long);
+  return JSX_OK;
+}
+
+extern "C" int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, float eps,
+                                 const void* w_vocab, int vocab_local, int vocab_offset, int M,
+                                 int hidden, void* logits_out, int32_t* ids_out, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
+  int st = check_common(h, w_vocab, M, hidden, vocab_local);
+  if (st) return st;
+  size_t need = 0;
+  jsx_lmhead_workspace_size(M, &need);
+  JSX_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
+              "workspace of %zu bytes (16-byte aligned) required", need);
+  JSX_REQUIRE(ids_out != nullptr, "null ids_out");
+  JSX_REQUIRE(vocab_offset >= 0, "vocab_offset=%d", vocab_offset);
+  JSX_REQUIRE(norm_gamma == nullptr || aligned16(norm_gamma), "gamma must be 16-byte aligned");
+  GemvArgs a = {};
+  a.x = (const bf16*)h; a.gamma = (const bf16*)norm_gamma; a.eps = eps; a.w = (const bf16*)w_vocab;
+  a.M = M; a.K = hidden; a.N = vocab_local; a.y = (bf16*)logits_out; a.vocab_offset = vocab_offset;
+  a.done = (uint32_t*)workspace;
+  a.keys = (unsigned long long*)((char*)workspace + 256);
+  a.ids = ids_out;
+  CommDev c = {};
+  c.world = 1;
+  if (comm) {
+    c = comm_view(comm);
+    JSX_REQUIRE(M <= c.max_tokens, "M=%d exceeds the comm buffer (%d tokens)", M, c.max_tokens);
+  }
+  return launch_gemv<EPI_LMHEAD>(a, c, (cudaStream_t)stream, 1 << 30);
+}

@@ -1,0 +1,230 @@
+"""GLM-4-9B dense decoder (models/glm4.py:20-260) on libjsx kernels.
+
+One decode step per rank is 5 kernels per layer plus 2:
+
+    jsx_embed                                  Embed (layers/embedding.py:35-51)
+    per layer:
+      jsx_qkv_rope_cache   input_layernorm + q/k/v + bias + RoPE + KV write (models/glm4.py:118-120)
+      jsx_attn_decode      SDPA over cache rows [0, pos] (layers/attention.py:148-153)
+      jsx_row_linear_allreduce  o_proj + TP all-reduce + residual (layers/attention.py:159, models/glm4.py:124)
+      jsx_gate_up_swiglu   post_attention_layernorm + gate/up + SwiGLU (models/glm4.py:128, :46-48)
+      jsx_row_linear_allreduce  down_proj + TP all-reduce + residual (models/glm4.py:49, :130)
+    jsx_lmhead_argmax                          final norm + LM head + argmax (models/glm4.py:193, :251; runner.py:297)
+
+The greedy token is written back into the step's input-id buffer, so
+consecutive steps chain on the device and a whole step can be captured in a
+CUDA graph (DecodeGraph).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.distributed as dist
+
+from . import kernels as K
+from .config import ModelConfig
+from .layers._param import to_device
+from .layers.kv_cache import KVCache, init_kv_caches, local_kv_heads
+from .layers.rotary import RotaryEmbedding
+from .weights import PackedLayer, RandomLayerSource, pack_layer
+
+CHUNK = K.MAX_DECODE_TOKENS
+
+
+class DecodeState:
+    """Device buffers of one batch: token ids, positions, activations, caches, workspaces."""
+
+    def __init__(self, model: "GLM4ForCausalLM", batch: int, max_seq: int, caches=None,
+                 want_logits: bool = False):
+        dev, c = model.device, model.config
+        self.batch, self.max_seq = batch, max_seq
+        self.ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.h = torch.zeros(batch, c.hidden_size, dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros(batch, model.nq_l * c.head_dim, dtype=torch.bfloat16, device=dev)
+        self.attn = torch.zeros_like(self.q)
+        self.act = torch.zeros(batch, model.I_l, dtype=torch.bfloat16, device=dev)
+        self.caches = caches if caches is not None else init_kv_caches(
+            batch, max_seq, c.num_hidden_layers, c.num_key_value_heads, c.head_dim, mesh=model.mesh,
+            num_heads=c.num_attention_heads, device=dev)
+        self.attn_ws = K.attn_workspace(batch, model.nq_l, model.nkv_l, c.head_dim, max_seq, dev)
+        self.lm_ws = K.lmhead_workspace(CHUNK, dev)
+        self.logits = (torch.zeros(batch, model.V_l, dtype=torch.bfloat16, device=dev)
+                       if want_logits else None)
+
+
+class GLM4ForCausalLM:
+    """models/glm4.py:198-260.  __call__ keeps the reference signature; the
+    decode fast path is step()/DecodeGraph."""
+
+    def __init__(self, config: ModelConfig, mesh, dtype=torch.bfloat16):
+        c = config
+        self.config, self.mesh, self.dtype = c, mesh, dtype
+        self.device = mesh.device if mesh.device is not None else torch.device("cuda")
+        self.tp = mesh.shape.get("tensor", 1)
+        self.rank = mesh.tp_rank
+        t = self.tp
+        if c.num_attention_heads % t or c.intermediate_size % t or c.vocab_size % t:
+            raise ValueError(f"tp={t} must divide heads, intermediate_size and vocab_size")
+        self.nq_l = c.num_attention_heads // t
+        self.kv0, self.nkv_l = ((0, c.num_key_value_heads) if t == 1 else
+                                local_kv_heads(c.num_attention_heads, c.num_key_value_heads, t, self.rank))
+        self.I_l = c.intermediate_size // t
+        self.V_l = c.vocab_size // t
+        self.vocab_offset = self.rank * self.V_l
+        self.rotary = RotaryEmbedding(c.head_dim, c.max_position_embeddings, c.rope_theta, dtype,
+                                      c.partial_rotary_factor)
+        self.inv_freq = self.rotary.inv_freq(self.device)
+        self.scale = c.head_dim ** -0.5
+        self.layers: list[PackedLayer] = []
+        self.embed = None     # [V, H] replicated
+        self.norm = None      # [H]
+        self.lm_head = None   # [V_l, H]
+        self.comm = mesh.comm(CHUNK, c.hidden_size) if t > 1 else None
+
+    # ---- weights ----
+    def load_state(self, params) -> None:
+        """params: reference-layout parameters (attributes or keys embed, layers[i].{ln1, wq, bq,
+        wk, bk, wv, bv, wo, ln2, wg, wu, wd}, norm, lm_head [V, H])."""
+        g = (lambda o, n: o[n] if isinstance(o, dict) else getattr(o, n))
+        dev, c = self.device, self.config
+        self.layers = [pack_layer(lp, c, self.tp, self.rank, dev) for lp in g(params, "layers")]
+        self.embed = to_device(g(params, "embed"), dev)
+        self.norm = to_device(g(params, "norm"), dev)
+        lm = to_device(g(params, "lm_head"), dev)
+        self.lm_head = lm[self.vocab_offset:self.vocab_offset + self.V_l].contiguous()
+        del lm
+        torch.cuda.synchronize(dev)
+
+    def init_random(self, seed: int = 0) -> None:
+        """Synthetic N(0, 0.02) bf16 weights generated on the device, gains = 1."""
+        dev, c = self.device, self.config
+        src = RandomLayerSource(c, dev, seed)
+        self.embed = src.normal(c.vocab_size, c.hidden_size)
+        self.layers = []
+        for _ in range(c.num_hidden_layers):
+            lp = src.layer()
+            self.layers.append(pack_layer(lp, c, self.tp, self.rank, dev))
+            del lp
+        self.norm = torch.ones(c.hidden_size, dtype=torch.bfloat16, device=dev)
+        lm = src.normal(c.vocab_size, c.hidden_size)
+        self.lm_head = lm[self.vocab_offset:self.vocab_offset + self.V_l].contiguous()
+        del lm
+        torch.cuda.synchronize(dev)
+
+    def weight_bytes(self) -> int:
+        """Bytes of weights this rank streams per decode step (layers + LM-head shard + norm)."""
+        n = sum(lp.nbytes() for lp in self.layers)
+        return n + self.lm_head.numel() * 2 + self.norm.numel() * 2
+
+    # ---- the decode step ----
+    def run_body(self, st: DecodeState) -> None:
+        """Embedding + all decoder layers for one token per sequence at st.pos."""
+        c = self.config
+        B, eps, hd, rot = st.batch, c.rms_norm_eps, c.head_dim, self.rotary.rotary_dim
+        K.embed(st.ids, self.embed, out=st.h)
+        for lp, cache in zip(self.layers, st.caches):
+            for b0 in range(0, B, CHUNK):
+                b1 = min(B, b0 + CHUNK)
+                K.qkv_rope_cache(st.h[b0:b1], lp.ln1, eps, lp.w_qkv, lp.b_qkv, self.inv_freq,
+                                 st.pos[b0:b1], st.q[b0:b1], cache.k[b0:b1], cache.v[b0:b1],
+                                 self.nq_l, self.nkv_l, hd, rot)
+            K.attn_decode(st.q, cache.k, cache.v, st.attn, st.pos, self.scale, st.attn_ws)
+            for b0 in range(0, B, CHUNK):
+                b1 = min(B, b0 + CHUNK)
+                K.row_linear_allreduce(self.comm, st.attn[b0:b1], lp.w_o, st.h[b0:b1])
+            for b0 in range(0, B, CHUNK):
+                b1 = min(B, b0 + CHUNK)
+                K.gate_up_swiglu(st.h[b0:b1], lp.ln2, eps, lp.w_gu, st.act[b0:b1])
+            for b0 in range(0, B, CHUNK):
+                b1 = min(B, b0 + CHUNK)
+                K.row_linear_allreduce(self.comm, st.act[b0:b1], lp.w_d, st.h[b0:b1])
+
+    def run_head(self, st: DecodeState) -> None:
+        """Final norm + LM head + greedy argmax; the token ids overwrite st.ids."""
+        for b0 in range(0, st.batch, CHUNK):
+            b1 = min(st.batch, b0 + CHUNK)
+            K.lmhead_argmax(self.comm, st.h[b0:b1], self.norm, self.config.rms_norm_eps, self.lm_head,
+                            self.vocab_offset, st.ids[b0:b1], st.lm_ws,
+                            None if st.logits is None else st.logits[b0:b1])
+
+    def step(self, st: DecodeState, head: bool = True) -> None:
+        self.run_body(st)
+        if head:
+            self.run_head(st)
+        st.pos.add_(1)
+
+    def kernels_per_step(self, batch: int, head: bool = True) -> int:
+        ch = math.ceil(batch / CHUNK)
+        n = 1 + self.config.num_hidden_layers * (1 + 4 * ch)
+        return n + (ch if head else 0)
+
+    # ---- reference-signature forward (models/glm4.py:226-260) ----
+    def __call__(self, input_ids, positions, attention_mask=None, kv_caches=None, cache_position=None):
+        """logits [B, S, V] (bf16, gathered over TP ranks) and the updated caches.
+        Tokens are run one position at a time (causal, exactly the reference's
+        prefill/decode masks); positions must equal cache_position."""
+        dev = self.device
+        ids = torch.as_tensor(input_ids).to(device=dev, dtype=torch.int32)
+        B, S = ids.shape
+        pos = torch.as_tensor(positions).to(device=dev, dtype=torch.int32).reshape(B, S)
+        if cache_position is not None:
+            cp = torch.as_tensor(cache_position).to(device=dev, dtype=torch.int32).reshape(1, S)
+            if not torch.equal(pos, cp.expand(B, S)):
+                raise ValueError("positions must equal cache_position for every sequence")
+        L = kv_caches[0].k.shape[1] if kv_caches is not None else int(pos.max()) + 1
+        st = DecodeState(self, B, L, caches=kv_caches, want_logits=True)
+        logits = torch.empty(B, S, self.config.vocab_size, dtype=torch.bfloat16, device=dev)
+        for s in range(S):
+            st.ids.copy_(ids[:, s])
+            st.pos.copy_(pos[:, s])
+            self.run_body(st)
+            self.run_head(st)
+            if self.tp > 1:
+                parts = [torch.empty_like(st.logits) for _ in range(self.tp)]
+                dist.all_gather(parts, st.logits, group=self.mesh.group("tensor"))
+                logits[:, s] = torch.cat(parts, dim=-1)
+            else:
+                logits[:, s] = st.logits
+        return logits, (st.caches if kv_caches is not None else None)
+
+    def init_kv_caches(self, batch_size: int, max_seq_len: int) -> list[KVCache]:
+        c = self.config
+        return init_kv_caches(batch_size, max_seq_len, c.num_hidden_layers, c.num_key_value_heads,
+                              c.head_dim, mesh=self.mesh, num_heads=c.num_attention_heads,
+                              device=self.device)
+
+
+class DecodeGraph:
+    """CUDA graphs of one decode step (body + head + pos advance) and of one
+    prefill step (body + pos advance) over a DecodeState."""
+
+    def __init__(self, model: GLM4ForCausalLM, st: DecodeState, warmup: bool = True):
+        self.model, self.st = model, st
+        if warmup:
+            # one eager pass per graph so every lazily-initialised resource exists
+            # before capture; restore the state afterwards
+            ids, pos = st.ids.clone(), st.pos.clone()
+            model.step(st, head=True)
+            st.ids.copy_(ids)
+            st.pos.copy_(pos)
+            torch.cuda.synchronize(model.device)
+        self.pool = torch.cuda.graph_pool_handle()
+        self.g_decode = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g_decode, pool=self.pool):
+            model.step(st, head=True)
+        self.g_prefill = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.g_prefill, pool=self.pool):
+            model.step(st, head=False)
+
+    def decode(self) -> None:
+        self.g_decode.replay()
+
+    def prefill(self) -> None:
+        self.g_prefill.replay()
+
+    def release(self) -> None:
+        self.g_decode = None
+        self.g_prefill = None

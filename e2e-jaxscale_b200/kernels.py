@@ -1,0 +1,220 @@
+"""torch-tensor front end of the C ABI (include/jsx.h).
+
+Each function checks devices/dtypes/contiguity, then calls one jsx_* entry
+point on torch's current CUDA stream.  Tensors are plain device memory here:
+torch is the allocator and stream provider, the arithmetic is in libjsx.so.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from ._lib import JSX_LAUNCH_PDL, call, lib  # noqa: F401  (re-exported)
+
+BF16 = torch.bfloat16
+MAX_DECODE_TOKENS = 8  # rows per GEMV call (include/jsx.h: 1 <= M <= 8)
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _need(t, name, dtype=BF16):
+    if t is None:
+        raise ValueError(f"{name} is required")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (got {t.device})")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype} (got {t.dtype})")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    return t
+
+
+def _opt(t, name, dtype=BF16):
+    return None if t is None else _need(t, name, dtype)
+
+
+def set_pdl(enabled: bool) -> None:
+    call("jsx_set_launch_flags", JSX_LAUNCH_PDL if enabled else 0)
+
+
+def pdl_enabled() -> bool:
+    return bool(lib.jsx_get_launch_flags() & JSX_LAUNCH_PDL)
+
+
+def sm_count() -> int:
+    out = ctypes.c_int(0)
+    call("jsx_device_sm_count", ctypes.byref(out))
+    return out.value
+
+
+# ---- packing ------------------------------------------------------------------
+def pack_transpose(w_kn: torch.Tensor) -> torch.Tensor:
+    _need(w_kn, "w")
+    K, N = w_kn.shape
+    out = torch.empty((N, K), dtype=BF16, device=w_kn.device)
+    call("jsx_pack_transpose", _p(w_kn), _p(out), K, N, _stream())
+    return out
+
+
+def pack_qkv(wq, wk, wv, nq, nkv, head_dim, rotary_dim) -> torch.Tensor:
+    for t, n in ((wq, "wq"), (wk, "wk"), (wv, "wv")):
+        _need(t, n)
+    K = wq.shape[0]
+    out = torch.empty(((nq + 2 * nkv) * head_dim, K), dtype=BF16, device=wq.device)
+    call("jsx_pack_qkv", _p(wq), _p(wk), _p(wv), _p(out), K, nq, nkv, head_dim, rotary_dim, _stream())
+    return out
+
+
+def pack_gate_up(wg, wu) -> torch.Tensor:
+    _need(wg, "w_gate")
+    _need(wu, "w_up")
+    K, I = wg.shape
+    out = torch.empty((2 * I, K), dtype=BF16, device=wg.device)
+    call("jsx_pack_gate_up", _p(wg), _p(wu), _p(out), K, I, _stream())
+    return out
+
+
+# ---- ops --------------------------------------------------------------------------
+def rmsnorm(x, gamma, eps, out=None):
+    _need(x, "x")
+    _need(gamma, "gamma")
+    hidden = x.shape[-1]
+    rows = x.numel() // hidden
+    out = torch.empty_like(x) if out is None else _need(out, "out")
+    call("jsx_rmsnorm", _p(x), _p(gamma), _p(out), rows, hidden, ctypes.c_float(eps), _stream())
+    return out
+
+
+def embed(ids, table, out=None):
+    _need(ids, "ids", torch.int32)
+    _need(table, "table")
+    V, H = table.shape
+    M = ids.numel()
+    out = torch.empty((M, H), dtype=BF16, device=table.device) if out is None else _need(out, "out")
+    call("jsx_embed", _p(ids), _p(table), _p(out), M, H, V, _stream())
+    return out
+
+
+def linear(x, w_nk, bias=None, gamma=None, eps=0.0, out=None):
+    """y = bf16(x @ W) (+ bias in bf16); RMSNorm prologue when gamma is given."""
+    _need(x, "x")
+    _need(w_nk, "w_nk")
+    _opt(bias, "bias")
+    _opt(gamma, "gamma")
+    N, K = w_nk.shape
+    x2 = x.reshape(-1, K)
+    M = x2.shape[0]
+    out = torch.empty((M, N), dtype=BF16, device=x.device) if out is None else _need(out, "out")
+    for m0 in range(0, M, MAX_DECODE_TOKENS):
+        m = min(MAX_DECODE_TOKENS, M - m0)
+        call("jsx_linear", _p(x2[m0:m0 + m]), _p(gamma), ctypes.c_float(eps), _p(w_nk), _p(bias),
+             _p(out[m0:m0 + m]), m, K, N, _stream())
+    return out.reshape(*x.shape[:-1], N)
+
+
+def qkv_rope_cache(h, ln_gamma, eps, w_qkv, b_qkv, inv_freq, positions, q_out, k_cache, v_cache,
+                   nq, nkv, head_dim, rotary_dim, tokens_per_seq=1):
+    _need(h, "h")
+    _opt(ln_gamma, "ln_gamma")
+    _need(w_qkv, "w_qkv")
+    _opt(b_qkv, "b_qkv")
+    _need(inv_freq, "inv_freq", torch.float32)
+    _need(positions, "positions", torch.int32)
+    _need(q_out, "q_out")
+    _need(k_cache, "k_cache")
+    _need(v_cache, "v_cache")
+    M, K = h.shape
+    max_seq = k_cache.shape[1]
+    call("jsx_qkv_rope_cache", _p(h), _p(ln_gamma), ctypes.c_float(eps), _p(w_qkv), _p(b_qkv),
+         _p(inv_freq), _p(positions), _p(q_out), _p(k_cache), _p(v_cache), M, tokens_per_seq, K,
+         nq, nkv, head_dim, rotary_dim, max_seq, _stream())
+
+
+def gate_up_swiglu(h, ln_gamma, eps, w_gu, act):
+    _need(h, "h")
+    _opt(ln_gamma, "ln_gamma")
+    _need(w_gu, "w_gu")
+    _need(act, "act")
+    M, K = h.shape
+    I = w_gu.shape[0] // 2
+    call("jsx_gate_up_swiglu", _p(h), _p(ln_gamma), ctypes.c_float(eps), _p(w_gu), _p(act), M, K, I,
+         _stream())
+
+
+def attn_workspace(B, nq, nkv, head_dim, max_seq, device) -> torch.Tensor:
+    n = ctypes.c_size_t(0)
+    call("jsx_attn_decode_workspace_size", B, nq, nkv, head_dim, max_seq, ctypes.byref(n))
+    return torch.zeros(n.value, dtype=torch.uint8, device=device)
+
+
+def attn_decode(q, k_cache, v_cache, out, positions, scale, workspace):
+    _need(q, "q")
+    _need(k_cache, "k_cache")
+    _need(v_cache, "v_cache")
+    _need(out, "out")
+    _need(positions, "positions", torch.int32)
+    _need(workspace, "workspace", torch.uint8)
+    B, max_seq, nkv, hd = k_cache.shape
+    nq = q.numel() // (B * hd)
+    call("jsx_attn_decode", _p(q), _p(k_cache), _p(v_cache), _p(out), _p(positions), B, nq, nkv, hd,
+         max_seq, ctypes.c_float(scale), _p(workspace), workspace.numel(), _stream())
+
+
+def row_linear_allreduce(comm, x, w_nk, h):
+    """h = bf16(h + bf16(sum over ranks of x_r @ W_r)); comm None for one rank."""
+    _need(x, "x")
+    _need(w_nk, "w_nk")
+    _need(h, "h")
+    N, K = w_nk.shape
+    M = x.numel() // K
+    handle = None if comm is None else comm.handle
+    call("jsx_row_linear_allreduce", handle, _p(x), _p(w_nk), _p(h), M, K, N, _stream())
+
+
+def lmhead_workspace(M, device) -> torch.Tensor:
+    n = ctypes.c_size_t(0)
+    call("jsx_lmhead_workspace_size", M, ctypes.byref(n))
+    return torch.zeros(n.value, dtype=torch.uint8, device=device)
+
+
+def lmhead_argmax(comm, h, norm_gamma, eps, w_vocab, vocab_offset, ids_out, workspace,
+                  logits_out=None):
+    _need(h, "h")
+    _opt(norm_gamma, "norm_gamma")
+    _need(w_vocab, "w_vocab")
+    _need(ids_out, "ids_out", torch.int32)
+    _need(workspace, "workspace", torch.uint8)
+    _opt(logits_out, "logits_out")
+    M, H = h.shape
+    Vl = w_vocab.shape[0]
+    handle = None if comm is None else comm.handle
+    call("jsx_lmhead_argmax", handle, _p(h), _p(norm_gamma), ctypes.c_float(eps), _p(w_vocab), Vl,
+         vocab_offset, M, H, _p(logits_out), _p(ids_out), _p(workspace), workspace.numel(), _stream())
+
+
+def moe_gate(x, w_nk, k, scale, norm=True, correction_bias=None, logits_given=False):
+    """Router of layers/moe.py:54-79.  With logits_given, x holds bf16 logits [N, E]."""
+    _need(x, "x")
+    _opt(correction_bias, "correction_bias", torch.float32)
+    if logits_given:
+        N, E = x.shape
+        H = 0
+        w = None
+    else:
+        _need(w_nk, "w_nk")
+        E, H = w_nk.shape
+        N = x.numel() // H
+        w = w_nk
+    topk_w = torch.empty((N, k), dtype=BF16, device=x.device)
+    topk_i = torch.empty((N, k), dtype=torch.int32, device=x.device)
+    call("jsx_moe_gate", _p(x), _p(w), _p(correction_bias), _p(topk_w), _p(topk_i), N, H, E, k,
+         ctypes.c_float(scale), int(bool(norm)), _stream())
+    return topk_w, topk_i

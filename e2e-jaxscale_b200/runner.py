@@ -1,0 +1,107 @@
+"""Generation runner (runner.py:1-308): masks, positions, greedy generation.
+
+The reference jit-compiles one XLA program per shape and syncs with the host
+after every decode step (the EOS check, runner.py:300-306).  Here each step is
+a CUDA-graph replay of the per-rank kernel sequence (glm4.DecodeGraph); the
+greedy token stays on the device and feeds the next step, and the host reads
+it back every step (the same sync the reference performs) only to collect the
+output and test for EOS.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .glm4 import DecodeGraph, DecodeState, GLM4ForCausalLM
+
+NEG = -1e9
+
+
+def make_causal_mask(seq_len: int, dtype=torch.bfloat16) -> torch.Tensor:
+    """runner.py:23-30."""
+    m = torch.triu(torch.full((seq_len, seq_len), NEG, dtype=dtype), diagonal=1)
+    return m[None, None]
+
+
+def make_prefill_mask(seq_len: int, max_cache_len: int, dtype=torch.bfloat16) -> torch.Tensor:
+    """runner.py:33-46."""
+    causal = torch.triu(torch.full((seq_len, seq_len), NEG, dtype=dtype), diagonal=1)
+    pad = torch.full((seq_len, max_cache_len - seq_len), NEG, dtype=dtype)
+    return torch.cat([causal, pad], dim=1)[None, None]
+
+
+def make_decode_mask(cache_position: int, max_cache_len: int, dtype=torch.bfloat16) -> torch.Tensor:
+    """runner.py:49-63."""
+    m = torch.where(torch.arange(max_cache_len) <= cache_position,
+                    torch.zeros(max_cache_len, dtype=dtype), torch.full((max_cache_len,), NEG, dtype=dtype))
+    return m[None, None, None]
+
+
+def make_positions(seq_len: int, batch_size: int = 1) -> torch.Tensor:
+    """runner.py:70-73."""
+    return torch.arange(seq_len, dtype=torch.int32)[None].expand(batch_size, seq_len)
+
+
+class JittedModel:
+    """runner.py:113-233 counterpart: same call signature; warmup() builds the
+    decode/prefill CUDA graphs for one batch size and cache length."""
+
+    def __init__(self, model: GLM4ForCausalLM):
+        self.model = model
+        self.config = model.config
+        self.dtype = model.dtype
+        self.mesh = model.mesh
+        self._graphs = {}
+
+    def __call__(self, input_ids, positions, attention_mask, kv_caches=None, cache_position=None):
+        return self.model(input_ids, positions, attention_mask, kv_caches=kv_caches,
+                          cache_position=cache_position)
+
+    def graph(self, batch_size: int, max_cache_len: int) -> DecodeGraph:
+        key = (batch_size, max_cache_len)
+        if key not in self._graphs:
+            st = DecodeState(self.model, batch_size, max_cache_len)
+            self._graphs[key] = DecodeGraph(self.model, st)
+        return self._graphs[key]
+
+    def warmup(self, batch_size: int = 1, prompt_len: int = 128, max_cache_len: int = 256):
+        self.graph(batch_size, max_cache_len)
+
+
+def _eos_hit(tok: torch.Tensor, eos) -> bool:
+    if eos is None:
+        return False
+    eos = [eos] if isinstance(eos, int) else list(eos)
+    return bool(torch.isin(tok, torch.tensor(eos, dtype=tok.dtype)).all())
+
+
+def greedy_generate(model, input_ids, max_new_tokens: int = 128, max_cache_len: int | None = None,
+                    eos_token_id=None, graph: DecodeGraph | None = None) -> torch.Tensor:
+    """runner.py:240-308: prefill the prompt, then greedy decode with the static
+    KV cache; stops early when every sequence produced an EOS id.  Returns
+    [B, prompt_len + generated] int32 on the host."""
+    jm = model if isinstance(model, JittedModel) else JittedModel(model)
+    ids = torch.as_tensor(input_ids, dtype=torch.int32)
+    B, S = ids.shape
+    L = max_cache_len or (S + max_new_tokens)
+    g = graph if graph is not None else jm.graph(B, L)
+    st = g.st
+    dev = jm.model.device
+    for cache in st.caches:  # fresh cache (layers/kv_cache.py zero-init)
+        cache.k.zero_()
+        cache.v.zero_()
+    st.pos.zero_()
+    host_ids = ids.pin_memory() if torch.cuda.is_available() else ids
+    for s in range(S):
+        st.ids.copy_(host_ids[:, s].to(dev, non_blocking=True))
+        if s < S - 1:
+            g.prefill()
+        else:
+            g.decode()
+    out = [st.ids.to("cpu")]
+    for _ in range(max_new_tokens - 1):
+        g.decode()
+        out.append(st.ids.to("cpu"))
+        if _eos_hit(out[-1], eos_token_id):
+            break
+    return torch.cat([ids] + [t[:, None] for t in out], dim=1)

@@ -1,0 +1,173 @@
+/*
+ * jsx.h — C ABI of libjsx.so, the B200 (sm_100a) kernels behind the GLM-4
+ * tensor-parallel decoder step of JaxScale (sdh1014/e2e-JaxScale).
+ *
+ * Conventions
+ *  - Every entry point returns an int status (JSX_OK == 0).  Nothing throws
+ *    across the ABI; jsx_last_error() returns a thread-local message for the
+ *    most recent failing call on the calling thread.
+ *  - All tensor arguments are raw device pointers to row-major arrays; sizes
+ *    are element counts.  `stream` is a cudaStream_t passed as void* (NULL =
+ *    legacy default stream).  Calls are stream-ordered and never synchronise.
+ *  - bf16 means IEEE bfloat16 stored as 2 bytes; arithmetic is fp32 inside
+ *    the kernels with bf16 rounding (round-to-nearest-even) exactly where the
+ *    reference materialises a bf16 array.
+ *  - Weights are consumed in PACKED layouts produced once at load time by the
+ *    jsx_pack_* entry points from the reference's [in, out] matrices
+ *    (layers/linear.py:16 "Weight shape: (input_size, output_size)").
+ *  - No entry point allocates device memory except jsx_comm_create.  Scratch
+ *    ("workspace") is passed in by the caller, sized by the *_workspace_size
+ *    queries, zero-filled once by the caller and left zeroed by every call.
+ */
+#ifndef JSX_H_
+#define JSX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  JSX_OK = 0,
+  JSX_EINVAL = 1,    /* bad shape, alignment, pointer or argument */
+  JSX_ECUDA = 2,     /* a CUDA runtime call failed */
+  JSX_ETIMEDOUT = 3, /* a peer did not arrive within the comm timeout */
+  JSX_ENOTSUP = 4,   /* shape outside the compiled kernel set */
+  JSX_ENOMEM = 5
+};
+
+typedef struct jsx_comm jsx_comm; /* tensor-parallel group state (one per rank) */
+
+/* ---- library ------------------------------------------------------------ */
+int jsx_abi_version(void);
+const char* jsx_last_error(void);
+/* Number of SMs of the current device (grid sizing and tests). */
+int jsx_device_sm_count(int* out);
+/* Launch flags for every later launch of this process.  JSX_LAUNCH_PDL (1):
+ * programmatic dependent launch — each kernel streams its first weight tiles
+ * while the previous kernel in the stream drains (default: the JSX_PDL
+ * environment variable, "1" = on).  No reference counterpart (XLA schedules
+ * its own fusions). */
+#define JSX_LAUNCH_PDL 1
+int jsx_set_launch_flags(int flags);
+int jsx_get_launch_flags(void);
+
+/* ---- packing (load-time, replaces utils/weight_utils.py:248-265 placement) */
+/* W[K][N] (reference layout, (in, out)) -> Wt[N][K].  Plain transpose used by
+ * jsx_linear, o_proj/down_proj (jsx_row_linear_allreduce) and the router. */
+int jsx_pack_transpose(const void* w_kn, void* w_nk, int K, int N, void* stream);
+/* q/k/v weights W_q[K][nq*hd], W_k[K][nkv*hd], W_v[K][nkv*hd] -> the fused
+ * qkv layout of jsx_qkv_rope_cache: per head, rotary pairs (d, d+1, d+r, d+r+1)
+ * grouped in fours (r = rotary_dim/2), then the pass-through dims in fours.
+ * layers/attention.py:47-61 (q/k/v projections) + layers/rotary.py:88-91. */
+int jsx_pack_qkv(const void* w_q, const void* w_k, const void* w_v, void* w_qkv,
+                 int K, int nq, int nkv, int head_dim, int rotary_dim, void* stream);
+/* gate W_g[K][I], up W_u[K][I] -> rows (g_j, g_j+1, u_j, u_j+1) per pair j.
+ * models/glm4.py:30-39 (gate_proj / up_proj). */
+int jsx_pack_gate_up(const void* w_gate, const void* w_up, void* w_gu, int K, int I, void* stream);
+
+/* ---- ops ------------------------------------------------------------------ */
+/* layers/normalization.py:31-37 RMSNorm.__call__: y = bf16((f32(x)*rsqrt(mean(x^2)+eps))*f32(g)). */
+int jsx_rmsnorm(const void* x, const void* gamma, void* y, int rows, int hidden, float eps,
+                void* stream);
+
+/* layers/embedding.py:35-51 Embed.__call__: out[m] = table[ids[m]] (ids device int32[M]). */
+int jsx_embed(const int32_t* ids, const void* table, void* out, int M, int hidden, int vocab,
+              void* stream);
+
+/* layers/linear.py:57-82 LinearBase.__call__ without a collective (column-
+ * parallel or replicated): y = bf16(x @ W) then y = bf16(y + b) when bias is
+ * non-NULL.  x[M][K], w_nk[N][K] (jsx_pack_transpose), y[M][N].
+ * When gamma is non-NULL the RMSNorm of layers/normalization.py:31-37 is
+ * applied to x first (fused prologue).  1 <= M <= 8 per call. */
+int jsx_linear(const void* x, const void* gamma, float eps, const void* w_nk, const void* bias,
+               void* y, int M, int K, int N, void* stream);
+
+/* Fused input_layernorm + q/k/v projections + bias + partial neox RoPE + KV
+ * cache write of one decoder layer (models/glm4.py:118-120,
+ * layers/attention.py:104-133, layers/rotary.py:36-93).
+ *   h[M][K] bf16, ln_gamma[K] bf16, w_qkv packed ((nq+2*nkv)*hd rows),
+ *   b_qkv[(nq+2*nkv)*hd] bf16 in reference order (q | k | v), inv_freq[rotary_dim/2] f32,
+ *   positions[M] int32 (RoPE angle and cache slot), token m belongs to
+ *   sequence m / tokens_per_seq.
+ *   q_out[M][nq*hd] (rotated), k_cache/v_cache [B][max_seq][nkv][hd]. */
+int jsx_qkv_rope_cache(const void* h, const void* ln_gamma, float eps, const void* w_qkv,
+                       const void* b_qkv, const float* inv_freq, const int32_t* positions,
+                       void* q_out, void* k_cache, void* v_cache, int M, int tokens_per_seq,
+                       int K, int nq, int nkv, int head_dim, int rotary_dim, int max_seq,
+                       void* stream);
+
+/* Fused post_attention_layernorm + gate/up projections + SwiGLU
+ * (models/glm4.py:128-129 and :46-49 up to the down_proj input):
+ *   act[M][I] = bf16(bf16(silu(bf16(h@Wg))) * bf16(h@Wu)). */
+int jsx_gate_up_swiglu(const void* h, const void* ln_gamma, float eps, const void* w_gu,
+                       void* act, int M, int K, int I, void* stream);
+
+/* Decode attention over the static KV cache (layers/attention.py:136-153,
+ * SDPA with the decode mask of runner.py:49-63): each sequence b attends to
+ * cache rows [0, positions[b]] (the masked rows of the reference contribute
+ * exactly zero).  q[B][nq][hd] (already rotated), caches [B][max_seq][nkv][hd],
+ * out[B][nq*hd].  Split over the context; partial results go to `workspace`. */
+int jsx_attn_decode_workspace_size(int B, int nq, int nkv, int head_dim, int max_seq,
+                                   size_t* bytes);
+int jsx_attn_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
+                    const int32_t* positions, int B, int nq, int nkv, int head_dim,
+                    int max_seq, float scale, void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Row-parallel projection (o_proj / down_proj) fused with the tensor-parallel
+ * all-reduce and the residual add (layers/linear.py:72-78 row-parallel
+ * constraint that makes XLA all-reduce; layers/attention.py:159;
+ * models/glm4.py:49,124,130):
+ *   h[m] = bf16(h[m] + bf16(sum_ranks x_r[m] @ W_r))
+ * x[M][K_local], w_nk[N][K_local] (this rank's input-dim shard, transposed),
+ * h[M][N] residual stream (in/out, identical on every rank afterwards).
+ * Partials are pushed as fp32 into the peers' buffers over NVLink (P2P
+ * stores) and summed in rank order on every rank.  comm may be NULL for a
+ * single rank (TP=1). */
+int jsx_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h,
+                             int M, int K_local, int N, void* stream);
+
+/* Final norm + LM head + greedy argmax (models/glm4.py:193, :251-252,
+ * layers/embedding.py:79-92, runner.py:281/:297).  The vocabulary is
+ * sharded: this rank holds rows [vocab_offset, vocab_offset+vocab_local) of
+ * the [V][H] head.  logits are rounded to bf16 like the reference and the
+ * lowest index wins ties (jnp.argmax).  ids_out[M] int32 receives the global
+ * argmax on every rank; logits_out[M][vocab_local] bf16 is written when non-NULL. */
+int jsx_lmhead_workspace_size(int M, size_t* bytes);
+int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, float eps,
+                      const void* w_vocab, int vocab_local, int vocab_offset, int M, int hidden,
+                      void* logits_out, int32_t* ids_out, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* MoE router (layers/moe.py:54-79 MoEGate.__call__): logits = bf16(x @ Wg),
+ * softmax in f32, + correction bias (nullable), top-k (ties -> lower index),
+ * weights = uncorrected probabilities renormalised (+1e-20) when norm != 0,
+ * times scale, rounded to bf16.  x[N][H], w_nk[E][H], topk_w[N][k] bf16,
+ * topk_idx[N][k] int32.  E <= 256, k <= 8. */
+int jsx_moe_gate(const void* x, const void* w_nk, const float* correction_bias, void* topk_w,
+                 int32_t* topk_idx, int N, int H, int E, int k, float scale, int norm,
+                 void* stream);
+
+/* ---- tensor-parallel group (utils/mesh_utils.py:8-45 "tensor" axis) ------- */
+/* Allocates this rank's symmetric buffer on the current device: fp32 partial
+ * slots for up to max_tokens x hidden, flags and state.  timeout_ns bounds
+ * every wait on a peer (0 = 2 s default). */
+int jsx_comm_create(int rank, int world, int max_tokens, int hidden, uint64_t timeout_ns,
+                    jsx_comm** out);
+/* CUDA IPC handle of the symmetric buffer (64 bytes). */
+int jsx_comm_ipc_handle(jsx_comm* comm, void* out64);
+/* Opens every peer's handle (handles = world x 64 bytes, in rank order). */
+int jsx_comm_open_peers(jsx_comm* comm, const void* handles);
+/* Reads and clears the device error word: *status = JSX_OK or JSX_ETIMEDOUT.
+ * Synchronises the device. */
+int jsx_comm_check(jsx_comm* comm, int* status);
+int jsx_comm_destroy(jsx_comm* comm);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JSX_H_ */
