@@ -58,7 +58,9 @@ def parse():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--impl", choices=["jsx", "reference"], default="jsx")
     ap.add_argument("--no-pdl", action="store_true", help="disable programmatic dependent launch")
+    # profiling-only shape overrides (a smaller device footprint for ncu captures)
     ap.add_argument("--layers", type=int, default=40, help=argparse.SUPPRESS)
+    ap.add_argument("--vocab", type=int, default=151552, help=argparse.SUPPRESS)
     return ap.parse_args()
 
 
@@ -246,7 +248,7 @@ def run_gpu(args) -> None:
         return float(t.item())
 
     mesh = jsx.create_mesh(tp=args.gpus)
-    cfg = jsx.ModelConfig(num_hidden_layers=args.layers)
+    cfg = jsx.ModelConfig(num_hidden_layers=args.layers, vocab_size=args.vocab)
     model = jsx.GLM4ForCausalLM(cfg, mesh)
     model.init_random(seed=args.seed)
     B, C = args.batch, args.ctx

@@ -267,7 +267,8 @@ def forward(p: ModelParams, input_ids, positions, mask, kv_caches, cache_positio
         kv = kv_caches[i] if kv_caches is not None else None
         h = decoder_layer(lp, cfg, h, np.asarray(positions), mask, kv, cache_position, inv)
     hn = rmsnorm(h, p.norm, cfg.rms_norm_eps)
-    logits = bf16(np.matmul(hn, p.lm_head.T))
+    # layers/embedding.py:88-92: einsum('...h,vh->...v') with fp32 accumulation, bf16 result
+    logits = bf16(np.einsum("bsh,vh->bsv", hn, p.lm_head, dtype=np.float32))
     if return_hidden:
         return logits, h
     return logits

@@ -1,0 +1,166 @@
+"""Generates tests/golden/reference_golden.npz by executing the REFERENCE's own
+source files (layers/*.py, models/glm4.py, runner.py of sdh1014/e2e-JaxScale)
+on the CPU through the numpy stand-in under tests/golden/jaxshim/ (JAX and Flax
+are not installable here).  The fixture pins the oracle (oracle/glm4_ref.py)
+to the reference's composition of operations: where it rounds to bf16, adds
+biases and residuals, splits RoPE halves, builds masks and loops greedily.
+
+    python tests/golden/make_golden.py [--reference PATH]
+
+Inputs are seeded; model weights come from oracle.glm4_ref.init_params (a
+checksum of them is stored so a drift of the numpy generator is detected).
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+
+
+def params_checksum(p) -> str:
+    h = hashlib.sha256()
+    arrs = [p.embed] + [getattr(lp, n) for lp in p.layers for n in
+                        ("ln1", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "ln2", "wg", "wu", "wd")]
+    arrs += [p.norm, p.lm_head]
+    for a in arrs:
+        h.update(np.ascontiguousarray(a, np.float32).tobytes())
+    return h.hexdigest()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--out", default=os.path.join(HERE, "reference_golden.npz"))
+    args = ap.parse_args()
+
+    sys.path.insert(0, os.path.join(HERE, "jaxshim"))
+    sys.path.insert(1, args.reference)
+    sys.path.insert(2, ROOT)
+    import ml_dtypes
+
+    from configs.model_config import ModelConfig  # reference
+    from layers.attention import GQAAttention  # reference
+    from layers.kv_cache import init_kv_caches  # reference
+    from layers.linear import LinearBase  # reference
+    from layers.moe import MoEGate  # reference
+    from layers.normalization import RMSNorm  # reference
+    from layers.rotary import RotaryEmbedding  # reference
+    from models.glm4 import GLM4ForCausalLM  # reference
+    import runner  # reference
+
+    from oracle import glm4_ref as ref
+
+    BF = ml_dtypes.bfloat16
+    rng = np.random.default_rng(2024)
+
+    def rnd(shape, std=1.0):
+        return (rng.standard_normal(shape, dtype=np.float32) * np.float32(std)).astype(BF)
+
+    out = {}
+    eps = 1.5625e-07
+
+    # RMSNorm (layers/normalization.py)
+    x = rnd((3, 5, 256), 2.0)
+    norm = RMSNorm(256, epsilon=eps, param_dtype=BF)
+    norm.scale.value = rnd((256,), 1.0)
+    out.update(rms_x=x, rms_scale=norm.scale.value, rms_y=norm(x))
+
+    # LinearBase with bias (layers/linear.py), no mesh
+    lin = LinearBase(256, 96, None, use_bias=True, params_dtype=BF)
+    lin.weight.value = rnd((256, 96), 0.05)
+    lin.bias.value = rnd((96,), 0.05)
+    xl = rnd((2, 3, 256))
+    out.update(lin_x=xl, lin_w=lin.weight.value, lin_b=lin.bias.value, lin_y=lin(xl))
+
+    # RotaryEmbedding (layers/rotary.py)
+    rope = RotaryEmbedding(head_dim=128, rope_theta=10000.0, dtype=BF)
+    pos = np.array([0, 1, 7, 300, 1023, 4095], np.int32)
+    q = rnd((6, 4, 128))
+    k = rnd((6, 2, 128))
+    qo, ko = rope(pos, q, k)
+    out.update(rope_pos=pos, rope_q=q, rope_k=k, rope_qo=qo, rope_ko=ko)
+
+    # GQAAttention prefill into a static cache, then one decode step (layers/attention.py)
+    att = GQAAttention(256, 4, 2, 128, 4096, 10000.0, None, attention_bias=True, dtype=BF)
+    for name, (i, o) in {"q_proj": (256, 512), "k_proj": (256, 256), "v_proj": (256, 256),
+                         "o_proj": (512, 256)}.items():
+        lay = getattr(att, name)
+        lay.weight.value = rnd((i, o), 0.05)
+        if lay.bias is not None:
+            lay.bias.value = rnd((o,), 0.05)
+        out[f"att_{name}_w"] = lay.weight.value
+        if lay.bias is not None:
+            out[f"att_{name}_b"] = lay.bias.value
+    B, S, L = 2, 5, 12
+    hs = rnd((B, S, 256))
+    caches = init_kv_caches(B, L, 1, 2, 128, dtype=BF, mesh=None)
+    mask = runner.make_prefill_mask(S, L, dtype=BF)
+    y, c1 = att(hs, runner.make_positions(S, B), mask, kv_cache=caches[0],
+                cache_position=np.arange(S, dtype=np.int32))
+    hd1 = rnd((B, 1, 256))
+    y2, c2 = att(hd1, np.full((B, 1), S, np.int32), runner.make_decode_mask(S, L, dtype=BF),
+                 kv_cache=c1, cache_position=np.array([S], np.int32))
+    out.update(att_h=hs, att_y=y, att_h2=hd1, att_y2=y2, att_k=c2.k, att_v=c2.v)
+
+    # MoEGate (layers/moe.py), with and without a correction bias
+    gate = MoEGate(256, 64, 4, 1.8, True, None, dtype=BF)
+    gate.weight.weight.value = rnd((256, 64), 0.05)
+    xg = rnd((2, 7, 256))
+    gate.e_score_correction_bias.value = np.zeros(64, np.float32)
+    w0, i0 = gate(xg)
+    gate.e_score_correction_bias.value = (rng.standard_normal(64).astype(np.float32) * np.float32(1e-3))
+    w1, i1 = gate(xg)
+    out.update(moe_x=xg, moe_w=gate.weight.weight.value, moe_bias=gate.e_score_correction_bias.value,
+               moe_w0=w0, moe_i0=i0, moe_w1=w1, moe_i1=i1)
+
+    # Full model + greedy generation (models/glm4.py, runner.py)
+    rc = ref.GLMConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                       head_dim=128, intermediate_size=384, vocab_size=1000)
+    p = ref.init_params(rc, seed=0)
+    cfg = ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                      head_dim=128, intermediate_size=384, vocab_size=1000)
+    model = GLM4ForCausalLM(cfg, None, dtype=BF)
+    m = model.model
+    m.embed_tokens.embedding.value = p.embed.astype(BF)
+    for lay, lp in zip(m.layers, p.layers):
+        a = lay.self_attn
+        a.q_proj.weight.value, a.q_proj.bias.value = lp.wq.astype(BF), lp.bq.astype(BF)
+        a.k_proj.weight.value, a.k_proj.bias.value = lp.wk.astype(BF), lp.bk.astype(BF)
+        a.v_proj.weight.value, a.v_proj.bias.value = lp.wv.astype(BF), lp.bv.astype(BF)
+        a.o_proj.weight.value = lp.wo.astype(BF)
+        lay.mlp.gate_proj.weight.value = lp.wg.astype(BF)
+        lay.mlp.up_proj.weight.value = lp.wu.astype(BF)
+        lay.mlp.down_proj.weight.value = lp.wd.astype(BF)
+        lay.input_layernorm.scale.value = lp.ln1.astype(BF)
+        lay.post_attention_layernorm.scale.value = lp.ln2.astype(BF)
+    m.norm.scale.value = p.norm.astype(BF)
+    model.lm_head.embedding.value = p.lm_head.astype(BF)
+    prompt = np.random.default_rng(1).integers(0, 1000, (2, 7)).astype(np.int32)
+    gen = runner.greedy_generate(model, prompt, max_new_tokens=6, max_cache_len=16)
+    # logits of the prefill's last position and of the first decode step
+    kv = init_kv_caches(2, 16, 2, 2, 128, dtype=BF, mesh=None)
+    lg, kv = model(prompt, runner.make_positions(7, 2), runner.make_prefill_mask(7, 16, dtype=BF),
+                   kv_caches=kv, cache_position=np.arange(7, dtype=np.int32))
+    nxt = np.asarray(gen[:, 7:8], np.int32)
+    lg2, kv = model(nxt, np.full((2, 1), 7, np.int32), runner.make_decode_mask(7, 16, dtype=BF),
+                    kv_caches=kv, cache_position=np.array([7], np.int32))
+    out.update(model_prompt=prompt, model_gen=np.asarray(gen), model_prefill_logits=lg[:, -1],
+               model_decode_logits=lg2[:, -1], model_params_sha256=np.array(params_checksum(p)))
+
+    ser = {}
+    for k_, v in out.items():
+        v = np.asarray(v)
+        ser[k_] = v.astype(np.float32) if v.dtype == BF else v
+    np.savez_compressed(args.out, **ser)
+    print(f"wrote {args.out}: {len(ser)} arrays, {os.path.getsize(args.out)} bytes")
+
+
+if __name__ == "__main__":
+    main()

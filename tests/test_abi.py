@@ -1,0 +1,62 @@
+"""The C ABI library loads and exports every entry point declared in
+include/jsx.h; argument validation answers without touching a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "jsx.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(jsx_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for n in ("jsx_linear", "jsx_qkv_rope_cache", "jsx_gate_up_swiglu", "jsx_attn_decode",
+              "jsx_row_linear_allreduce", "jsx_lmhead_argmax", "jsx_moe_gate", "jsx_comm_create"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(jsx):
+    lib = ctypes.CDLL(jsx._lib.LIB_PATH)
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+    assert set(jsx._lib.SIGNATURES) | {"jsx_last_error"} >= set(declared_functions())
+
+
+def test_abi_version(jsx):
+    assert jsx._lib.lib.jsx_abi_version() == 1
+
+
+@pytest.mark.parametrize("call,args", [
+    ("jsx_linear", (None, None, 0.0, None, None, None, 1, 64, 8, None)),
+    ("jsx_comm_create", (0, 9, 8, 4096, 0, None)),
+    ("jsx_comm_create", (2, 2, 8, 4096, 0, None)),
+    ("jsx_moe_gate", (None, None, None, None, None, 1, 8, 512, 4, 1.0, 1, None)),
+    ("jsx_set_launch_flags", (0x10,)),
+])
+def test_invalid_arguments_are_rejected_on_the_host(jsx, call, args):
+    lib = jsx._lib
+    with pytest.raises(lib.JsxError) as e:
+        lib.call(call, *args)
+    assert e.value.status == lib.JSX_EINVAL
+    assert lib.last_error()
+
+
+def test_workspace_size_queries(jsx):
+    lib = jsx._lib
+    n = ctypes.c_size_t(0)
+    lib.call("jsx_attn_decode_workspace_size", 1, 32, 2, 128, 1152, ctypes.byref(n))
+    splits = (1152 + 31) // 32
+    assert n.value >= 1 * 2 * splits * 16 * 130 * 4
+    lib.call("jsx_lmhead_workspace_size", 8, ctypes.byref(n))
+    assert n.value >= 256 + 8 * 8
+    with pytest.raises(lib.JsxError):
+        lib.call("jsx_lmhead_workspace_size", 9, ctypes.byref(n))

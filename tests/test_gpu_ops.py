@@ -86,7 +86,8 @@ def test_rmsnorm(jsx, ref, cuda, rng):
     (2, 1, 64, 8, [0, 1, 2, 3, 100, 101, 511, 7]),
 ])
 def test_qkv_rope_cache(jsx, ref, cuda, rng, nq, nkv, hd, M, pos):
-    H, L, eps = 256, 512, 1.5625e-7
+    H, eps = 256, 1.5625e-7
+    L = max(512, max(pos) + 1)
     h = rand_bf16(ref, rng, (M, H), 1.0)
     g = np.ones(H, np.float32)
     wq = rand_bf16(ref, rng, (H, nq * hd), 0.05)

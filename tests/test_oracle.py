@@ -1,0 +1,87 @@
+"""Self-consistency of the CPU oracle, mirroring the reference's own checks
+(benchmarks/verify_kvcache.py) and the algebra the kernels rely on."""
+
+import numpy as np
+import pytest
+
+
+def small(ref, layers=2):
+    return ref.GLMConfig(hidden_size=128, num_hidden_layers=layers, num_attention_heads=4,
+                         num_key_value_heads=2, head_dim=64, intermediate_size=192, vocab_size=300)
+
+
+def test_cache_vs_no_cache_prefill(ref):
+    """verify_kvcache.py:36-78: cached and uncached prefill agree (< 1e-3)."""
+    rc = small(ref)
+    p = ref.init_params(rc, seed=1)
+    ids = np.random.default_rng(0).integers(0, rc.vocab_size, (2, 9))
+    pos = np.broadcast_to(np.arange(9), (2, 9))
+    kv = ref.init_kv_caches(rc, 2, 16)
+    a = ref.forward(p, ids, pos, ref.make_prefill_mask(9, 16), kv, np.arange(9))
+    causal = np.triu(np.full((9, 9), ref.NEG, np.float32), k=1)[None, None]
+    b = ref.forward(p, ids, pos, causal, None, None)
+    assert np.max(np.abs(a - b)) < 1e-3
+
+
+def test_teacher_forced_decode_matches_recompute(ref):
+    """verify_kvcache.py:81-183: decode with the cache vs full recompute (< 2.0, same tokens)."""
+    rc = small(ref)
+    p = ref.init_params(rc, seed=2)
+    ids = np.random.default_rng(1).integers(0, rc.vocab_size, (1, 6))
+    rec = []
+    out = ref.greedy_generate(p, ids, 5, max_cache_len=16, record=rec)
+    for t in range(1, 5):
+        seq = out[:, :6 + t]
+        S = seq.shape[1]
+        causal = np.triu(np.full((S, S), ref.NEG, np.float32), k=1)[None, None]
+        full = ref.forward(p, seq, np.broadcast_to(np.arange(S), (1, S)), causal, None, None)[:, -1]
+        assert np.max(np.abs(full - rec[t][0])) < 2.0
+        assert ref.argmax_first(full)[0] == out[0, 6 + t]
+
+
+def test_masked_rows_contribute_nothing(ref):
+    """The decode mask's -1e9 rows give exactly zero weight, so attending to rows
+    [0, cur] only (what the kernel does) is the same function."""
+    rng = np.random.default_rng(3)
+    q = ref.bf16(rng.standard_normal((1, 1, 8, 64)))
+    k = ref.bf16(rng.standard_normal((1, 40, 2, 64)))
+    v = ref.bf16(rng.standard_normal((1, 40, 2, 64)))
+    cur = 17
+    full = ref.sdpa(q, k, v, ref.make_decode_mask(cur, 40), 64 ** -0.5)
+    trunc = ref.sdpa(q, k[:, :cur + 1], v[:, :cur + 1], None, 64 ** -0.5)
+    assert np.array_equal(full, trunc)
+
+
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_row_parallel_shards_sum_to_the_full_product(ref, tp):
+    rng = np.random.default_rng(tp)
+    x = ref.bf16(rng.standard_normal((3, 512)))
+    w = ref.bf16(rng.standard_normal((512, 64)) * 0.02)
+    xs = [ref.shard_columns(x, tp, r) for r in range(tp)]
+    ws = [ref.shard_rows(w, tp, r) for r in range(tp)]
+    y = ref.row_parallel_reference(xs, ws)
+    full = ref.linear(x, w)
+    assert np.max(np.abs(y - full)) <= 2 ** -7 * np.max(np.abs(full))
+
+
+def test_rope_is_identity_at_position_zero(ref):
+    rng = np.random.default_rng(4)
+    q = ref.bf16(rng.standard_normal((1, 2, 128)))
+    k = ref.bf16(rng.standard_normal((1, 1, 128)))
+    qo, ko = ref.rope(np.array([0]), q, k, ref.rope_inv_freq(128))
+    assert np.array_equal(qo, q) and np.array_equal(ko, k)
+
+
+def test_moe_gate_weights(ref):
+    rng = np.random.default_rng(5)
+    x = ref.bf16(rng.standard_normal((10, 64)))
+    w = ref.bf16(rng.standard_normal((64, 16)) * 0.1)
+    wts, idx = ref.moe_gate(x, w, 4, 1.8, True)
+    assert idx.shape == (10, 4) and len(set(idx[0])) == 4
+    assert np.allclose(wts.sum(-1), 1.8, atol=0.03)
+    logits = ref.linear(x, w)
+    assert np.array_equal(idx[:, 0], np.argmax(logits, -1))
+
+
+def test_argmax_ties_pick_first(ref):
+    assert ref.argmax_first(np.array([[1.0, 3.0, 3.0, 2.0]]))[0] == 1

@@ -1,0 +1,84 @@
+"""Pins the CPU oracle to the reference's own code: tests/golden/reference_golden.npz
+was produced by running the reference's layers/, models/glm4.py and runner.py
+(through the numpy stand-in for jax/flax, tests/golden/make_golden.py).  The
+oracle must reproduce every recorded output bit for bit on the same inputs."""
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "reference_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def g():
+    return np.load(GOLDEN)
+
+
+def same(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    assert np.array_equal(a, b), f"max diff {np.max(np.abs(a - b))}"
+
+
+def test_rmsnorm(ref, g):
+    same(ref.rmsnorm(g["rms_x"], g["rms_scale"], 1.5625e-07), g["rms_y"])
+
+
+def test_linear_bias_after_round(ref, g):
+    same(ref.linear(g["lin_x"], g["lin_w"], g["lin_b"]), g["lin_y"])
+
+
+def test_rope_half_split(ref, g):
+    inv = ref.rope_inv_freq(128)
+    qo, ko = ref.rope(g["rope_pos"], g["rope_q"], g["rope_k"], inv)
+    same(qo, g["rope_qo"])
+    same(ko, g["rope_ko"])
+
+
+def test_gqa_attention_prefill_then_decode(ref, g):
+    cfg = ref.GLMConfig(hidden_size=256, num_attention_heads=4, num_key_value_heads=2, head_dim=128)
+    lp = ref.LayerParams(ln1=None, wq=g["att_q_proj_w"], bq=g["att_q_proj_b"], wk=g["att_k_proj_w"],
+                         bk=g["att_k_proj_b"], wv=g["att_v_proj_w"], bv=g["att_v_proj_b"],
+                         wo=g["att_o_proj_w"], ln2=None, wg=None, wu=None, wd=None)
+    B, S, L = 2, 5, 12
+    inv = ref.rope_inv_freq(128)
+    kc = np.zeros((B, L, 2, 128), np.float32)
+    vc = np.zeros_like(kc)
+    pos = np.broadcast_to(np.arange(S), (B, S))
+    y = ref.attention(lp, cfg, g["att_h"], pos, ref.make_prefill_mask(S, L), (kc, vc), np.arange(S), inv)
+    same(y, g["att_y"])
+    y2 = ref.attention(lp, cfg, g["att_h2"], np.full((B, 1), S), ref.make_decode_mask(S, L), (kc, vc),
+                       np.array([S]), inv)
+    same(y2, g["att_y2"])
+    same(kc, g["att_k"])
+    same(vc, g["att_v"])
+
+
+def test_moe_gate(ref, g):
+    w0, i0 = ref.moe_gate(g["moe_x"], g["moe_w"], 4, 1.8, True)
+    same(w0, g["moe_w0"])
+    assert np.array_equal(i0, g["moe_i0"])
+    w1, i1 = ref.moe_gate(g["moe_x"], g["moe_w"], 4, 1.8, True, g["moe_bias"])
+    same(w1, g["moe_w1"])
+    assert np.array_equal(i1, g["moe_i1"])
+
+
+def test_greedy_generation_and_logits(ref, g):
+    rc = ref.GLMConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                       head_dim=128, intermediate_size=384, vocab_size=1000)
+    p = ref.init_params(rc, seed=0)
+    h = hashlib.sha256()
+    for a in [p.embed] + [getattr(lp, n) for lp in p.layers for n in
+                          ("ln1", "wq", "bq", "wk", "bk", "wv", "bv", "wo", "ln2", "wg", "wu", "wd")] + \
+            [p.norm, p.lm_head]:
+        h.update(np.ascontiguousarray(a, np.float32).tobytes())
+    assert h.hexdigest() == str(g["model_params_sha256"]), "numpy generator stream changed"
+    prompt = g["model_prompt"]
+    record = []
+    gen = ref.greedy_generate(p, prompt, 6, max_cache_len=16, record=record)
+    assert np.array_equal(gen, g["model_gen"])
+    same(record[0][0], g["model_prefill_logits"])
+    same(record[1][0], g["model_decode_logits"])
