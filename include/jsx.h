@@ -59,12 +59,12 @@ int jsx_get_launch_flags(void);
  * jsx_linear, o_proj/down_proj (jsx_row_linear_allreduce) and the router. */
 int jsx_pack_transpose(const void* w_kn, void* w_nk, int K, int N, void* stream);
 /* q/k/v weights W_q[K][nq*hd], W_k[K][nkv*hd], W_v[K][nkv*hd] -> the fused
- * qkv layout of jsx_qkv_rope_cache: per head, rotary pairs (d, d+1, d+r, d+r+1)
- * grouped in fours (r = rotary_dim/2), then the pass-through dims in fours.
+ * qkv layout of jsx_qkv_rope_cache: per head, the rotary pairs (d, d+r) for
+ * d < r = rotary_dim/2, then the pass-through dims in pairs (d, d+1).
  * layers/attention.py:47-61 (q/k/v projections) + layers/rotary.py:88-91. */
 int jsx_pack_qkv(const void* w_q, const void* w_k, const void* w_v, void* w_qkv,
                  int K, int nq, int nkv, int head_dim, int rotary_dim, void* stream);
-/* gate W_g[K][I], up W_u[K][I] -> rows (g_j, g_j+1, u_j, u_j+1) per pair j.
+/* gate W_g[K][I], up W_u[K][I] -> rows interleaved (gate_j, up_j).
  * models/glm4.py:30-39 (gate_proj / up_proj). */
 int jsx_pack_gate_up(const void* w_gate, const void* w_up, void* w_gu, int K, int I, void* stream);
 
