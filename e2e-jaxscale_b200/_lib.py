@@ -50,6 +50,7 @@ SIGNATURES = {
     "jsx_gate_up_swiglu": [P, P, F, P, P, I, I, I, P],
     "jsx_attn_decode_workspace_size": [I, I, I, I, I, P],
     "jsx_attn_decode": [P, P, P, P, P, I, I, I, I, I, F, P, SZ, P],
+    "jsx_attn_decode_noalloc": [P, P, P, P, P, I, I, I, I, I, F, P],
     "jsx_row_linear_allreduce": [P, P, P, P, I, I, I, P],
     "jsx_lmhead_workspace_size": [I, P],
     "jsx_lmhead_argmax": [P, P, P, F, P, I, I, I, I, P, P, P, SZ, P],

@@ -116,6 +116,16 @@ int jsx_attn_decode(const void* q, const void* k_cache, const void* v_cache, voi
                     const int32_t* positions, int B, int nq, int nkv, int head_dim,
                     int max_seq, float scale, void* workspace, size_t workspace_bytes,
                     void* stream);
+/* Same computation as jsx_attn_decode, for callers that cannot allocate device
+ * memory: the split partials live in a 16 MiB static device array of the
+ * library instead of a caller workspace.  No counterpart in the reference (XLA
+ * allocates its own temporaries).  Shapes whose workspace exceeds 16 MiB get
+ * JSX_EINVAL.  The first call on a device looks up the array's address (make
+ * it before any stream capture); every call shares the array, so calls that
+ * overlap on the GPU race.  Allocates nothing. */
+int jsx_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
+                            const int32_t* positions, int B, int nq, int nkv, int head_dim,
+                            int max_seq, float scale, void* stream);
 
 /* Row-parallel projection (o_proj / down_proj) fused with the tensor-parallel
  * all-reduce and the residual add (layers/linear.py:72-78 row-parallel
