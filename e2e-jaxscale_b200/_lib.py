@@ -40,6 +40,7 @@ SIGNATURES = {
     "jsx_device_sm_count": [P],
     "jsx_set_launch_flags": [I],
     "jsx_get_launch_flags": [],
+    "jsx_device_error": [P],
     "jsx_pack_transpose": [P, P, I, I, P],
     "jsx_pack_qkv": [P, P, P, P, I, I, I, I, I, P],
     "jsx_pack_gate_up": [P, P, P, I, I, P],

@@ -23,6 +23,8 @@
 // BEFORE griddepcontrol.wait (weights never depend on the previous kernel) and
 // performs every activation read and every global write after it.
 #include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
 
 #include "comm.cuh"
 #include "common.cuh"
@@ -64,14 +66,23 @@ struct GemvArgs {
 
 // ---- activations -> shared memory (optionally RMS-normalised) --------------
 // layers/normalization.py:31-37: y = bf16((x * rsqrt(mean(x^2) + eps)) * g), fp32 inside.
-template <int M>
+// Barrier over the threads that stage the activations: the whole CTA (v1
+// kernel) or the 8 consumer warps of the streaming kernel (named barrier 1).
+template <bool kNamed>
+__device__ __forceinline__ void stage_sync() {
+  if constexpr (kNamed) asm volatile("bar.sync 1, 256;" ::: "memory");
+  else __syncthreads();
+}
+
+template <int M, bool kNamed = false>
 __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
+  constexpr int NT = kThreads;  // 256 staging threads in both kernels
   const int nvec = a.K >> 3;
   const uint4* xv = reinterpret_cast<const uint4*>(a.x);
   uint4* sv = reinterpret_cast<uint4*>(xs);
   if (a.gamma == nullptr) {
-    for (int i = threadIdx.x; i < M * nvec; i += blockDim.x) sv[i] = xv[i];
-    __syncthreads();
+    for (int i = threadIdx.x; i < M * nvec; i += NT) sv[i] = xv[i];
+    stage_sync<kNamed>();
     return;
   }
   __shared__ float red[M][kWarps];
@@ -79,7 +90,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
   float ss[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) ss[m] = 0.f;
-  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+  for (int v = threadIdx.x; v < nvec; v += NT) {
 #pragma unroll
     for (int m = 0; m < M; ++m) {
       float f[8];
@@ -94,16 +105,16 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
     float s = warp_sum(ss[m]);
     if (lane == 0) red[m][warp] = s;
   }
-  __syncthreads();
+  stage_sync<kNamed>();
   if (threadIdx.x < M) {
     float t = 0.f;
 #pragma unroll
     for (int w = 0; w < kWarps; ++w) t += red[threadIdx.x][w];
     rstd[threadIdx.x] = 1.0f / sqrtf(t / (float)a.K + a.eps);
   }
-  __syncthreads();
+  stage_sync<kNamed>();
   const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
-  for (int i = threadIdx.x; i < M * nvec; i += blockDim.x) {
+  for (int i = threadIdx.x; i < M * nvec; i += NT) {
     const int m = i / nvec, v = i - m * nvec;
     float f[8], g[8];
     unpack8(xv[i], f);
@@ -116,7 +127,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
     o.w = pack2((f[6] * r) * g[6], (f[7] * r) * g[7]);
     sv[i] = o;
   }
-  __syncthreads();
+  stage_sync<kNamed>();
 }
 
 // ---- weight batches -----------------------------------------------------------
@@ -175,11 +186,7 @@ __device__ __forceinline__ float pick(const float (&acc)[kRows][M], int r, int m
 // qkv packing (jsx_pack_qkv): per head hd/2 groups; group j < rot/2 holds rows
 // (j, j + rot/2) (a neox rotary pair), group j >= rot/2 holds the pass-through
 // pair (rot + 2(j - rot/2), +1).  Heads: q (nq), then k (nkv), then v (nkv).
-template <int M>
-__device__ __forceinline__ void epi_qkv(const GemvArgs& a, int g, const float (&acc)[kRows][M],
-                                        int lane) {
-  if (lane >= M) return;
-  const int m = lane;
+__device__ __forceinline__ void qkv_store(const GemvArgs& a, int g, int m, float acc0, float acc1) {
   const int gph = a.hd >> 1;
   const int head = g / gph, j = g - head * gph;
   const int rh = a.rot >> 1;
@@ -188,8 +195,8 @@ __device__ __forceinline__ void epi_qkv(const GemvArgs& a, int g, const float (&
   if (j < rh) { d0 = j; d1 = j + rh; rotary = true; }
   else { d0 = a.rot + 2 * (j - rh); d1 = d0 + 1; rotary = false; }
   const int col0 = head * a.hd + d0, col1 = head * a.hd + d1;  // index into q|k|v
-  float x1 = rbf(pick<M>(acc, 0, m));
-  float x2 = rbf(pick<M>(acc, 1, m));
+  float x1 = rbf(acc0);
+  float x2 = rbf(acc1);
   if (a.bias) {
     x1 = rbf(x1 + ldbf(a.bias + col0));
     x2 = rbf(x2 + ldbf(a.bias + col1));
@@ -224,16 +231,26 @@ __device__ __forceinline__ void epi_qkv(const GemvArgs& a, int g, const float (&
 
 // gate/up packing (jsx_pack_gate_up): group j holds rows (gate_j, up_j).
 // models/glm4.py:47-49 with jax.nn.silu(x) = x * sigmoid(x) on bf16 arrays.
+__device__ __forceinline__ void swiglu_store(const GemvArgs& a, int g, int m, float acc0, float acc1) {
+  const float gate = rbf(acc0);
+  const float up = rbf(acc1);
+  const float sig = rbf(1.0f / (1.0f + expf(-gate)));
+  const float act = rbf(rbf(gate * sig) * up);
+  a.y[(size_t)m * (a.N >> 1) + g] = __float2bfloat16_rn(act);
+}
+
+template <int M>
+__device__ __forceinline__ void epi_qkv(const GemvArgs& a, int g, const float (&acc)[kRows][M],
+                                        int lane) {
+  if (lane >= M) return;
+  qkv_store(a, g, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
+}
+
 template <int M>
 __device__ __forceinline__ void epi_swiglu(const GemvArgs& a, int g, const float (&acc)[kRows][M],
                                            int lane) {
   if (lane >= M) return;
-  const int m = lane;
-  const float gate = rbf(pick<M>(acc, 0, m));
-  const float up = rbf(pick<M>(acc, 1, m));
-  const float sig = rbf(1.0f / (1.0f + expf(-gate)));
-  const float act = rbf(rbf(gate * sig) * up);
-  a.y[(size_t)m * (a.N >> 1) + g] = __float2bfloat16_rn(act);
+  swiglu_store(a, g, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
 }
 
 // ---- the kernel ------------------------------------------------------------------
@@ -418,9 +435,462 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
   }
 }
 
+// ---- streaming kernel: weights through shared memory (cp.async.bulk) --------------
+// One CTA per SM: 8 consumer warps + 1 producer warp.  The CTA owns a
+// contiguous range of row pairs (packed rows 2b, 2b+1), split evenly to within
+// one pair.  An "item" is nb consecutive pairs (nb > 1 only for K <= 2048, so
+// that a stage carries >= 8 KB); items are dealt round-robin to the consumer
+// warps and every warp owns its items end to end: it accumulates both rows of
+// a pair over the K chunks, reduces inside the warp and runs the pair's
+// epilogue itself, so the main loop has no CTA-wide barrier.
+//
+// The producer warp's elected lane streams the units (one K chunk of one item,
+// <= 16 KB) into a ring of shared-memory stages with cp.async.bulk (L2
+// evict-first), in the order (group of 8 items, chunk, item) so the eight warps
+// are fed in turn; each stage completes on a full mbarrier (expect_tx) and is
+// handed back by its warp on an empty mbarrier.  The producer never reads
+// activations, so it skips griddepcontrol.wait and keeps loading weights while
+// the previous kernel drains.  Bytes in flight per SM = stages x 16 KB.
+//
+// Every wait is time-bounded; on a timeout the CTA raises an abort flag and the
+// device error word, warps stop waiting (they still hand back their stages),
+// and the producer drains the copies it issued before it exits.
+constexpr int kMaxStages = 48;
+constexpr int kMinStages = 12;
+constexpr int kConsumers = 8;
+constexpr int kStreamThreads = (kConsumers + 1) * 32;
+constexpr long long kWaitLimitCycles = 4000000000ll;
+
+static __device__ uint32_t g_gemv_error;  // read and cleared by jsx_device_error
+
+struct StreamPlan {
+  int stage_bytes;  // bytes per stage (4, 8 or 16 KB)
+  int nb;      // row pairs per item (1, 2 or 4)
+  int Kc;      // chunk length in elements (K when nchunk == 1)
+  int nchunk;  // chunks per item
+  int stages;
+  int x_bytes; // shared bytes of the staged activations (16-byte multiple)
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase of parity `parity` to complete.  Returns false
+// (without waiting) once the CTA has aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
+  if (*abort) return false;
+  if (mbar_try_wait(b, parity)) return true;
+  // bound on the SM cycle counter (cheap to read): kWaitLimitCycles ~ 2 s at the 1965 MHz max clock
+  const long long t0 = clock64();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort) return false;
+      if (clock64() - t0 > kWaitLimitCycles) {
+        *abort = 1;
+        atomicOr(&g_gemv_error, 1u);
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ uint64_t l2_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                          uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Epilogue of one row pair (packed rows 2g, 2g+1) for token m; returns the
+// argmax key of the pair (LM head) or 0.
+template <int EPI>
+__device__ __forceinline__ unsigned long long epi_pair(const GemvArgs& a, const CommDev& c, bool multi,
+                                                       int par, int g, int m, float v0, float v1) {
+  const int r0 = 2 * g;
+  if constexpr (EPI == EPI_LINEAR) {
+    float y0 = rbf(v0), y1 = rbf(v1);
+    if (a.bias) {
+      y0 = rbf(y0 + ldbf(a.bias + r0));
+      y1 = rbf(y1 + ldbf(a.bias + r0 + 1));
+    }
+    a.y[(size_t)m * a.N + r0] = __float2bfloat16_rn(y0);
+    a.y[(size_t)m * a.N + r0 + 1] = __float2bfloat16_rn(y1);
+  } else if constexpr (EPI == EPI_QKV) {
+    qkv_store(a, g, m, v0, v1);
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    swiglu_store(a, g, m, v0, v1);
+  } else if constexpr (EPI == EPI_ROWAR) {
+    if (!multi) {
+      bf16* hp = a.h + (size_t)m * a.N + r0;
+      hp[0] = __float2bfloat16_rn(__bfloat162float(hp[0]) + rbf(v0));
+      hp[1] = __float2bfloat16_rn(__bfloat162float(hp[1]) + rbf(v1));
+    } else {
+      for (int d = 0; d < c.world; ++d) {
+        float* dst = data_ptr(c, d, par, c.rank, m) + r0;
+        dst[0] = v0;
+        dst[1] = v1;
+      }
+    }
+  } else if constexpr (EPI == EPI_LMHEAD) {
+    const float l0 = rbf(v0), l1 = rbf(v1);
+    if (a.y) {
+      a.y[(size_t)m * a.N + r0] = __float2bfloat16_rn(l0);
+      a.y[(size_t)m * a.N + r0 + 1] = __float2bfloat16_rn(l1);
+    }
+    const unsigned long long k0 = argmax_key(l0, (uint32_t)(a.vocab_offset + r0));
+    const unsigned long long k1 = argmax_key(l1, (uint32_t)(a.vocab_offset + r0 + 1));
+    return k0 > k1 ? k0 : k1;
+  }
+  return 0ull;
+}
+
+template <int M, int EPI>
+__global__ void __launch_bounds__(kStreamThreads, 1) k_gemv_stream(GemvArgs a, CommDev c, StreamPlan pl) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* stages = smem_raw;
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw + (size_t)pl.stages * pl.stage_bytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + (size_t)pl.stages * pl.stage_bytes + pl.x_bytes);
+  uint64_t* empty = full + pl.stages;
+  __shared__ int abort_flag;
+  __shared__ bool is_last;
+  __shared__ unsigned long long cta_best[kConsumers][M];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = a.K;
+  const int NB = a.N >> 1;  // row pairs
+  const int b0 = (int)((long long)blockIdx.x * NB / gridDim.x);
+  const int b1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
+  const int nitems = (b1 - b0 + pl.nb - 1) / pl.nb;
+  const int units = nitems * pl.nchunk;
+  const int group_units = kConsumers * pl.nchunk;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < pl.stages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kConsumers) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t policy = l2_evict_first();
+      int u = 0;
+      for (; u < units; ++u) {
+        const int s = u % pl.stages, i = u / pl.stages;
+        if (i > 0 && !mbar_wait(empty + s, (i - 1) & 1, &abort_flag)) break;
+        const int gi = u / group_units, o = u - gi * group_units;
+        const int gsz = min(kConsumers, nitems - gi * kConsumers);
+        const int ch = o / gsz, item = gi * kConsumers + (o - ch * gsz);
+        const int p0 = b0 + item * pl.nb, np = min(pl.nb, b1 - p0);
+        const int k0 = ch * pl.Kc, kl = min(pl.Kc, K - k0);
+        unsigned char* dst = stages + (size_t)s * pl.stage_bytes;
+        if (pl.nchunk == 1) {
+          const uint32_t bytes = (uint32_t)np * 4u * (uint32_t)K;  // 2 np rows, contiguous
+          mbar_expect_tx(full + s, bytes);
+          bulk_load(dst, a.w + (size_t)p0 * 2 * K, bytes, full + s, policy);
+        } else {
+          const uint32_t bytes = (uint32_t)kl * 2u;
+          mbar_expect_tx(full + s, 2u * bytes);
+          bulk_load(dst, a.w + (size_t)(2 * p0) * K + k0, bytes, full + s, policy);
+          bulk_load(dst + bytes, a.w + (size_t)(2 * p0 + 1) * K + k0, bytes, full + s, policy);
+        }
+      }
+      // Drain: every copy issued must land before this CTA can exit.
+      volatile int no_abort = 0;
+      const int first = u > pl.stages ? u - pl.stages : 0;
+      for (int v = first; v < u; ++v) mbar_wait(full + v % pl.stages, (v / pl.stages) & 1, &no_abort);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();
+  const bool multi = (EPI == EPI_ROWAR || EPI == EPI_LMHEAD) && c.world > 1;
+  uint32_t epoch = 0;
+  int par = 0;
+  if (EPI == EPI_ROWAR && multi) {
+    epoch = read_epoch(c);
+    par = epoch & 1;
+  }
+  stage_x<M, true>(a, xs);
+
+  const uint4* xv = reinterpret_cast<const uint4*>(xs);
+  const int xstride = K >> 3;
+  unsigned long long best = 0ull;
+  float acc[kRows][M];
+  // acc += both rows of one pair over kl columns starting at k0 (stage rows w0, w1)
+  auto accumulate = [&](const unsigned char* pair_base, int kl, int k0) {
+    const uint4* w0 = reinterpret_cast<const uint4*>(pair_base);
+    const uint4* w1 = reinterpret_cast<const uint4*>(pair_base + (size_t)kl * 2);
+    const int kv = kl >> 3, xo = k0 >> 3;
+    for (int v = lane; v < kv; v += 32) {
+      float f0[8], f1[8];
+      unpack8(w0[v], f0);
+      unpack8(w1[v], f1);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float xf[8];
+        unpack8(xv[m * xstride + xo + v], xf);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          acc[0][m] = fmaf(f0[j], xf[j], acc[0][m]);
+          acc[1][m] = fmaf(f1[j], xf[j], acc[1][m]);
+        }
+      }
+    }
+  };
+  auto zero = [&]() {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
+  };
+  auto finish_pair = [&](int pair, bool ok) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+    if (ok && lane < M && !abort_flag) {
+      const unsigned long long k =
+          epi_pair<EPI>(a, c, multi, par, pair, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
+      best = k > best ? k : best;
+    }
+  };
+
+  for (int gi = 0; gi * kConsumers < nitems; ++gi) {
+    const int gsz = min(kConsumers, nitems - gi * kConsumers);
+    if (warp >= gsz) break;
+    const int item = gi * kConsumers + warp;
+    const int p0 = b0 + item * pl.nb, np = min(pl.nb, b1 - p0);
+    if (pl.nchunk == 1) {
+      // one stage holds the item's np whole pairs
+      const int u = gi * group_units + warp, s = u % pl.stages;
+      const bool ok = mbar_wait(full + s, (u / pl.stages) & 1, &abort_flag);
+      const unsigned char* st = stages + (size_t)s * pl.stage_bytes;
+      for (int pp = 0; pp < np; ++pp) {
+        zero();
+        if (ok) accumulate(st + (size_t)pp * 4 * K, K, 0);
+        if (pp == np - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty + s);
+        }
+        finish_pair(p0 + pp, ok);
+      }
+    } else {
+      // one pair, one K chunk per stage
+      zero();
+      bool ok_all = true;
+      for (int ch = 0; ch < pl.nchunk; ++ch) {
+        const int u = gi * group_units + ch * gsz + warp, s = u % pl.stages;
+        const bool ok = mbar_wait(full + s, (u / pl.stages) & 1, &abort_flag);
+        const int k0 = ch * pl.Kc, kl = min(pl.Kc, K - k0);
+        if (ok) accumulate(stages + (size_t)s * pl.stage_bytes, kl, k0);
+        ok_all = ok_all && ok;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + s);
+      }
+      finish_pair(p0, ok_all);
+    }
+  }
+
+  if constexpr (EPI == EPI_ROWAR) {
+    if (multi) {
+      __threadfence_system();
+      consumer_sync();
+      if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
+      if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
+      consumer_sync();
+      const int rows = 2 * (b1 - b0);
+      for (int e = threadIdx.x; e < rows * M; e += kThreads) {
+        const int m = e / rows, row = 2 * b0 + (e - (e / rows) * rows);
+        float sum = 0.f;
+        for (int src = 0; src < c.world; ++src) sum += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+        bf16* hp = a.h + (size_t)m * a.N + row;
+        *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(sum));
+      }
+      consumer_sync();
+      if (threadIdx.x == 0) {
+        if (atomicAdd(c.state + kDone, 1u) == gridDim.x - 1) {
+          c.state[kDone] = 0u;
+          __threadfence();
+          c.state[kCalls] = epoch;
+        }
+      }
+    }
+  }
+
+  if constexpr (EPI == EPI_LMHEAD) {
+    // lane m < M of every warp holds that warp's best key for token m
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const unsigned long long k = __shfl_sync(0xffffffffu, best, m);
+      if (lane == 0) cta_best[warp][m] = k;
+    }
+    consumer_sync();
+    if (threadIdx.x < M) {
+      unsigned long long b = 0ull;
+      for (int w = 0; w < kConsumers; ++w) b = cta_best[w][threadIdx.x] > b ? cta_best[w][threadIdx.x] : b;
+      if (b) atomicMax(a.keys + threadIdx.x, b);
+    }
+    __threadfence();
+    consumer_sync();
+    if (threadIdx.x == 0) is_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    consumer_sync();
+    if (is_last) {
+      __threadfence();
+      __shared__ unsigned long long fin[M];
+      if (threadIdx.x < M) fin[threadIdx.x] = atomicAdd(a.keys + threadIdx.x, 0ull);
+      consumer_sync();
+      if (multi) {
+        const uint32_t ep = read_epoch(c);
+        const int pr = ep & 1;
+        if (threadIdx.x < M)
+          for (int d = 0; d < c.world; ++d) key_ptr(c, d, pr, c.rank)[threadIdx.x] = fin[threadIdx.x];
+        __threadfence_system();
+        consumer_sync();
+        if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, kMaxCtas, c.rank), ep);
+        if (threadIdx.x < c.world) wait_flag(c, kMaxCtas, threadIdx.x, ep);
+        consumer_sync();
+        if (threadIdx.x < M) {
+          unsigned long long b = 0ull;
+          for (int sx = 0; sx < c.world; ++sx) {
+            const unsigned long long k = __ldcg(key_ptr(c, c.rank, pr, sx) + threadIdx.x);
+            b = k > b ? k : b;
+          }
+          fin[threadIdx.x] = b;
+        }
+        consumer_sync();
+        if (threadIdx.x == 0) c.state[kCalls] = ep;
+      }
+      if (threadIdx.x < M) {
+        a.ids[threadIdx.x] = (int32_t)argmax_key_index(fin[threadIdx.x]);
+        a.keys[threadIdx.x] = 0ull;
+      }
+      if (threadIdx.x == 0) *a.done = 0u;
+    }
+  }
+}
+
 // ---- host side ---------------------------------------------------------------------
+// JSX_GEMV=stream selects the shared-memory streaming kernel wherever its
+// stages fit.  Default: the register-streaming kernel, which measured faster on
+// B200 (gate/up GEMV 44 us vs 55 us with 16 KB stages; the bulk-copy ring
+// delivered ~30 GB/s per SM: each stage costs a fixed ~0.5 us however small).
+static bool stream_kernel_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("JSX_GEMV");
+    v = (e && strcmp(e, "stream") == 0) ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// Stage size in KB (JSX_STAGE_KB = 4, 8 or 16; default 8).  Every consumer warp
+// holds one stage while it computes, so smaller stages leave more of the ring
+// in flight.
+static int stage_kb() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("JSX_STAGE_KB");
+    const int k = e ? atoi(e) : 8;
+    v = (k == 4 || k == 8 || k == 16) ? k : 8;
+  }
+  return v;
+}
+
+// Stage plan of the streaming kernel; false when it does not fit shared memory.
+static bool make_stream_plan(const GemvArgs& a, StreamPlan* pl, size_t* smem) {
+  StreamPlan p = {};
+  p.stage_bytes = stage_kb() * 1024;
+  p.x_bytes = (int)(((size_t)a.M * a.K * sizeof(bf16) + 15) & ~(size_t)15);
+  const size_t sb = (size_t)p.stage_bytes;
+  const size_t pair_bytes = (size_t)a.K * 4;  // two bf16 rows
+  if (pair_bytes * 4 <= sb) p.nb = 4;
+  else if (pair_bytes * 2 <= sb) p.nb = 2;
+  else p.nb = 1;
+  if (pair_bytes <= sb) {
+    p.Kc = a.K;
+    p.nchunk = 1;
+  } else {
+    p.Kc = (int)(sb / 4);
+    p.nchunk = (a.K + p.Kc - 1) / p.Kc;
+  }
+  const size_t budget = 220 * 1024;  // dynamic part; the static part is < 1 KB
+  const size_t fixed = (size_t)p.x_bytes + (size_t)2 * kMaxStages * sizeof(uint64_t);
+  if (fixed + (size_t)kMinStages * sb > budget) return false;
+  const int stages = (int)((budget - fixed) / sb);
+  p.stages = stages > kMaxStages ? kMaxStages : stages;
+  *smem = (size_t)p.stages * sb + (size_t)p.x_bytes + (size_t)2 * p.stages * sizeof(uint64_t);
+  *pl = p;
+  return true;
+}
+
+template <int M, int EPI>
+static int launch_stream(const GemvArgs& a, const CommDev& c, cudaStream_t s, int max_grid,
+                         const StreamPlan& pl, size_t smem) {
+  auto kern = k_gemv_stream<M, EPI>;
+  JSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int grid = sm_count();
+  if (grid > max_grid) grid = max_grid;
+  JSX_CUDA(launch_kernel(kern, dim3(grid), dim3(kStreamThreads), smem, s, a, c, pl));
+  return JSX_OK;
+}
+
 template <int EPI>
 static int launch_gemv(const GemvArgs& a, const CommDev& c, cudaStream_t s, int max_grid) {
+  if (stream_kernel_enabled()) {
+    StreamPlan pl;
+    size_t ssmem = 0;
+    if (make_stream_plan(a, &pl, &ssmem)) {
+      switch (a.M) {
+        case 1: return launch_stream<1, EPI>(a, c, s, max_grid, pl, ssmem);
+        case 2: return launch_stream<2, EPI>(a, c, s, max_grid, pl, ssmem);
+        case 3: return launch_stream<3, EPI>(a, c, s, max_grid, pl, ssmem);
+        case 4: return launch_stream<4, EPI>(a, c, s, max_grid, pl, ssmem);
+        case 5: return launch_stream<5, EPI>(a, c, s, max_grid, pl, ssmem);
+        case 6: return launch_stream<6, EPI>(a, c, s, max_grid, pl, ssmem);
+        case 7: return launch_stream<7, EPI>(a, c, s, max_grid, pl, ssmem);
+        case 8: return launch_stream<8, EPI>(a, c, s, max_grid, pl, ssmem);
+        default: break;
+      }
+    }
+  }
   const size_t smem = (size_t)a.M * a.K * sizeof(bf16);
   JSX_REQUIRE(smem <= 200 * 1024, "activations of %d x %d bf16 exceed the shared-memory stage", a.M, a.K);
   const int ngroups = a.N / kRows;
@@ -578,4 +1048,16 @@ extern "C" int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm
     JSX_REQUIRE(M <= c.max_tokens, "M=%d exceeds the comm buffer (%d tokens)", M, c.max_tokens);
   }
   return launch_gemv<EPI_LMHEAD>(a, c, (cudaStream_t)stream, 1 << 30);
+}
+
+extern "C" int jsx_device_error(int* status) {
+  JSX_REQUIRE(status != nullptr, "null status");
+  uint32_t v = 0;
+  JSX_CUDA(cudaMemcpyFromSymbol(&v, g_gemv_error, sizeof(v)));
+  if (v) {
+    const uint32_t zero = 0;
+    JSX_CUDA(cudaMemcpyToSymbol(g_gemv_error, &zero, sizeof(zero)));
+  }
+  *status = v ? JSX_ETIMEDOUT : JSX_OK;
+  return JSX_OK;
 }

@@ -53,6 +53,10 @@ int jsx_device_sm_count(int* out);
 #define JSX_LAUNCH_PDL 1
 int jsx_set_launch_flags(int flags);
 int jsx_get_launch_flags(void);
+/* Reads and clears the device error word of the weight-streaming kernels: a
+ * bounded shared-memory pipeline wait that gave up (the kernel then finished
+ * without its result) reports JSX_ETIMEDOUT.  Synchronous (a device copy). */
+int jsx_device_error(int* status);
 
 /* ---- packing (load-time, replaces utils/weight_utils.py:248-265 placement) */
 /* W[K][N] (reference layout, (in, out)) -> Wt[N][K].  Plain transpose used by
