@@ -254,7 +254,7 @@ def run_gpu(args) -> None:
     model.init_random(seed=args.seed)
     B, C = args.batch, args.ctx
     e2e_steps = max(16, args.steps // 2)
-    L = C + 2 * args.warmup + args.steps + e2e_steps + 8
+    L = C + 2 * args.warmup + args.steps + e2e_steps + 24
     st = jsx.DecodeState(model, B, L)
     graph = jsx.DecodeGraph(model, st)
     barrier()
@@ -311,24 +311,7 @@ def run_gpu(args) -> None:
     e2e_ms = max_over_ranks((t1 - t0) * 1e3 / e2e_steps)
     clk = clocks.stop()
 
-    # dominant kernel: fused gate/up + SwiGLU GEMV, one launch per layer's weights
-    m = min(B, K.MAX_DECODE_TOKENS)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in model.layers]
-    torch.cuda.synchronize()
-    for (a, b), lp in zip(ev, model.layers):
-        a.record(stream)
-        K.gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m])
-        b.record(stream)
-    torch.cuda.synchronize()
-    dur = [a.elapsed_time(b) for a, b in ev]
-    kern_ms = statistics.mean(dur)
-    lp0 = model.layers[0]
-    kern_bytes = lp0.w_gu.numel() * 2 + m * cfg.hidden_size * 2 + m * model.I_l * 2 + cfg.hidden_size * 2
     peak, peak_kind = measured_hbm_peak()
-    achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
-    trafkey = f"gate_up_swiglu_tp{args.gpus}_m{m}"
-
     # step bytes: weights streamed + KV rows read/written + embedding rows
     c = cfg
     kv_bytes = B * c.num_hidden_layers * 2 * (C + args.warmup + args.steps) * model.nkv_l * c.head_dim * 2
@@ -339,6 +322,49 @@ def run_gpu(args) -> None:
         + c.num_attention_heads * c.head_dim + 2 * c.num_key_value_heads * c.head_dim
         + 3 * c.hidden_size * c.intermediate_size + 2 * c.hidden_size) + 2 * c.vocab_size * c.hidden_size + c.hidden_size)
     mbu_ref = ref_model_bytes / (ms * 1e-3) / (peak * 1e9 * args.gpus)
+
+    fused = model.fused_step and st.step_args is not None
+    phase_us = None
+    if fused:
+        # the whole step is one kernel launch: its duration is the timed step
+        kern_name = "jsx_decode_step (k_decode_step<M>): the whole decode step, one launch per step"
+        kern_ms, kern_bytes = ms, step_bytes
+        trafkey = f"decode_step_tp{args.gpus}_b{B}"
+        # per-phase breakdown from the kernel's %globaltimer trace (CTA 0, after each grid barrier)
+        nl = c.num_hidden_layers
+        tr = torch.zeros(2 + 5 * nl, dtype=torch.int64, device=dev)
+        st.step_args.trace = tr.data_ptr()
+        acc = None
+        for _ in range(8):
+            model.step(st, head=True)
+            d = np.diff(tr.cpu().numpy().astype(np.float64)) / 1e3
+            acc = d if acc is None else acc + d
+        st.step_args.trace = None
+        acc /= 8
+        per = acc[:5 * nl].reshape(nl, 5)
+        names = ["qkv", "attention", "o_proj_allreduce", "gate_up", "down_allreduce"]
+        phase_us = {n: float(per[:, i].mean()) for i, n in enumerate(names)}
+        phase_us["lm_head"] = float(acc[5 * nl])
+        phase_us["note"] = ("mean us per layer (lm_head: once per step) between grid barriers, each "
+                            "phase including its barrier; CTA 0 %globaltimer over 8 eager steps")
+    else:
+        # dominant kernel: fused gate/up + SwiGLU GEMV, one launch per layer's weights
+        m = min(B, K.MAX_DECODE_TOKENS)
+        lp0 = model.layers[0]
+        K.gate_up_swiglu(st.h[:m], lp0.ln2, cfg.rms_norm_eps, lp0.w_gu, st.act[:m])  # loads the module
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in model.layers]
+        torch.cuda.synchronize()
+        for (ea, eb), lp in zip(ev, model.layers):
+            ea.record(stream)
+            K.gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m])
+            eb.record(stream)
+        torch.cuda.synchronize()
+        kern_ms = statistics.median([ea.elapsed_time(eb) for ea, eb in ev])
+        kern_bytes = lp0.w_gu.numel() * 2 + m * cfg.hidden_size * 2 + m * model.I_l * 2 + cfg.hidden_size * 2
+        kern_name = "jsx_gate_up_swiglu (k_gemv<M,EPI_SWIGLU>)"
+        trafkey = f"gate_up_swiglu_tp{args.gpus}_m{m}"
+    achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
 
     launches = model.kernels_per_step(B, head=True) * args.steps
     cpu = cpu_decode_sample(C) if (rank == 0 and world == 1) else None
@@ -352,7 +378,7 @@ def run_gpu(args) -> None:
             "config": workload_config(args),
             "mbu": mbu, "bytes_per_step_per_gpu": step_bytes,
             "mbu_reference_formula": mbu_ref,
-            "roofline": {"bound": "hbm", "kernel": "jsx_gate_up_swiglu (k_gemv<M,EPI_SWIGLU>)",
+            "roofline": {"bound": "hbm", "kernel": kern_name,
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} hbm_gbs (burst, kernel timed alone)",
                          "traffic": ncu_traffic(trafkey), "algorithmic_bytes_per_launch": kern_bytes,
@@ -361,6 +387,7 @@ def run_gpu(args) -> None:
             "e2e": {"value": B / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
             "gpu_launches": launches,
+            "phase_us": phase_us,
             "pdl": K.pdl_enabled(),
             "clocks": clk,
         }

@@ -56,6 +56,8 @@ SIGNATURES = {
     "jsx_lmhead_workspace_size": [I, P],
     "jsx_lmhead_argmax": [P, P, P, F, P, I, I, I, I, P, P, P, SZ, P],
     "jsx_moe_gate": [P, P, P, P, P, I, I, I, I, F, I, P],
+    "jsx_decode_step_workspace_size": [P, P],
+    "jsx_decode_step": [P, P, P],
     "jsx_comm_create": [I, I, I, I, U64, P],
     "jsx_comm_ipc_handle": [P, P],
     "jsx_comm_open_peers": [P, P],

@@ -1,0 +1,263 @@
+// Split-context GQA decode attention: the per-item body shared by the
+// standalone kernel (attention.cu) and the whole-step decode kernel.
+#pragma once
+
+#include <math.h>
+
+#include "common.cuh"
+#include "launch.cuh"
+
+namespace jsx {
+
+constexpr int kChunk = 64;                 // cache rows per split
+constexpr int kRowBlocks = kChunk / 32;    // 32-row blocks per split (one row per lane)
+constexpr int kAttnThreads = 128;
+
+// Work unit ("item"): one split of kChunk cache rows of one (sequence, kv head)
+// for a group of gi query heads of that kv head (hg = G / gi groups).  Splitting
+// the G heads of a kv head over several items spreads a decode step's small
+// attention over more CTAs and lets several CTAs merge splits in parallel.
+struct AttnArgs {
+  const bf16* q;   // [B][nq][hd]
+  const bf16* kc;  // [B][max_seq][nkv][hd]
+  const bf16* vc;
+  bf16* out;       // [B][nq*hd]
+  const int32_t* pos;
+  int B, nq, nkv, hd, max_seq, splits;
+  int gi, hg;      // heads per item, head groups per kv head
+  float scale;
+  float* part;     // [B*nkv*hg][splits][split_stride(gi)]: acc [gi][hd], then m [gi], l [gi] (padded)
+  uint32_t* cnt;   // [B*nkv*hg], zero on entry, left zero
+};
+
+// floats per split record: the accumulator tile, then (m, l) per head, padded so
+// every record starts on a 16-byte boundary (float4 reads in the combine)
+__host__ __device__ __forceinline__ int split_stride(int G, int hd) {
+  return G * hd + ((2 * G + 3) & ~3);
+}
+
+__host__ __device__ __forceinline__ int attn_heads_per_item(int G) {
+  return G % 4 == 0 ? 4 : (G % 2 == 0 ? 2 : 1);
+}
+
+// Workspace: 256-byte header, per-item-group counters padded to 256 bytes, then
+// the split records.
+struct AttnLayout {
+  int gi, hg, splits, stride;
+  size_t counter_bytes;  // header + counters (must be zero before a call)
+  size_t bytes;          // whole workspace
+};
+
+// Heads are split over several items only when (sequence, kv head, split)
+// items alone would leave most of the GPU idle (small batches): each head
+// group re-reads the kv head's rows.
+__host__ __device__ __forceinline__ AttnLayout attn_layout(int B, int nq, int nkv, int hd, int max_seq) {
+  AttnLayout L;
+  const int G = nq / nkv;
+  L.splits = (max_seq + kChunk - 1) / kChunk;
+  L.gi = ((size_t)B * nkv * L.splits >= 256) ? G : attn_heads_per_item(G);
+  L.hg = G / L.gi;
+  L.stride = split_stride(L.gi, hd);
+  const size_t groups = (size_t)B * nkv * L.hg;
+  L.counter_bytes = 256 + ((groups * sizeof(uint32_t) + 255) & ~(size_t)255);
+  L.bytes = L.counter_bytes + groups * L.splits * L.stride * sizeof(float);
+  return L;
+}
+
+// Shared bytes of one item: q (fp32), scores/probabilities, padded K rows, V
+// rows; the combine reuses the K/V area.
+__host__ __device__ __forceinline__ size_t attn_smem(int gi, int hd, int splits) {
+  const int hw = hd / 2;
+  const size_t stage = (size_t)kChunk * (hw + 1) * 4 + (size_t)kChunk * hw * 4;
+  const size_t combine = ((size_t)2 * splits * gi + 2 * gi) * 4;
+  return (size_t)gi * hd * 4 + (size_t)gi * kChunk * 4 + (stage > combine ? stage : combine);
+}
+
+// One work item: cache rows [64 s, 64 s + 64) of item group vb (sequence b,
+// kv head kvh, head group j; vb = (b * nkv + kvh) * hg + j), processed by NT
+// threads; the item that completes the set of splits of its group merges them.
+// kCoherent: read q and the cache with ld.global.cg (they were written by
+// other CTAs of the same kernel).  kEager: load the split's rows together with
+// the position (one round trip; splits past the context load rows they do not
+// use) instead of after it.
+template <int NT, bool kCoherent, bool kEager>
+__device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsigned char* smem_raw) {
+  constexpr int NW = NT / 32;
+  const int G = a.nq / a.nkv, gi = a.gi;
+  const int hd = a.hd, hw = hd >> 1, hq = hd >> 3;  // head dim in 4- and 16-byte words
+  const int stride = split_stride(gi, hd);
+  float* qs = reinterpret_cast<float*>(smem_raw);                  // [gi][hd]
+  float* ps = qs + gi * hd;                                         // [gi][kChunk]
+  uint32_t* ks = reinterpret_cast<uint32_t*>(ps + gi * kChunk);     // [kChunk][hw+1] (padded)
+  uint32_t* vs = ks + kChunk * (hw + 1);                            // [kChunk][hw]
+  __shared__ bool is_last;
+
+  const int b = vb / (a.nkv * a.hg);
+  const int kvh = (vb / a.hg) % a.nkv, j = vb % a.hg;
+  const int head0 = kvh * G + j * gi;  // first query head of the item
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __syncthreads();  // a CTA may run several items back to back over the same shared memory
+
+  // q, the item's K/V rows and the position are loaded together: the rows are
+  // staged whether or not they are inside the context (masked below)
+  const int p0 = s * kChunk;
+  int cur = a.pos[b];
+  const int rows = kEager ? min(kChunk, a.max_seq - p0) : max(0, min(kChunk, min(cur, a.max_seq - 1) + 1 - p0));
+  const bf16* qg = a.q + ((size_t)b * a.nq + head0) * hd;
+  for (int i = tid; i < gi * hd; i += NT) qs[i] = __bfloat162float(kCoherent ? __ldcg(qg + i) : qg[i]);
+  const size_t row_stride = (size_t)a.nkv * hd;  // elements between consecutive cache rows
+  const bf16* kb = a.kc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * hd;
+  const bf16* vbp = a.vc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * hd;
+  for (int i = tid; i < rows * hq; i += NT) {
+    const int r = i / hq, c = i - (i / hq) * hq;
+    const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)r * row_stride) + c;
+    const uint4* vp = reinterpret_cast<const uint4*>(vbp + (size_t)r * row_stride) + c;
+    const uint4 kv = kCoherent ? __ldcg(kp) : *kp;
+    const uint4 vv = kCoherent ? __ldcg(vp) : *vp;
+    uint32_t* kd = ks + r * (hw + 1) + 4 * c;
+    kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
+    reinterpret_cast<uint4*>(vs + r * hw)[c] = vv;
+  }
+  if (cur > a.max_seq - 1) cur = a.max_seq - 1;
+  if (cur < 0) cur = 0;
+  int n = cur + 1 - p0;  // rows of this split inside [0, cur]; n <= rows
+  if (n > kChunk) n = kChunk;
+  float* part = a.part + ((size_t)vb * a.splits + s) * stride;
+  __syncthreads();
+
+  if (n > 0) {
+    // scores: one (head, 32-row block) task per warp pass, one row per lane;
+    // q is a broadcast read, four partial sums keep the FMA chains short
+    for (int t = warp; t < gi * kRowBlocks; t += NW) {
+      const int h = t / kRowBlocks, r = (t - h * kRowBlocks) * 32 + lane;
+      const float* qr = qs + h * hd;
+      const uint32_t* kr = ks + r * (hw + 1);
+      float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll 4
+      for (int w = 0; w < hw; w += 2) {
+        const uint32_t k0 = kr[w], k1 = kr[w + 1];
+        d0 = fmaf(qr[2 * w], bf_lo(k0), d0);
+        d1 = fmaf(qr[2 * w + 1], bf_hi(k0), d1);
+        d2 = fmaf(qr[2 * w + 2], bf_lo(k1), d2);
+        d3 = fmaf(qr[2 * w + 3], bf_hi(k1), d3);
+      }
+      ps[h * kChunk + r] = r < n ? ((d0 + d1) + (d2 + d3)) * a.scale : -INFINITY;
+    }
+    __syncthreads();
+    // softmax pieces of the split: per head max m, e = exp(s - m), sum l
+    for (int h = warp; h < gi; h += NW) {
+      float v[kRowBlocks];
+      float m = -INFINITY;
+#pragma unroll
+      for (int rb = 0; rb < kRowBlocks; ++rb) {
+        v[rb] = ps[h * kChunk + rb * 32 + lane];
+        m = fmaxf(m, v[rb]);
+      }
+      m = warp_max(m);
+      float l = 0.f;
+#pragma unroll
+      for (int rb = 0; rb < kRowBlocks; ++rb) {
+        const float e = (rb * 32 + lane < n) ? expf(v[rb] - m) : 0.f;
+        ps[h * kChunk + rb * 32 + lane] = e;
+        l += e;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        part[gi * hd + h] = m;
+        part[gi * hd + gi + h] = l;
+      }
+    }
+    __syncthreads();
+    // P.V: each thread owns up to 4 (head, dim-pair) outputs and walks the rows
+    // once for all of them (independent accumulators)
+    for (int base = tid; base < gi * hw; base += 4 * NT) {
+      float x0[4], x1[4];
+      int gg[4], ww[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = base + k * NT;
+        gg[k] = i < gi * hw ? i / hw : 0;
+        ww[k] = i < gi * hw ? i - (i / hw) * hw : 0;
+        x0[k] = 0.f;
+        x1[k] = 0.f;
+      }
+#pragma unroll 2
+      for (int p = 0; p < n; ++p) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t vw = vs[p * hw + ww[k]];
+          const float pr = ps[gg[k] * kChunk + p];
+          x0[k] = fmaf(pr, bf_lo(vw), x0[k]);
+          x1[k] = fmaf(pr, bf_hi(vw), x1[k]);
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int i = base + k * NT;
+        if (i < gi * hw) {
+          part[gg[k] * hd + 2 * ww[k]] = x0[k];
+          part[gg[k] * hd + 2 * ww[k] + 1] = x1[k];
+        }
+      }
+    }
+  }
+
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(a.cnt + vb, 1u) == (uint32_t)(a.splits - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  // Combine the splits holding rows [0, cur]: weights w_t[h] = exp(m_t - M) / L
+  // are formed once in shared memory (the staging buffers are free now), then
+  // every output element is a short dot product over the splits.
+  const int used = (cur + kChunk) / kChunk;
+  const float* pb = a.part + (size_t)vb * a.splits * stride;
+  float* wm = reinterpret_cast<float*>(ks);  // [used][gi] m, then weights
+  float* wl = wm + a.splits * gi;            // [used][gi] l
+  float* Mg = wl + a.splits * gi;            // [gi]
+  float* Lg = Mg + gi;                       // [gi]
+  for (int i = tid; i < used * gi; i += NT) {
+    const int t = i / gi, h = i - (i / gi) * gi;
+    wm[i] = __ldcg(pb + (size_t)t * stride + gi * hd + h);
+    wl[i] = __ldcg(pb + (size_t)t * stride + gi * hd + gi + h);
+  }
+  __syncthreads();
+  for (int h = tid; h < gi; h += NT) {
+    float M = -INFINITY;
+    for (int t = 0; t < used; ++t) M = fmaxf(M, wm[t * gi + h]);
+    float L = 0.f;
+    for (int t = 0; t < used; ++t) L = fmaf(wl[t * gi + h], expf(wm[t * gi + h] - M), L);
+    Mg[h] = M;
+    Lg[h] = L;
+  }
+  __syncthreads();
+  for (int i = tid; i < used * gi; i += NT) {
+    const int h = i - (i / gi) * gi;
+    wm[i] = expf(wm[i] - Mg[h]) / Lg[h];
+  }
+  __syncthreads();
+  bf16* ob = a.out + ((size_t)b * a.nq + head0) * hd;
+  const int nv = (gi * hd) >> 2;
+  for (int i = tid; i < nv; i += NT) {
+    const int e = i << 2, h = e / hd;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int t = 0; t < used; ++t) {
+      const float w = wm[t * gi + h];
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)t * stride + e));
+      o.x = fmaf(v.x, w, o.x);
+      o.y = fmaf(v.y, w, o.y);
+      o.z = fmaf(v.z, w, o.z);
+      o.w = fmaf(v.w, w, o.w);
+    }
+    uint2 packed;
+    packed.x = pack2(o.x, o.y);
+    packed.y = pack2(o.z, o.w);
+    *reinterpret_cast<uint2*>(ob + e) = packed;
+  }
+  if (tid == 0) a.cnt[vb] = 0u;
+}
+
+}  // namespace jsx

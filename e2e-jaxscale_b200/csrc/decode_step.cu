@@ -1,0 +1,517 @@
+// Whole decode step in one cooperative kernel (jsx_decode_step).
+//
+// A GLM-4 decode step at batch <= 8 is ~200 dependent phases (5 per layer),
+// each a weight stream of 1-200 MB.  Launched as separate kernels every phase
+// pays its own ramp (CTA launch, activation staging, first DRAM round trip,
+// tail) — about 7 us each on B200, more than the o_proj stream itself.  Here
+// one persistent grid (co-resident by cooperative launch) runs all phases:
+//
+//   embed | per layer: qkv -> attention -> o_proj(+AR) -> gate/up -> down(+AR) | LM head + argmax
+//
+// separated by grid barriers.  Before a warp waits at a barrier it issues its
+// first weight batch of the next phase (weights never depend on activations),
+// so the next stream is already in flight while the barrier completes.
+//
+// The phase bodies are the per-op kernels' device code (gemv_core.cuh,
+// attn_core.cuh) with the same work split (row pair g -> CTA g mod grid), so
+// results equal the per-op entry points'.  Activations written by other CTAs
+// of this kernel are read through L2 (ld.global.cg).  Tensor-parallel
+// all-reduces use the per-CTA flag protocol of comm.cuh with epochs
+// epoch0 .. epoch0 + 2 * n_layers (the LM-head exchange takes the last).
+// Every barrier and peer wait is time-bounded: a timeout sets the error word
+// (jsx_device_error) and the kernel runs on to its end without waiting.
+#include <stdio.h>
+
+#include "attn_core.cuh"
+#include "comm.cuh"
+#include "common.cuh"
+#include "gemv_core.cuh"
+#include "launch.cuh"
+
+namespace jsx {
+
+static __device__ uint32_t g_step_error;  // read and cleared through jsx_device_error
+
+int read_clear_step_error(uint32_t* out) {
+  uint32_t v = 0;
+  JSX_CUDA(cudaMemcpyFromSymbol(&v, g_step_error, sizeof(v)));
+  if (v) {
+    const uint32_t zero = 0;
+    JSX_CUDA(cudaMemcpyToSymbol(g_step_error, &zero, sizeof(zero)));
+  }
+  *out = v;
+  return JSX_OK;
+}
+
+constexpr long long kBarrierLimitCycles = 4000000000ll;  // ~2 s at the 1965 MHz max clock
+
+// workspace layout: [barrier 256 B][LM-head keys/done 256 B][attention workspace]
+constexpr size_t kWsBarrier = 0;
+constexpr size_t kWsLm = 256;
+constexpr size_t kWsAttn = 512;
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Grid barrier: count bar[0], generation bar[1].  Thread 0 of each CTA
+// arrives; the last arrival resets the count and publishes the next
+// generation.  `gen` lives in thread 0 only.
+__device__ __forceinline__ void grid_sync(uint32_t* bar, uint32_t& gen) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const uint32_t target = gen + 1u;
+    if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+      bar[0] = 0u;
+      __threadfence();
+      st_release_gpu(bar + 1, target);
+    } else {
+      const long long t0 = clock64();
+      uint32_t it = 0;
+      while ((int)(ld_acquire_gpu(bar + 1) - target) < 0) {
+        if ((++it & 63u) == 0 && clock64() - t0 > kBarrierLimitCycles) {
+          atomicOr(&g_step_error, 1u);
+          break;
+        }
+      }
+    }
+    gen = target;
+  }
+  __syncthreads();
+}
+
+// Phase trace: CTA 0 stamps %globaltimer after every grid barrier (and at the end).
+__device__ __forceinline__ void trace_mark(uint64_t* trace, int& n) {
+  if (trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0) trace[n] = globaltimer();
+  ++n;
+}
+
+// First weight batch of this warp's first row pair of the next GEMV phase.
+__device__ __forceinline__ void prefetch(Batch& bt, const bf16* w, int K, int N) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = blockIdx.x + gridDim.x * warp;
+  const int nvec = K >> 3;
+  if (g < N / kRows) load_batch(bt, reinterpret_cast<const uint4*>(w) + (size_t)g * kRows * nvec, nvec, 0, lane);
+}
+
+// One GEMV phase (bt holds the first batch of this warp's first group).
+template <int M, int EPI>
+__device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c, bool multi, int par,
+                                           const bf16* xs, Batch& bt, unsigned long long (&best)[M]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = ga.K >> 3, ngroups = ga.N / kRows, G = gridDim.x;
+  const uint4* wbase = reinterpret_cast<const uint4*>(ga.w);
+  const size_t gvecs = (size_t)kRows * nvec;
+  const uint4* xv = reinterpret_cast<const uint4*>(xs);
+  for (int g = blockIdx.x + G * warp; g < ngroups; g += G * kWarps) {
+    const uint4* wv = wbase + (size_t)g * gvecs;
+    float acc[kRows][M];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
+    for (int base = 0; base < nvec; base += 32 * kUnroll) {
+      if (base > 0) load_batch(bt, wv, nvec, base, lane);
+      fma_batch<M>(bt, xv, nvec, base, lane, acc);
+    }
+    const int gn = g + G * kWarps;
+    if (gn < ngroups) load_batch(bt, wbase + (size_t)gn * gvecs, nvec, 0, lane);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+
+    if constexpr (EPI == EPI_QKV) {
+      epi_qkv<M>(ga, g, acc, lane);
+    } else if constexpr (EPI == EPI_SWIGLU) {
+      epi_swiglu<M>(ga, g, acc, lane);
+    } else if constexpr (EPI == EPI_ROWAR) {
+      if (lane < kRows * M) {
+        const int r = lane / M, m = lane - (lane / M) * M;
+        const int row = g * kRows + r;
+        const float v = pick<M>(acc, r, m);
+        if (!multi) {
+          bf16* hp = ga.h + (size_t)m * ga.N + row;
+          *hp = __float2bfloat16_rn(__bfloat162float(__ldcg(hp)) + rbf(v));
+        } else {
+          for (int d = 0; d < c.world; ++d) data_ptr(c, d, par, c.rank, m)[row] = v;
+        }
+      }
+    } else if constexpr (EPI == EPI_LMHEAD) {
+      unsigned long long key = 0ull;
+      int mine = -1;
+      if (lane < kRows * M) {
+        const int r = lane / M, m = lane - (lane / M) * M;
+        const int row = g * kRows + r;
+        const float v = rbf(pick<M>(acc, r, m));
+        if (ga.y) ga.y[(size_t)m * ga.N + row] = __float2bfloat16_rn(v);
+        key = argmax_key(v, (uint32_t)(ga.vocab_offset + row));
+        mine = m;
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const unsigned long long k = warp_max_u64(mine == m ? key : 0ull);
+        best[m] = k > best[m] ? k : best[m];
+      }
+    }
+  }
+}
+
+// Row-parallel exchange of one all-reduce phase: publish this CTA's partial
+// rows to every rank, wait for the peers' and add the rank-ordered sum.
+template <int M>
+__device__ __forceinline__ void allreduce_rows(const GemvArgs& ga, const CommDev& c, uint32_t epoch, int par) {
+  const int ngroups = ga.N / kRows, G = gridDim.x;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
+  if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
+  __syncthreads();
+  const int my_groups = (ngroups - (int)blockIdx.x + G - 1) / G;
+  const int entries = my_groups * kRows * M;
+  for (int e = threadIdx.x; e < entries; e += blockDim.x) {
+    const int gl = e / (kRows * M);
+    const int rem = e - gl * kRows * M;
+    const int r = rem / M, m = rem - (rem / M) * M;
+    const int row = (blockIdx.x + G * gl) * kRows + r;
+    float s = 0.f;
+    for (int src = 0; src < c.world; ++src) s += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+    bf16* hp = ga.h + (size_t)m * ga.N + row;
+    *hp = __float2bfloat16_rn(__bfloat162float(__ldcg(hp)) + rbf(s));
+  }
+}
+
+template <int M>
+__global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_args a, CommDev c) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  bf16* xs = reinterpret_cast<bf16*>(smem_raw);
+  __shared__ bool is_last;
+  __shared__ unsigned long long cta_best[kWarps][M];
+  __shared__ unsigned long long fin[M];
+
+  unsigned char* ws = reinterpret_cast<unsigned char*>(a.workspace);
+  uint32_t* bar = reinterpret_cast<uint32_t*>(ws + kWsBarrier);
+  uint32_t* lm_done = reinterpret_cast<uint32_t*>(ws + kWsLm);
+  unsigned long long* keys = reinterpret_cast<unsigned long long*>(ws + kWsLm + 64);
+  const jsx_layer_weights* layers = a.layers;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool multi = c.world > 1;
+  int tn = 0;
+  uint32_t gen = 0;
+  if (threadIdx.x == 0) gen = ld_acquire_gpu(bar + 1);
+  const uint32_t epoch0 = multi ? read_epoch(c) : 0u;
+  const int qdim = a.n_heads * a.head_dim;
+  const int qkv_rows = (a.n_heads + 2 * a.n_kv_heads) * a.head_dim;
+
+  // ---- embedding (layers/embedding.py:35-51), CTA 0 ----
+  if (blockIdx.x == 0) {
+    const int hv = a.hidden >> 3;
+    for (int i = threadIdx.x; i < M * hv; i += blockDim.x) {
+      const int m = i / hv, v = i - (i / hv) * hv;
+      const int id = a.ids[m];
+      uint4 val;
+      if (id < 0 || id >= a.vocab) {
+        const uint32_t nan2 = 0x7fc07fc0u;
+        val = make_uint4(nan2, nan2, nan2, nan2);
+      } else {
+        val = reinterpret_cast<const uint4*>(a.embed)[(size_t)id * hv + v];
+      }
+      reinterpret_cast<uint4*>(a.h)[(size_t)m * hv + v] = val;
+    }
+  }
+  Batch bt;
+  unsigned long long best[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) best[m] = 0ull;
+  prefetch(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows);
+  grid_sync(bar, gen);
+  trace_mark(a.trace, tn);
+
+  AttnArgs at;
+  at.q = reinterpret_cast<const bf16*>(a.q);
+  at.out = reinterpret_cast<bf16*>(a.attn);
+  at.pos = a.positions;
+  at.B = M;
+  at.nq = a.n_heads;
+  at.nkv = a.n_kv_heads;
+  at.hd = a.head_dim;
+  at.max_seq = a.max_seq;
+  const AttnLayout lay = attn_layout(M, a.n_heads, a.n_kv_heads, a.head_dim, a.max_seq);
+  at.splits = lay.splits;
+  at.gi = lay.gi;
+  at.hg = lay.hg;
+  at.scale = a.scale;
+  at.cnt = reinterpret_cast<uint32_t*>(ws + kWsAttn + 256);
+  at.part = reinterpret_cast<float*>(ws + kWsAttn + lay.counter_bytes);
+  const int attn_items = M * a.n_kv_heads * lay.hg * lay.splits;
+
+  for (int l = 0; l < a.n_layers; ++l) {
+    const jsx_layer_weights L = layers[l];
+    // ---- q/k/v + bias + RoPE + KV write (models/glm4.py:118-120) ----
+    {
+      GemvArgs ga = {};
+      ga.x = reinterpret_cast<const bf16*>(a.h);
+      ga.gamma = reinterpret_cast<const bf16*>(L.ln1);
+      ga.eps = a.eps;
+      ga.w = reinterpret_cast<const bf16*>(L.w_qkv);
+      ga.M = M; ga.K = a.hidden; ga.N = qkv_rows;
+      ga.bias = reinterpret_cast<const bf16*>(L.b_qkv);
+      ga.y = reinterpret_cast<bf16*>(a.q);
+      ga.inv_freq = a.inv_freq; ga.pos = a.positions;
+      ga.kc = reinterpret_cast<bf16*>(L.k_cache); ga.vc = reinterpret_cast<bf16*>(L.v_cache);
+      ga.nq = a.n_heads; ga.nkv = a.n_kv_heads; ga.hd = a.head_dim; ga.rot = a.rotary_dim;
+      ga.max_seq = a.max_seq; ga.tps = 1;
+      stage_x<M, false, true>(ga, xs);
+      gemv_phase<M, EPI_QKV>(ga, c, multi, 0, xs, bt, best);
+    }
+    grid_sync(bar, gen);
+  trace_mark(a.trace, tn);
+    // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
+    at.kc = reinterpret_cast<const bf16*>(L.k_cache);
+    at.vc = reinterpret_cast<const bf16*>(L.v_cache);
+    for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
+      attn_item<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
+    prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden);
+    grid_sync(bar, gen);
+  trace_mark(a.trace, tn);
+    // ---- o_proj + all-reduce + residual (layers/attention.py:159, models/glm4.py:124) ----
+    {
+      GemvArgs ga = {};
+      ga.x = reinterpret_cast<const bf16*>(a.attn);
+      ga.w = reinterpret_cast<const bf16*>(L.w_o);
+      ga.M = M; ga.K = qdim; ga.N = a.hidden;
+      ga.h = reinterpret_cast<bf16*>(a.h);
+      const uint32_t ep = epoch0 + 2u * l;
+      stage_x<M, false, true>(ga, xs);
+      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep & 1, xs, bt, best);
+      if (multi) allreduce_rows<M>(ga, c, ep, ep & 1);
+    }
+    prefetch(bt, reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter);
+    grid_sync(bar, gen);
+  trace_mark(a.trace, tn);
+    // ---- post-attention norm + gate/up + SwiGLU (models/glm4.py:128, :46-48) ----
+    {
+      GemvArgs ga = {};
+      ga.x = reinterpret_cast<const bf16*>(a.h);
+      ga.gamma = reinterpret_cast<const bf16*>(L.ln2);
+      ga.eps = a.eps;
+      ga.w = reinterpret_cast<const bf16*>(L.w_gu);
+      ga.M = M; ga.K = a.hidden; ga.N = 2 * a.inter;
+      ga.y = reinterpret_cast<bf16*>(a.act);
+      stage_x<M, false, true>(ga, xs);
+      gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0, xs, bt, best);
+    }
+    prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden);
+    grid_sync(bar, gen);
+  trace_mark(a.trace, tn);
+    // ---- down_proj + all-reduce + residual (models/glm4.py:49, :130) ----
+    {
+      GemvArgs ga = {};
+      ga.x = reinterpret_cast<const bf16*>(a.act);
+      ga.w = reinterpret_cast<const bf16*>(L.w_d);
+      ga.M = M; ga.K = a.inter; ga.N = a.hidden;
+      ga.h = reinterpret_cast<bf16*>(a.h);
+      const uint32_t ep = epoch0 + 2u * l + 1u;
+      stage_x<M, false, true>(ga, xs);
+      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep & 1, xs, bt, best);
+      if (multi) allreduce_rows<M>(ga, c, ep, ep & 1);
+    }
+    if (l + 1 < a.n_layers)
+      prefetch(bt, reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows);
+    else if (a.head)
+      prefetch(bt, reinterpret_cast<const bf16*>(a.lm_head), a.hidden, a.vocab_local);
+    grid_sync(bar, gen);
+  trace_mark(a.trace, tn);
+  }
+
+  const uint32_t last_epoch = epoch0 + 2u * a.n_layers - 1u;
+  if (!a.head) {
+    // prefill step: no LM head; advance the positions once every CTA is done
+    if (blockIdx.x == 0 && threadIdx.x < M) {
+      if (threadIdx.x == 0 && a.trace) a.trace[tn] = globaltimer();
+      if (a.advance) a.positions[threadIdx.x] += 1;
+      if (threadIdx.x == 0 && multi) c.state[kCalls] = last_epoch;
+    }
+    return;
+  }
+
+  // ---- final norm + LM head + greedy argmax (models/glm4.py:193, :251; runner.py:297) ----
+  {
+    GemvArgs ga = {};
+    ga.x = reinterpret_cast<const bf16*>(a.h);
+    ga.gamma = reinterpret_cast<const bf16*>(a.final_norm);
+    ga.eps = a.eps;
+    ga.w = reinterpret_cast<const bf16*>(a.lm_head);
+    ga.M = M; ga.K = a.hidden; ga.N = a.vocab_local;
+    ga.y = reinterpret_cast<bf16*>(a.logits);
+    ga.vocab_offset = a.vocab_offset;
+    stage_x<M, false, true>(ga, xs);
+    gemv_phase<M, EPI_LMHEAD>(ga, c, multi, 0, xs, bt, best);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int m = 0; m < M; ++m) cta_best[warp][m] = best[m];
+  }
+  __syncthreads();
+  if (threadIdx.x < M) {
+    unsigned long long b = 0ull;
+    for (int w = 0; w < kWarps; ++w) b = cta_best[w][threadIdx.x] > b ? cta_best[w][threadIdx.x] : b;
+    atomicMax(keys + threadIdx.x, b);
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = atomicAdd(lm_done, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (threadIdx.x < M) fin[threadIdx.x] = atomicAdd(keys + threadIdx.x, 0ull);
+  __syncthreads();
+  if (multi) {
+    const uint32_t ep = last_epoch + 1u;
+    const int pr = ep & 1;
+    if (threadIdx.x < M)
+      for (int d = 0; d < c.world; ++d) key_ptr(c, d, pr, c.rank)[threadIdx.x] = fin[threadIdx.x];
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, kMaxCtas, c.rank), ep);
+    if (threadIdx.x < c.world) wait_flag(c, kMaxCtas, threadIdx.x, ep);
+    __syncthreads();
+    if (threadIdx.x < M) {
+      unsigned long long b = 0ull;
+      for (int s = 0; s < c.world; ++s) {
+        const unsigned long long k = __ldcg(key_ptr(c, c.rank, pr, s) + threadIdx.x);
+        b = k > b ? k : b;
+      }
+      fin[threadIdx.x] = b;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) c.state[kCalls] = ep;
+  }
+  if (threadIdx.x < M) {
+    a.ids[threadIdx.x] = (int32_t)argmax_key_index(fin[threadIdx.x]);
+    keys[threadIdx.x] = 0ull;
+    if (a.advance) a.positions[threadIdx.x] += 1;
+  }
+  if (threadIdx.x == 0) {
+    *lm_done = 0u;
+    if (a.trace) a.trace[tn] = globaltimer();
+  }
+}
+
+static size_t step_smem(const jsx_decode_step_args& a) {
+  const int M = a.batch;
+  int kmax = a.hidden;
+  if (a.inter > kmax) kmax = a.inter;
+  if (a.n_heads * a.head_dim > kmax) kmax = a.n_heads * a.head_dim;
+  const size_t x = (size_t)M * kmax * sizeof(bf16);
+  const AttnLayout lay = attn_layout(M, a.n_heads, a.n_kv_heads, a.head_dim, a.max_seq);
+  const size_t at = attn_smem(lay.gi, a.head_dim, lay.splits);
+  return x > at ? x : at;
+}
+
+static size_t step_workspace(const jsx_decode_step_args& a) {
+  return kWsAttn + attn_layout(a.batch, a.n_heads, a.n_kv_heads, a.head_dim, a.max_seq).bytes;
+}
+
+static int check_step(const jsx_decode_step_args* a) {
+  JSX_REQUIRE(a != nullptr, "null args");
+  JSX_REQUIRE(a->batch >= 1 && a->batch <= kMaxM, "batch=%d outside 1..%d", a->batch, kMaxM);
+  JSX_REQUIRE(a->hidden >= 8 && a->hidden % 8 == 0, "hidden=%d must be a multiple of 8", a->hidden);
+  JSX_REQUIRE(a->n_heads >= 1 && a->n_kv_heads >= 1 && a->n_heads % a->n_kv_heads == 0,
+              "heads %d / kv heads %d", a->n_heads, a->n_kv_heads);
+  JSX_REQUIRE(a->head_dim >= 8 && a->head_dim % 8 == 0, "head_dim=%d must be a multiple of 8", a->head_dim);
+  JSX_REQUIRE(a->rotary_dim >= 0 && a->rotary_dim <= a->head_dim && a->rotary_dim % 2 == 0,
+              "rotary_dim=%d", a->rotary_dim);
+  JSX_REQUIRE(a->inter >= 8 && a->inter % 8 == 0, "inter=%d must be a multiple of 8", a->inter);
+  JSX_REQUIRE(a->vocab_local >= 2 && a->vocab_local % 2 == 0 && a->vocab >= a->vocab_local,
+              "vocab_local=%d", a->vocab_local);
+  JSX_REQUIRE(a->max_seq >= 1 && a->n_layers >= 1, "max_seq=%d n_layers=%d", a->max_seq, a->n_layers);
+  JSX_REQUIRE(a->layers && a->embed && a->final_norm && a->lm_head && a->inv_freq && a->ids &&
+                  a->positions && a->h && a->q && a->attn && a->act && a->workspace,
+              "null pointer argument");
+  JSX_REQUIRE(aligned16(a->embed) && aligned16(a->lm_head) && aligned16(a->final_norm) && aligned16(a->h) &&
+                  aligned16(a->q) && aligned16(a->attn) && aligned16(a->act) && aligned16(a->workspace),
+              "tensors must be 16-byte aligned");
+  JSX_REQUIRE(a->workspace_bytes >= step_workspace(*a), "workspace of %zu bytes required",
+              step_workspace(*a));
+  return JSX_OK;
+}
+
+}  // namespace jsx
+
+using namespace jsx;
+
+
+extern "C" int jsx_decode_step_workspace_size(const jsx_decode_step_args* args, size_t* bytes) {
+  JSX_REQUIRE(args && bytes, "null argument");
+  JSX_REQUIRE(args->batch >= 1 && args->n_kv_heads >= 1 && args->n_heads % args->n_kv_heads == 0 &&
+                  args->max_seq >= 1,
+              "bad shape");
+  *bytes = step_workspace(*args);
+  return JSX_OK;
+}
+
+namespace jsx {
+CommDev comm_view(jsx_comm* comm);  // comm.cu
+}
+
+extern "C" int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args, void* stream) {
+  int st = check_step(args);
+  if (st) return st;
+  const jsx_decode_step_args& a = *args;
+  CommDev c = {};
+  c.world = 1;
+  if (comm) {
+    c = jsx::comm_view(comm);
+    JSX_REQUIRE(a.batch <= c.max_tokens && a.hidden <= c.hidden,
+                "batch %d / hidden %d exceed the comm buffer", a.batch, a.hidden);
+  }
+  const size_t smem = step_smem(a);
+  JSX_REQUIRE(smem <= 200 * 1024, "step needs %zu bytes of shared memory", smem);
+#define JSX_STEP_CASE(MM)                                                                    \
+  case MM: {                                                                                 \
+    auto kern = k_decode_step<MM>;                                                           \
+    JSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+                                  (int)smem));                                               \
+    int occ = 0;                                                                             \
+    JSX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kThreads, smem));     \
+    JSX_REQUIRE(occ > 0, "decode step kernel does not fit on an SM");                       \
+    if (occ > 2) occ = 2;                                                                    \
+    int grid = sm_count() * occ;                                                             \
+    if (grid > kMaxCtas) grid = kMaxCtas;                                                    \
+    cudaLaunchConfig_t cfg = {};                                                             \
+    cfg.gridDim = dim3(grid);                                                                \
+    cfg.blockDim = dim3(kThreads);                                                           \
+    cfg.dynamicSmemBytes = smem;                                                             \
+    cfg.stream = (cudaStream_t)stream;                                                       \
+    cudaLaunchAttribute attr[1];                                                             \
+    attr[0].id = cudaLaunchAttributeCooperative;                                             \
+    attr[0].val.cooperative = 1;                                                             \
+    cfg.attrs = attr;                                                                        \
+    cfg.numAttrs = 1;                                                                        \
+    JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, a, c));                                          \
+    return JSX_OK;                                                                           \
+  }
+  switch (a.batch) {
+    JSX_STEP_CASE(1)
+    JSX_STEP_CASE(2)
+    JSX_STEP_CASE(3)
+    JSX_STEP_CASE(4)
+    JSX_STEP_CASE(5)
+    JSX_STEP_CASE(6)
+    JSX_STEP_CASE(7)
+    JSX_STEP_CASE(8)
+    default:
+      break;
+  }
+#undef JSX_STEP_CASE
+  set_error("batch %d outside the decode-step kernel set", a.batch);
+  return JSX_ENOTSUP;
+}

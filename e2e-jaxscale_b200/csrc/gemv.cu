@@ -28,230 +28,10 @@
 
 #include "comm.cuh"
 #include "common.cuh"
+#include "gemv_core.cuh"
 #include "launch.cuh"
 
 namespace jsx {
-
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kRows = 2;    // rows per warp group (the qkv / gate_up packings assume 2)
-constexpr int kUnroll = 8;  // 16-byte vectors per lane per row in flight
-constexpr int kMaxM = 8;
-
-enum Epi { EPI_LINEAR = 0, EPI_QKV = 1, EPI_SWIGLU = 2, EPI_ROWAR = 3, EPI_LMHEAD = 4 };
-
-struct GemvArgs {
-  const bf16* x;      // [M][K]
-  const bf16* gamma;  // RMSNorm gain [K] or null
-  float eps;
-  const bf16* w;      // packed [N][K]
-  int M, K, N;        // N = packed rows
-  // EPI_LINEAR
-  const bf16* bias;
-  bf16* y;            // [M][N] (linear), q_out [M][nq*hd] (qkv), act [M][N/2] (swiglu)
-  // EPI_QKV
-  const float* inv_freq;
-  const int32_t* pos;
-  bf16* kc;
-  bf16* vc;
-  int nq, nkv, hd, rot, max_seq, tps;
-  // EPI_ROWAR
-  bf16* h;            // residual [M][N]
-  // EPI_LMHEAD
-  int vocab_offset;
-  unsigned long long* keys;  // [M] workspace (zero on entry, left zero)
-  uint32_t* done;            // workspace counter (zero on entry, left zero)
-  int32_t* ids;              // [M]
-};
-
-// ---- activations -> shared memory (optionally RMS-normalised) --------------
-// layers/normalization.py:31-37: y = bf16((x * rsqrt(mean(x^2) + eps)) * g), fp32 inside.
-// Barrier over the threads that stage the activations: the whole CTA (v1
-// kernel) or the 8 consumer warps of the streaming kernel (named barrier 1).
-template <bool kNamed>
-__device__ __forceinline__ void stage_sync() {
-  if constexpr (kNamed) asm volatile("bar.sync 1, 256;" ::: "memory");
-  else __syncthreads();
-}
-
-template <int M, bool kNamed = false>
-__device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
-  constexpr int NT = kThreads;  // 256 staging threads in both kernels
-  const int nvec = a.K >> 3;
-  const uint4* xv = reinterpret_cast<const uint4*>(a.x);
-  uint4* sv = reinterpret_cast<uint4*>(xs);
-  if (a.gamma == nullptr) {
-    for (int i = threadIdx.x; i < M * nvec; i += NT) sv[i] = xv[i];
-    stage_sync<kNamed>();
-    return;
-  }
-  __shared__ float red[M][kWarps];
-  __shared__ float rstd[M];
-  float ss[M];
-#pragma unroll
-  for (int m = 0; m < M; ++m) ss[m] = 0.f;
-  for (int v = threadIdx.x; v < nvec; v += NT) {
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      float f[8];
-      unpack8(xv[m * nvec + v], f);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss[m] = fmaf(f[j], f[j], ss[m]);
-    }
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int m = 0; m < M; ++m) {
-    float s = warp_sum(ss[m]);
-    if (lane == 0) red[m][warp] = s;
-  }
-  stage_sync<kNamed>();
-  if (threadIdx.x < M) {
-    float t = 0.f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) t += red[threadIdx.x][w];
-    rstd[threadIdx.x] = 1.0f / sqrtf(t / (float)a.K + a.eps);
-  }
-  stage_sync<kNamed>();
-  const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
-  for (int i = threadIdx.x; i < M * nvec; i += NT) {
-    const int m = i / nvec, v = i - m * nvec;
-    float f[8], g[8];
-    unpack8(xv[i], f);
-    unpack8(gv[v], g);
-    const float r = rstd[m];
-    uint4 o;
-    o.x = pack2((f[0] * r) * g[0], (f[1] * r) * g[1]);
-    o.y = pack2((f[2] * r) * g[2], (f[3] * r) * g[3]);
-    o.z = pack2((f[4] * r) * g[4], (f[5] * r) * g[5]);
-    o.w = pack2((f[6] * r) * g[6], (f[7] * r) * g[7]);
-    sv[i] = o;
-  }
-  stage_sync<kNamed>();
-}
-
-// ---- weight batches -----------------------------------------------------------
-struct Batch {
-  uint4 w[kUnroll][kRows];
-};
-
-__device__ __forceinline__ void load_batch(Batch& b, const uint4* __restrict__ wv, int nvec,
-                                           int base, int lane) {
-#pragma unroll
-  for (int u = 0; u < kUnroll; ++u) {
-    const int v = base + u * 32 + lane;
-#pragma unroll
-    for (int r = 0; r < kRows; ++r)
-      b.w[u][r] = (v < nvec) ? ld_stream(wv + (size_t)r * nvec + v) : make_uint4(0, 0, 0, 0);
-  }
-}
-
-template <int M>
-__device__ __forceinline__ void fma_batch(const Batch& b, const uint4* __restrict__ xv, int nvec,
-                                          int base, int lane, float (&acc)[kRows][M]) {
-#pragma unroll
-  for (int u = 0; u < kUnroll; ++u) {
-    const int v = base + u * 32 + lane;
-    if (v < nvec) {
-      float wf[kRows][8];
-#pragma unroll
-      for (int r = 0; r < kRows; ++r) unpack8(b.w[u][r], wf[r]);
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float xf[8];
-        unpack8(xv[m * nvec + v], xf);
-#pragma unroll
-        for (int r = 0; r < kRows; ++r)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[r][m] = fmaf(wf[r][j], xf[j], acc[r][m]);
-      }
-    }
-  }
-}
-
-// Value (r, m) of a warp-reduced accumulator tile, selected without dynamic
-// register indexing.
-template <int M>
-__device__ __forceinline__ float pick(const float (&acc)[kRows][M], int r, int m) {
-  float v = 0.f;
-#pragma unroll
-  for (int rr = 0; rr < kRows; ++rr)
-#pragma unroll
-    for (int mm = 0; mm < M; ++mm)
-      if (rr == r && mm == m) v = acc[rr][mm];
-  return v;
-}
-
-// ---- epilogues ------------------------------------------------------------------
-// qkv packing (jsx_pack_qkv): per head hd/2 groups; group j < rot/2 holds rows
-// (j, j + rot/2) (a neox rotary pair), group j >= rot/2 holds the pass-through
-// pair (rot + 2(j - rot/2), +1).  Heads: q (nq), then k (nkv), then v (nkv).
-__device__ __forceinline__ void qkv_store(const GemvArgs& a, int g, int m, float acc0, float acc1) {
-  const int gph = a.hd >> 1;
-  const int head = g / gph, j = g - head * gph;
-  const int rh = a.rot >> 1;
-  int d0, d1;
-  bool rotary;
-  if (j < rh) { d0 = j; d1 = j + rh; rotary = true; }
-  else { d0 = a.rot + 2 * (j - rh); d1 = d0 + 1; rotary = false; }
-  const int col0 = head * a.hd + d0, col1 = head * a.hd + d1;  // index into q|k|v
-  float x1 = rbf(acc0);
-  float x2 = rbf(acc1);
-  if (a.bias) {
-    x1 = rbf(x1 + ldbf(a.bias + col0));
-    x2 = rbf(x2 + ldbf(a.bias + col1));
-  }
-  const int p = a.pos[m];
-  const bool is_v = head >= a.nq + a.nkv;
-  if (rotary && !is_v) {
-    // layers/rotary.py:56-58 (fp32 angle, bf16 cos/sin) and :88-91 (half split)
-    float s, c;
-    sincosf((float)p * a.inv_freq[j], &s, &c);
-    c = rbf(c);
-    s = rbf(s);
-    const float o1 = rbf(rbf(x1 * c) - rbf(x2 * s));
-    const float o2 = rbf(rbf(x2 * c) + rbf(x1 * s));
-    x1 = o1;
-    x2 = o2;
-  }
-  if (head < a.nq) {
-    bf16* q = a.y + (size_t)m * a.nq * a.hd + head * a.hd;
-    q[d0] = __float2bfloat16_rn(x1);
-    q[d1] = __float2bfloat16_rn(x2);
-  } else {
-    const int kvh = is_v ? head - a.nq - a.nkv : head - a.nq;
-    const int b = m / a.tps;
-    // dynamic_update_slice clamps the start row into [0, max_seq - 1] (layers/attention.py:127-133)
-    const int slot = p < 0 ? 0 : (p >= a.max_seq ? a.max_seq - 1 : p);
-    bf16* dst = (is_v ? a.vc : a.kc) + (((size_t)b * a.max_seq + slot) * a.nkv + kvh) * a.hd;
-    dst[d0] = __float2bfloat16_rn(x1);
-    dst[d1] = __float2bfloat16_rn(x2);
-  }
-}
-
-// gate/up packing (jsx_pack_gate_up): group j holds rows (gate_j, up_j).
-// models/glm4.py:47-49 with jax.nn.silu(x) = x * sigmoid(x) on bf16 arrays.
-__device__ __forceinline__ void swiglu_store(const GemvArgs& a, int g, int m, float acc0, float acc1) {
-  const float gate = rbf(acc0);
-  const float up = rbf(acc1);
-  const float sig = rbf(1.0f / (1.0f + expf(-gate)));
-  const float act = rbf(rbf(gate * sig) * up);
-  a.y[(size_t)m * (a.N >> 1) + g] = __float2bfloat16_rn(act);
-}
-
-template <int M>
-__device__ __forceinline__ void epi_qkv(const GemvArgs& a, int g, const float (&acc)[kRows][M],
-                                        int lane) {
-  if (lane >= M) return;
-  qkv_store(a, g, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
-}
-
-template <int M>
-__device__ __forceinline__ void epi_swiglu(const GemvArgs& a, int g, const float (&acc)[kRows][M],
-                                           int lane) {
-  if (lane >= M) return;
-  swiglu_store(a, g, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
-}
 
 // ---- the kernel ------------------------------------------------------------------
 template <int M, int EPI>
@@ -1050,6 +830,10 @@ extern "C" int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm
   return launch_gemv<EPI_LMHEAD>(a, c, (cudaStream_t)stream, 1 << 30);
 }
 
+namespace jsx {
+int read_clear_step_error(uint32_t* out);  // decode_step.cu
+}
+
 extern "C" int jsx_device_error(int* status) {
   JSX_REQUIRE(status != nullptr, "null status");
   uint32_t v = 0;
@@ -1058,6 +842,9 @@ extern "C" int jsx_device_error(int* status) {
     const uint32_t zero = 0;
     JSX_CUDA(cudaMemcpyToSymbol(g_gemv_error, &zero, sizeof(zero)));
   }
-  *status = v ? JSX_ETIMEDOUT : JSX_OK;
+  uint32_t w = 0;
+  const int st = jsx::read_clear_step_error(&w);
+  if (st != JSX_OK) return st;
+  *status = (v | w) ? JSX_ETIMEDOUT : JSX_OK;
   return JSX_OK;
 }

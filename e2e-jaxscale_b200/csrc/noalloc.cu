@@ -24,6 +24,7 @@
 //    first call before any stream capture begins.
 #include <mutex>
 
+#include "attn_core.cuh"
 #include "common.cuh"
 
 namespace jsx {
@@ -68,10 +69,9 @@ extern "C" int jsx_attn_decode_noalloc(const void* q, const void* k_cache, const
   void* ws = nullptr;
   const int sa = scratch_address(dev, &ws);
   if (sa != JSX_OK) return sa;
-  // The header and per-(sequence, kv-head) counters sit in the first 256 +
-  // round_up(B * nkv * 4, 256) bytes (the jsx_attn_decode workspace layout);
-  // they must be zero when the kernel starts.
-  const size_t counters = 256 + (((size_t)B * nkv * sizeof(uint32_t) + 255) & ~(size_t)255);
+  // The header and the per-item-group counters open the jsx_attn_decode
+  // workspace (attn_layout); they must be zero when the kernel starts.
+  const size_t counters = attn_layout(B, nq, nkv, head_dim, max_seq).counter_bytes;
   JSX_CUDA(cudaMemsetAsync(ws, 0, counters, (cudaStream_t)stream));
   return jsx_attn_decode(q, k_cache, v_cache, out, positions, B, nq, nkv, head_dim, max_seq, scale,
                          ws, kNoAllocScratchBytes, stream);

@@ -19,6 +19,7 @@ CUDA graph (DecodeGraph).
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 import torch.distributed as dist
@@ -53,6 +54,30 @@ class DecodeState:
         self.lm_ws = K.lmhead_workspace(CHUNK, dev)
         self.logits = (torch.zeros(batch, model.V_l, dtype=torch.bfloat16, device=dev)
                        if want_logits else None)
+        self.step_args = None
+        if batch <= CHUNK and model.layers:
+            self._build_step_args(model)
+
+    def _build_step_args(self, model: "GLM4ForCausalLM") -> None:
+        """Arguments of the whole-step kernel (jsx_decode_step) over these buffers."""
+        c, dev = model.config, model.device
+        a = K.StepArgs()
+        a.batch, a.hidden, a.n_heads, a.n_kv_heads = self.batch, c.hidden_size, model.nq_l, model.nkv_l
+        a.head_dim, a.rotary_dim, a.inter = c.head_dim, model.rotary.rotary_dim, model.I_l
+        a.vocab, a.vocab_local, a.vocab_offset = c.vocab_size, model.V_l, model.vocab_offset
+        a.max_seq, a.n_layers = self.max_seq, len(model.layers)
+        a.eps, a.scale = c.rms_norm_eps, model.scale
+        self.layer_table = K.layer_table(model.layers, self.caches, dev)
+        a.layers = self.layer_table.data_ptr()
+        a.embed, a.final_norm, a.lm_head = model.embed.data_ptr(), model.norm.data_ptr(), model.lm_head.data_ptr()
+        a.inv_freq = model.inv_freq.data_ptr()
+        a.ids, a.positions = self.ids.data_ptr(), self.pos.data_ptr()
+        a.advance, a.head = 1, 1
+        a.h, a.q, a.attn, a.act = self.h.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(), self.act.data_ptr()
+        a.logits = None if self.logits is None else self.logits.data_ptr()
+        self.step_ws = K.step_workspace(a, dev)
+        a.workspace, a.workspace_bytes = self.step_ws.data_ptr(), self.step_ws.numel()
+        self.step_args = a
 
 
 class GLM4ForCausalLM:
@@ -83,6 +108,7 @@ class GLM4ForCausalLM:
         self.norm = None      # [H]
         self.lm_head = None   # [V_l, H]
         self.comm = mesh.comm(CHUNK, c.hidden_size) if t > 1 else None
+        self.fused_step = os.environ.get("JSX_FUSED_STEP", "1") != "0"
 
     # ---- weights ----
     def load_state(self, params) -> None:
@@ -151,12 +177,21 @@ class GLM4ForCausalLM:
                             None if st.logits is None else st.logits[b0:b1])
 
     def step(self, st: DecodeState, head: bool = True) -> None:
+        """One token per sequence at st.pos; st.ids <- greedy tokens (head), st.pos += 1.
+        Batch <= 8 runs the whole step as one kernel (jsx_decode_step) unless
+        self.fused_step is False; larger batches chain the per-op kernels."""
+        if self.fused_step and st.step_args is not None:
+            st.step_args.head = 1 if head else 0
+            K.decode_step(self.comm, st.step_args)
+            return
         self.run_body(st)
         if head:
             self.run_head(st)
         st.pos.add_(1)
 
     def kernels_per_step(self, batch: int, head: bool = True) -> int:
+        if self.fused_step and batch <= CHUNK:
+            return 1
         ch = math.ceil(batch / CHUNK)
         n = 1 + self.config.num_hidden_layers * (1 + 4 * ch)
         return n + (ch if head else 0)

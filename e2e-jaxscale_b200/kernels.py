@@ -218,3 +218,46 @@ def moe_gate(x, w_nk, k, scale, norm=True, correction_bias=None, logits_given=Fa
     call("jsx_moe_gate", _p(x), _p(w), _p(correction_bias), _p(topk_w), _p(topk_i), N, H, E, k,
          ctypes.c_float(scale), int(bool(norm)), _stream())
     return topk_w, topk_i
+
+
+# ---- whole decode step (jsx_decode_step) --------------------------------------
+class LayerWeights(ctypes.Structure):
+    """jsx_layer_weights (include/jsx.h)."""
+    _fields_ = [(n, ctypes.c_void_p) for n in
+                ("ln1", "w_qkv", "b_qkv", "w_o", "ln2", "w_gu", "w_d", "k_cache", "v_cache")]
+
+
+class StepArgs(ctypes.Structure):
+    """jsx_decode_step_args (include/jsx.h)."""
+    _fields_ = ([(n, ctypes.c_int) for n in ("batch", "hidden", "n_heads", "n_kv_heads", "head_dim",
+                                            "rotary_dim", "inter", "vocab", "vocab_local", "vocab_offset",
+                                            "max_seq", "n_layers")]
+                + [("eps", ctypes.c_float), ("scale", ctypes.c_float)]
+                + [(n, ctypes.c_void_p) for n in ("layers", "embed", "final_norm", "lm_head", "inv_freq",
+                                                  "ids", "positions")]
+                + [("advance", ctypes.c_int), ("head", ctypes.c_int)]
+                + [(n, ctypes.c_void_p) for n in ("h", "q", "attn", "act", "logits", "workspace")]
+                + [("workspace_bytes", ctypes.c_size_t), ("trace", ctypes.c_void_p)])
+
+
+def layer_table(layers, caches, device) -> torch.Tensor:
+    """Device array of jsx_layer_weights for the whole-step kernel."""
+    arr = (LayerWeights * len(layers))()
+    for e, lp, c in zip(arr, layers, caches):
+        e.ln1, e.w_qkv = lp.ln1.data_ptr(), lp.w_qkv.data_ptr()
+        e.b_qkv = None if lp.b_qkv is None else lp.b_qkv.data_ptr()
+        e.w_o, e.ln2, e.w_gu, e.w_d = lp.w_o.data_ptr(), lp.ln2.data_ptr(), lp.w_gu.data_ptr(), lp.w_d.data_ptr()
+        e.k_cache, e.v_cache = c.k.data_ptr(), c.v.data_ptr()
+    raw = torch.frombuffer(bytearray(bytes(arr)), dtype=torch.uint8)
+    return raw.to(device)
+
+
+def step_workspace(args: StepArgs, device) -> torch.Tensor:
+    n = ctypes.c_size_t(0)
+    call("jsx_decode_step_workspace_size", ctypes.byref(args), ctypes.byref(n))
+    return torch.zeros(n.value, dtype=torch.uint8, device=device)
+
+
+def decode_step(comm, args: StepArgs) -> None:
+    handle = None if comm is None else comm.handle
+    call("jsx_decode_step", handle, ctypes.byref(args), _stream())

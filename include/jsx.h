@@ -53,9 +53,10 @@ int jsx_device_sm_count(int* out);
 #define JSX_LAUNCH_PDL 1
 int jsx_set_launch_flags(int flags);
 int jsx_get_launch_flags(void);
-/* Reads and clears the device error word of the weight-streaming kernels: a
- * bounded shared-memory pipeline wait that gave up (the kernel then finished
- * without its result) reports JSX_ETIMEDOUT.  Synchronous (a device copy). */
+/* Reads and clears the device error words of the streaming GEMV and of the
+ * whole-step kernel: a bounded pipeline or grid-barrier wait that gave up (the
+ * kernel then finished without its result) reports JSX_ETIMEDOUT.
+ * Synchronous (a device copy). */
 int jsx_device_error(int* status);
 
 /* ---- packing (load-time, replaces utils/weight_utils.py:248-265 placement) */
@@ -155,6 +156,54 @@ int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, flo
                       const void* w_vocab, int vocab_local, int vocab_offset, int M, int hidden,
                       void* logits_out, int32_t* ids_out, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/* ---- whole decode step ------------------------------------------------------
+ * One cooperative kernel runs a full GLM-4 decode step for batch <= 8 on this
+ * rank: embedding, every decoder layer (the work of jsx_qkv_rope_cache,
+ * jsx_attn_decode, jsx_row_linear_allreduce (o_proj), jsx_gate_up_swiglu,
+ * jsx_row_linear_allreduce (down_proj)) and the final norm + LM head +
+ * argmax, with grid-wide barriers between the phases instead of kernel
+ * launches (models/glm4.py:162-195, :226-260 inside the jit step of
+ * runner.py:139-164, greedy argmax runner.py:297).  Results equal the per-op
+ * entry points'.  ids are read as the fed tokens and overwritten with the
+ * greedy tokens (head != 0); positions are advanced by one when advance != 0. */
+typedef struct {
+  const void* ln1;    /* [hidden] bf16 */
+  const void* w_qkv;  /* jsx_pack_qkv layout, (nq + 2 nkv) * head_dim rows */
+  const void* b_qkv;  /* [(nq + 2 nkv) * head_dim] or NULL */
+  const void* w_o;    /* [hidden][nq * head_dim] (jsx_pack_transpose of this rank's shard) */
+  const void* ln2;    /* [hidden] */
+  const void* w_gu;   /* jsx_pack_gate_up layout, 2 * inter rows */
+  const void* w_d;    /* [hidden][inter] */
+  void* k_cache;      /* [batch][max_seq][nkv][head_dim] */
+  void* v_cache;
+} jsx_layer_weights;
+
+typedef struct {
+  int batch, hidden, n_heads, n_kv_heads, head_dim, rotary_dim, inter;  /* per-rank head/inter counts */
+  int vocab, vocab_local, vocab_offset, max_seq, n_layers;
+  float eps, scale;
+  const jsx_layer_weights* layers; /* DEVICE array of n_layers entries */
+  const void* embed;               /* [vocab][hidden] */
+  const void* final_norm;          /* [hidden] */
+  const void* lm_head;             /* [vocab_local][hidden] */
+  const float* inv_freq;           /* [rotary_dim / 2] */
+  int32_t* ids;                    /* [batch] */
+  int32_t* positions;              /* [batch] */
+  int advance, head;
+  void* h;                         /* [batch][hidden] residual stream */
+  void* q;                         /* [batch][nq * head_dim] */
+  void* attn;                      /* [batch][nq * head_dim] */
+  void* act;                       /* [batch][inter] */
+  void* logits;                    /* [batch][vocab_local] or NULL */
+  void* workspace;                 /* jsx_decode_step_workspace_size bytes, zeroed once */
+  size_t workspace_bytes;
+  uint64_t* trace;                 /* NULL, or [2 + 5 n_layers] u64: %globaltimer (ns) after the
+                                      embedding, after each phase of each layer, and at the end */
+} jsx_decode_step_args;
+
+int jsx_decode_step_workspace_size(const jsx_decode_step_args* args, size_t* bytes);
+int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args, void* stream);
 
 /* MoE router (layers/moe.py:54-79 MoEGate.__call__): logits = bf16(x @ Wg),
  * softmax in f32, + correction bias (nullable), top-k (ties -> lower index),

@@ -160,3 +160,39 @@ def test_config0_glm4_9b_two_layers(jsx, ref, cuda):
     got, record = run_teacher_forced(jsx, ref, rc, params, prompt, steps=31, L=512)
     flips = check_steps(ref, got, record)
     print("near-tie flips (step, seq, margin, bound):", flips)
+
+
+@pytest.mark.parametrize("B", [1, 3, 8])
+def test_fused_step_matches_per_op_kernels(jsx, ref, cuda, B):
+    """The whole-step kernel (jsx_decode_step) gives exactly the per-op kernels' results:
+    the same per-row work and reduction order, only without the launches between them."""
+    rc = small_cfg(ref)
+    params = ref.init_params(rc, seed=9)
+    model = jsx.GLM4ForCausalLM(to_model_config(jsx, rc), jsx.create_mesh(1))
+    model.load_state(params)
+    prompt = np.random.default_rng(10).integers(0, rc.vocab_size, (B, 6))
+    runs = {}
+    for fused in (False, True):
+        model.fused_step = fused
+        st = jsx.DecodeState(model, B, 24, want_logits=True)
+        for s in range(6):
+            st.ids.copy_(torch.from_numpy(prompt[:, s].astype(np.int32)))
+            model.step(st, head=(s == 5))
+        seq = [(st.ids.cpu().numpy().copy(), st.logits.float().cpu().numpy(), st.h.float().cpu().numpy())]
+        for _ in range(5):
+            model.step(st, head=True)
+            seq.append((st.ids.cpu().numpy().copy(), st.logits.float().cpu().numpy(),
+                        st.h.float().cpu().numpy()))
+        runs[fused] = (seq, st.pos.cpu().numpy().copy(), [c.k.float().cpu().numpy() for c in st.caches])
+    model.fused_step = True
+    (a, pa, ka), (b, pb, kb) = runs[False], runs[True]
+    assert np.array_equal(pa, pb)
+    for (ia, la, ha), (ib, lb, hb) in zip(a, b):
+        assert np.array_equal(ia, ib)
+        assert np.array_equal(la, lb)
+        assert np.array_equal(ha, hb)
+    for x, y in zip(ka, kb):
+        assert np.array_equal(x, y)
+    status = __import__("ctypes").c_int(-1)
+    jsx._lib.call("jsx_device_error", __import__("ctypes").byref(status))
+    assert status.value == 0
