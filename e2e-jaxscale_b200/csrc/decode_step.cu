@@ -59,31 +59,43 @@ __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Grid barrier: count bar[0], generation bar[1].  Thread 0 of each CTA
-// arrives; the last arrival resets the count and publishes the next
-// generation.  `gen` lives in thread 0 only.
-__device__ __forceinline__ void grid_sync(uint32_t* bar, uint32_t& gen) {
+// Grid barrier in two halves: count bar[0], generation bar[1].  grid_arrive:
+// thread 0 of each CTA publishes the CTA's writes and arrives; the last
+// arrival resets the count and releases the next generation.  grid_wait: wait
+// for that generation.  The next phase's weight prefetch is issued between the
+// halves, so it neither delays the arrival (a fence would wait for it) nor
+// waits for the release.  `gen` lives in thread 0 only.
+__device__ __forceinline__ void grid_arrive(uint32_t* bar, uint32_t gen) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const uint32_t target = gen + 1u;
     if (atomicAdd(bar, 1u) == gridDim.x - 1) {
       bar[0] = 0u;
       __threadfence();
-      st_release_gpu(bar + 1, target);
-    } else {
-      const long long t0 = clock64();
-      uint32_t it = 0;
-      while ((int)(ld_acquire_gpu(bar + 1) - target) < 0) {
-        if ((++it & 63u) == 0 && clock64() - t0 > kBarrierLimitCycles) {
-          atomicOr(&g_step_error, 1u);
-          break;
-        }
+      st_release_gpu(bar + 1, gen + 1u);
+    }
+  }
+}
+
+__device__ __forceinline__ void grid_wait(uint32_t* bar, uint32_t& gen) {
+  if (threadIdx.x == 0) {
+    const uint32_t target = gen + 1u;
+    const long long t0 = clock64();
+    uint32_t it = 0;
+    while ((int)(ld_acquire_gpu(bar + 1) - target) < 0) {
+      if ((++it & 63u) == 0 && clock64() - t0 > kBarrierLimitCycles) {
+        atomicOr(&g_step_error, 1u);
+        break;
       }
     }
     gen = target;
   }
   __syncthreads();
+}
+
+__device__ __forceinline__ void grid_sync(uint32_t* bar, uint32_t& gen) {
+  grid_arrive(bar, gen);
+  grid_wait(bar, gen);
 }
 
 // Phase trace: CTA 0 stamps %globaltimer after every grid barrier (and at the end).
@@ -230,8 +242,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   unsigned long long best[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) best[m] = 0ull;
+  grid_arrive(bar, gen);
   prefetch(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows);
-  grid_sync(bar, gen);
+  grid_wait(bar, gen);
   trace_mark(a.trace, tn);
 
   AttnArgs at;
@@ -251,6 +264,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   at.cnt = reinterpret_cast<uint32_t*>(ws + kWsAttn + 256);
   at.part = reinterpret_cast<float*>(ws + kWsAttn + lay.counter_bytes);
   const int attn_items = M * a.n_kv_heads * lay.hg * lay.splits;
+  at.pf_slots = attn_items;
+  // bytes of gate/up weights pulled into L2 behind the o_proj weights during
+  // attention (o_proj + this prefix stay well inside the 126 MB L2)
+  const size_t gu_prefix = (size_t)64 << 20;
 
   for (int l = 0; l < a.n_layers; ++l) {
     const jsx_layer_weights L = layers[l];
@@ -276,10 +293,18 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
     at.kc = reinterpret_cast<const bf16*>(L.k_cache);
     at.vc = reinterpret_cast<const bf16*>(L.v_cache);
+    at.pf_ptr[0] = reinterpret_cast<const char*>(L.w_o);
+    at.pf_bytes[0] = (size_t)a.hidden * qdim * sizeof(bf16);
+    at.pf_ptr[1] = reinterpret_cast<const char*>(L.w_gu);
+    {
+      const size_t gu = (size_t)2 * a.inter * a.hidden * sizeof(bf16);
+      at.pf_bytes[1] = gu < gu_prefix ? gu : gu_prefix;
+    }
     for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
       attn_item<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
+    grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden);
-    grid_sync(bar, gen);
+    grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- o_proj + all-reduce + residual (layers/attention.py:159, models/glm4.py:124) ----
     {
@@ -293,8 +318,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep & 1, xs, bt, best);
       if (multi) allreduce_rows<M>(ga, c, ep, ep & 1);
     }
+    grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter);
-    grid_sync(bar, gen);
+    grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- post-attention norm + gate/up + SwiGLU (models/glm4.py:128, :46-48) ----
     {
@@ -308,8 +334,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       stage_x<M, false, true>(ga, xs);
       gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0, xs, bt, best);
     }
+    grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden);
-    grid_sync(bar, gen);
+    grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- down_proj + all-reduce + residual (models/glm4.py:49, :130) ----
     {
@@ -323,11 +350,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep & 1, xs, bt, best);
       if (multi) allreduce_rows<M>(ga, c, ep, ep & 1);
     }
+    grid_arrive(bar, gen);
     if (l + 1 < a.n_layers)
       prefetch(bt, reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows);
     else if (a.head)
       prefetch(bt, reinterpret_cast<const bf16*>(a.lm_head), a.hidden, a.vocab_local);
-    grid_sync(bar, gen);
+    grid_wait(bar, gen);
   trace_mark(a.trace, tn);
   }
 
