@@ -67,9 +67,6 @@ extern "C" int jsx_attn_decode(const void* q, const void* k_cache, const void* v
   a.out = (bf16*)out; a.pos = positions; a.B = B; a.nq = nq; a.nkv = nkv; a.hd = head_dim;
   a.max_seq = max_seq; a.splits = splits; a.scale = scale;
   a.gi = lay.gi; a.hg = lay.hg;
-  a.pf_ptr[0] = a.pf_ptr[1] = nullptr;
-  a.pf_bytes[0] = a.pf_bytes[1] = 0;
-  a.pf_slots = 0;
   a.cnt = (uint32_t*)((char*)workspace + 256);
   a.part = (float*)((char*)workspace + lay.counter_bytes);
   auto kern = k_attn_decode;

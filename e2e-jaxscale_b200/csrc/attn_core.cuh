@@ -28,35 +28,7 @@ struct AttnArgs {
   float scale;
   float* part;     // [B*nkv*hg][splits][split_stride(gi)]: acc [gi][hd], then m [gi], l [gi] (padded)
   uint32_t* cnt;   // [B*nkv*hg], zero on entry, left zero
-  // Optional L2 prefetch issued by the items once their rows are staged (the
-  // whole-step kernel: the next phases' weights, while attention is latency
-  // bound): up to two byte ranges, shared out over pf_slots items.
-  const char* pf_ptr[2];
-  size_t pf_bytes[2];
-  int pf_slots;
 };
-
-constexpr uint32_t kPrefetchPiece = 32768;
-
-__device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
-// This item's share of the prefetch ranges (pieces slot, slot + slots, ... over the
-// item's threads).
-template <int NT>
-__device__ __forceinline__ void attn_prefetch_share(const AttnArgs& a, int slot) {
-  for (int r = 0; r < 2; ++r) {
-    const size_t bytes = a.pf_bytes[r];
-    const size_t pieces = (bytes + kPrefetchPiece - 1) / kPrefetchPiece;
-    for (size_t k = (size_t)slot + (size_t)a.pf_slots * threadIdx.x; k < pieces; k += (size_t)a.pf_slots * NT) {
-      const size_t off = k * kPrefetchPiece;
-      const size_t left = bytes - off;
-      const uint32_t n = (uint32_t)(left < kPrefetchPiece ? left : kPrefetchPiece) & ~15u;
-      if (n) l2_prefetch(a.pf_ptr[r] + off, n);
-    }
-  }
-}
 
 // floats per split record: the accumulator tile, then (m, l) per head, padded so
 // every record starts on a 16-byte boundary (float4 reads in the combine)
@@ -152,7 +124,6 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
   if (n > kChunk) n = kChunk;
   float* part = a.part + ((size_t)vb * a.splits + s) * stride;
   __syncthreads();
-  if (a.pf_slots > 0) attn_prefetch_share<NT>(a, vb * a.splits + s);
 
   if (n > 0) {
     // scores: one (head, 32-row block) task per warp pass, one row per lane;

@@ -264,10 +264,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   at.cnt = reinterpret_cast<uint32_t*>(ws + kWsAttn + 256);
   at.part = reinterpret_cast<float*>(ws + kWsAttn + lay.counter_bytes);
   const int attn_items = M * a.n_kv_heads * lay.hg * lay.splits;
-  at.pf_slots = attn_items;
-  // bytes of gate/up weights pulled into L2 behind the o_proj weights during
-  // attention (o_proj + this prefix stay well inside the 126 MB L2)
-  const size_t gu_prefix = (size_t)64 << 20;
 
   for (int l = 0; l < a.n_layers; ++l) {
     const jsx_layer_weights L = layers[l];
@@ -293,13 +289,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
     at.kc = reinterpret_cast<const bf16*>(L.k_cache);
     at.vc = reinterpret_cast<const bf16*>(L.v_cache);
-    at.pf_ptr[0] = reinterpret_cast<const char*>(L.w_o);
-    at.pf_bytes[0] = (size_t)a.hidden * qdim * sizeof(bf16);
-    at.pf_ptr[1] = reinterpret_cast<const char*>(L.w_gu);
-    {
-      const size_t gu = (size_t)2 * a.inter * a.hidden * sizeof(bf16);
-      at.pf_bytes[1] = gu < gu_prefix ? gu : gu_prefix;
-    }
     for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
       attn_item<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
     grid_arrive(bar, gen);
@@ -502,7 +491,7 @@ extern "C" int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args,
                 "batch %d / hidden %d exceed the comm buffer", a.batch, a.hidden);
   }
   const size_t smem = step_smem(a);
-  JSX_REQUIRE(smem <= 200 * 1024, "step needs %zu bytes of shared memory", smem);
+  JSX_REQUIRE(smem <= kMaxDynSmem, "step needs %zu bytes of shared memory", smem);
 #define JSX_STEP_CASE(MM)                                                                    \
   case MM: {                                                                                 \
     auto kern = k_decode_step<MM>;                                                           \

@@ -672,7 +672,7 @@ static int launch_gemv(const GemvArgs& a, const CommDev& c, cudaStream_t s, int 
     }
   }
   const size_t smem = (size_t)a.M * a.K * sizeof(bf16);
-  JSX_REQUIRE(smem <= 200 * 1024, "activations of %d x %d bf16 exceed the shared-memory stage", a.M, a.K);
+  JSX_REQUIRE(smem <= kMaxDynSmem, "activations of %d x %d bf16 exceed the shared-memory stage", a.M, a.K);
   const int ngroups = a.N / kRows;
 #define JSX_GEMV_CASE(MM)                                                                   \
   case MM: {                                                                                \

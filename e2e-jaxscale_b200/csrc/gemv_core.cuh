@@ -15,6 +15,8 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kRows = 2;    // rows per warp group (the qkv / gate_up packings assume 2)
 constexpr int kUnroll = 8;  // 16-byte vectors per lane per row in flight
 constexpr int kMaxM = 8;
+// dynamic shared memory a decode kernel may request (B200: 227 KB per CTA, less the static part)
+constexpr size_t kMaxDynSmem = 225 * 1024;
 
 enum Epi { EPI_LINEAR = 0, EPI_QKV = 1, EPI_SWIGLU = 2, EPI_ROWAR = 3, EPI_LMHEAD = 4 };
 

@@ -55,8 +55,10 @@ def test_workspace_size_queries(jsx):
     n = ctypes.c_size_t(0)
     lib.call("jsx_attn_decode_workspace_size", 1, 32, 2, 128, 1152, ctypes.byref(n))
     splits = (1152 + 63) // 64           # 64 cache rows per split
-    record = 16 * 128 + 32               # accumulator tile + (m, l) per head, padded to 16 bytes
-    assert n.value >= 1 * 2 * splits * record * 4
+    # batch 1 leaves the GPU mostly idle, so each kv head's 16 query heads are split in 4 groups
+    groups, heads = 1 * 2 * 4, 4
+    record = heads * 128 + 8             # accumulator tile + (m, l) per head, padded to 16 bytes
+    assert n.value >= groups * splits * record * 4
     lib.call("jsx_lmhead_workspace_size", 8, ctypes.byref(n))
     assert n.value >= 256 + 8 * 8
     with pytest.raises(lib.JsxError):

@@ -196,3 +196,26 @@ def test_fused_step_matches_per_op_kernels(jsx, ref, cuda, B):
     status = __import__("ctypes").c_int(-1)
     jsx._lib.call("jsx_device_error", __import__("ctypes").byref(status))
     assert status.value == 0
+
+
+def test_fused_step_batch8_full_width(jsx, ref, cuda):
+    """Batch 8 at the GLM-4-9B widths (down_proj K = 13696): the activations fill
+    219 KB of shared memory, one CTA per SM; fused and per-op steps agree exactly."""
+    rc = ref.GLMConfig(num_hidden_layers=1, vocab_size=2048)
+    params = ref.init_params(rc, seed=11)
+    cfg = to_model_config(jsx, rc)
+    model = jsx.GLM4ForCausalLM(cfg, jsx.create_mesh(1))
+    model.load_state(params)
+    prompt = np.random.default_rng(12).integers(0, rc.vocab_size, (8, 3))
+    out = {}
+    for fused in (False, True):
+        model.fused_step = fused
+        st = jsx.DecodeState(model, 8, 16, want_logits=True)
+        for s in range(3):
+            st.ids.copy_(torch.from_numpy(prompt[:, s].astype(np.int32)))
+            model.step(st, head=(s == 2))
+        model.step(st, head=True)
+        out[fused] = (st.ids.cpu().numpy(), st.logits.float().cpu().numpy(), st.h.float().cpu().numpy())
+    model.fused_step = True
+    for x, y in zip(out[False], out[True]):
+        assert np.array_equal(x, y)
