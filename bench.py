@@ -348,22 +348,32 @@ def run_gpu(args) -> None:
         phase_us["note"] = ("mean us per layer (lm_head: once per step) between grid barriers, each "
                             "phase including its barrier; CTA 0 %globaltimer over 8 eager steps")
     else:
-        # dominant kernel: fused gate/up + SwiGLU GEMV, one launch per layer's weights
-        m = min(B, K.MAX_DECODE_TOKENS)
+        # dominant op: fused gate/up + SwiGLU, one call per layer's weights (every layer once:
+        # 40 x 224 MB streams past the L2 between two calls on the same weights)
         lp0 = model.layers[0]
-        K.gate_up_swiglu(st.h[:m], lp0.ln2, cfg.rms_norm_eps, lp0.w_gu, st.act[:m])  # loads the module
+        if st.tc:
+            m = min(B, K.TC_MAX_TOKENS)
+            gu = lambda lp: K.tc_gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m],
+                                                st.tc_ws)
+            kern_name = ("jsx_tc_gate_up_swiglu (rmsnorm + k_tc_gemm tcgen05/TMA split-K + "
+                         "k_tc_rows<EPI_SWIGLU>), the three launches timed together")
+            trafkey = f"tc_gate_up_swiglu_tp{args.gpus}_m{m}"
+        else:
+            m = min(B, K.MAX_DECODE_TOKENS)
+            gu = lambda lp: K.gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m])
+            kern_name = "jsx_gate_up_swiglu (k_gemv<M,EPI_SWIGLU>)"
+            trafkey = f"gate_up_swiglu_tp{args.gpus}_m{m}"
+        gu(lp0)  # loads the module
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in model.layers]
         torch.cuda.synchronize()
         for (ea, eb), lp in zip(ev, model.layers):
             ea.record(stream)
-            K.gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m])
+            gu(lp)
             eb.record(stream)
         torch.cuda.synchronize()
         kern_ms = statistics.median([ea.elapsed_time(eb) for ea, eb in ev])
         kern_bytes = lp0.w_gu.numel() * 2 + m * cfg.hidden_size * 2 + m * model.I_l * 2 + cfg.hidden_size * 2
-        kern_name = "jsx_gate_up_swiglu (k_gemv<M,EPI_SWIGLU>)"
-        trafkey = f"gate_up_swiglu_tp{args.gpus}_m{m}"
     achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
 
     launches = model.kernels_per_step(B, head=True) * args.steps

@@ -55,6 +55,12 @@ SIGNATURES = {
     "jsx_row_linear_allreduce": [P, P, P, P, I, I, I, P],
     "jsx_lmhead_workspace_size": [I, P],
     "jsx_lmhead_argmax": [P, P, P, F, P, I, I, I, I, P, P, P, SZ, P],
+    "jsx_tc_workspace_size": [I, I, I, P],
+    "jsx_tc_linear": [P, P, F, P, P, P, I, I, I, P, SZ, P],
+    "jsx_tc_qkv_rope_cache": [P, P, F, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P, SZ, P],
+    "jsx_tc_gate_up_swiglu": [P, P, F, P, P, I, I, I, P, SZ, P],
+    "jsx_tc_row_linear_allreduce": [P, P, P, P, I, I, I, P, SZ, P],
+    "jsx_tc_lmhead_argmax": [P, P, P, F, P, I, I, I, I, P, P, P, SZ, P],
     "jsx_moe_gate": [P, P, P, P, P, I, I, I, I, F, I, P],
     "jsx_decode_step_workspace_size": [P, P],
     "jsx_decode_step": [P, P, P],

@@ -240,4 +240,47 @@ __device__ __forceinline__ void epi_swiglu(const GemvArgs& a, int g, const float
   swiglu_store(a, g, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
 }
 
+// Epilogue of one row pair (packed rows 2g, 2g+1) for token m; returns the
+// argmax key of the pair (LM head) or 0.
+template <int EPI>
+__device__ __forceinline__ unsigned long long epi_pair(const GemvArgs& a, const CommDev& c, bool multi,
+                                                       int par, int g, int m, float v0, float v1) {
+  const int r0 = 2 * g;
+  if constexpr (EPI == EPI_LINEAR) {
+    float y0 = rbf(v0), y1 = rbf(v1);
+    if (a.bias) {
+      y0 = rbf(y0 + ldbf(a.bias + r0));
+      y1 = rbf(y1 + ldbf(a.bias + r0 + 1));
+    }
+    a.y[(size_t)m * a.N + r0] = __float2bfloat16_rn(y0);
+    a.y[(size_t)m * a.N + r0 + 1] = __float2bfloat16_rn(y1);
+  } else if constexpr (EPI == EPI_QKV) {
+    qkv_store(a, g, m, v0, v1);
+  } else if constexpr (EPI == EPI_SWIGLU) {
+    swiglu_store(a, g, m, v0, v1);
+  } else if constexpr (EPI == EPI_ROWAR) {
+    if (!multi) {
+      bf16* hp = a.h + (size_t)m * a.N + r0;
+      hp[0] = __float2bfloat16_rn(__bfloat162float(hp[0]) + rbf(v0));
+      hp[1] = __float2bfloat16_rn(__bfloat162float(hp[1]) + rbf(v1));
+    } else {
+      for (int d = 0; d < c.world; ++d) {
+        float* dst = data_ptr(c, d, par, c.rank, m) + r0;
+        dst[0] = v0;
+        dst[1] = v1;
+      }
+    }
+  } else if constexpr (EPI == EPI_LMHEAD) {
+    const float l0 = rbf(v0), l1 = rbf(v1);
+    if (a.y) {
+      a.y[(size_t)m * a.N + r0] = __float2bfloat16_rn(l0);
+      a.y[(size_t)m * a.N + r0 + 1] = __float2bfloat16_rn(l1);
+    }
+    const unsigned long long k0 = argmax_key(l0, (uint32_t)(a.vocab_offset + r0));
+    const unsigned long long k1 = argmax_key(l1, (uint32_t)(a.vocab_offset + r0 + 1));
+    return k0 > k1 ? k0 : k1;
+  }
+  return 0ull;
+}
+
 }  // namespace jsx

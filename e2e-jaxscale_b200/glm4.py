@@ -32,6 +32,7 @@ from .layers.rotary import RotaryEmbedding
 from .weights import PackedLayer, RandomLayerSource, pack_layer
 
 CHUNK = K.MAX_DECODE_TOKENS
+TC_CHUNK = K.TC_MAX_TOKENS
 
 
 class DecodeState:
@@ -57,6 +58,14 @@ class DecodeState:
         self.step_args = None
         if batch <= CHUNK and model.layers:
             self._build_step_args(model)
+        # batches above the GEMV width run the projections on the tensor cores
+        self.tc = batch > CHUNK
+        self.tc_ws = None
+        if self.tc and model.layers:
+            lp, H = model.layers[0], c.hidden_size
+            shapes = [tuple(reversed(lp.w_qkv.shape)), tuple(reversed(lp.w_o.shape)),
+                      tuple(reversed(lp.w_gu.shape)), tuple(reversed(lp.w_d.shape)), (H, model.V_l)]
+            self.tc_ws = K.tc_workspace(min(batch, TC_CHUNK), shapes, dev)
 
     def _build_step_args(self, model: "GLM4ForCausalLM") -> None:
         """Arguments of the whole-step kernel (jsx_decode_step) over these buffers."""
@@ -107,7 +116,7 @@ class GLM4ForCausalLM:
         self.embed = None     # [V, H] replicated
         self.norm = None      # [H]
         self.lm_head = None   # [V_l, H]
-        self.comm = mesh.comm(CHUNK, c.hidden_size) if t > 1 else None
+        self.comm = mesh.comm(TC_CHUNK, c.hidden_size) if t > 1 else None
         self.fused_step = os.environ.get("JSX_FUSED_STEP", "1") != "0"
 
     # ---- weights ----
@@ -151,6 +160,9 @@ class GLM4ForCausalLM:
         c = self.config
         B, eps, hd, rot = st.batch, c.rms_norm_eps, c.head_dim, self.rotary.rotary_dim
         K.embed(st.ids, self.embed, out=st.h)
+        if st.tc:
+            self._run_body_tc(st)
+            return
         for lp, cache in zip(self.layers, st.caches):
             for b0 in range(0, B, CHUNK):
                 b1 = min(B, b0 + CHUNK)
@@ -168,8 +180,33 @@ class GLM4ForCausalLM:
                 b1 = min(B, b0 + CHUNK)
                 K.row_linear_allreduce(self.comm, st.act[b0:b1], lp.w_d, st.h[b0:b1])
 
+    def _run_body_tc(self, st: DecodeState) -> None:
+        """Decoder layers with the projections on the tensor cores (jsx_tc_*), up to 32 tokens a call."""
+        c = self.config
+        B, eps, hd, rot, ws = st.batch, c.rms_norm_eps, c.head_dim, self.rotary.rotary_dim, st.tc_ws
+        spans = [(b0, min(B, b0 + TC_CHUNK)) for b0 in range(0, B, TC_CHUNK)]
+        for lp, cache in zip(self.layers, st.caches):
+            for b0, b1 in spans:
+                K.tc_qkv_rope_cache(st.h[b0:b1], lp.ln1, eps, lp.w_qkv, lp.b_qkv, self.inv_freq,
+                                    st.pos[b0:b1], st.q[b0:b1], cache.k[b0:b1], cache.v[b0:b1],
+                                    self.nq_l, self.nkv_l, hd, rot, ws)
+            K.attn_decode(st.q, cache.k, cache.v, st.attn, st.pos, self.scale, st.attn_ws)
+            for b0, b1 in spans:
+                K.tc_row_linear_allreduce(self.comm, st.attn[b0:b1], lp.w_o, st.h[b0:b1], ws)
+            for b0, b1 in spans:
+                K.tc_gate_up_swiglu(st.h[b0:b1], lp.ln2, eps, lp.w_gu, st.act[b0:b1], ws)
+            for b0, b1 in spans:
+                K.tc_row_linear_allreduce(self.comm, st.act[b0:b1], lp.w_d, st.h[b0:b1], ws)
+
     def run_head(self, st: DecodeState) -> None:
         """Final norm + LM head + greedy argmax; the token ids overwrite st.ids."""
+        if st.tc:
+            for b0 in range(0, st.batch, TC_CHUNK):
+                b1 = min(st.batch, b0 + TC_CHUNK)
+                K.tc_lmhead_argmax(self.comm, st.h[b0:b1], self.norm, self.config.rms_norm_eps, self.lm_head,
+                                   self.vocab_offset, st.ids[b0:b1], st.tc_ws,
+                                   None if st.logits is None else st.logits[b0:b1])
+            return
         for b0 in range(0, st.batch, CHUNK):
             b1 = min(st.batch, b0 + CHUNK)
             K.lmhead_argmax(self.comm, st.h[b0:b1], self.norm, self.config.rms_norm_eps, self.lm_head,
@@ -192,6 +229,11 @@ class GLM4ForCausalLM:
     def kernels_per_step(self, batch: int, head: bool = True) -> int:
         if self.fused_step and batch <= CHUNK:
             return 1
+        if batch > CHUNK:
+            # per layer: rmsnorm + GEMM + epilogue (qkv, gate_up), GEMM + epilogue (o, down), attention
+            ch = math.ceil(batch / TC_CHUNK)
+            n = 1 + self.config.num_hidden_layers * (1 + 10 * ch)
+            return n + (3 * ch if head else 0)
         ch = math.ceil(batch / CHUNK)
         n = 1 + self.config.num_hidden_layers * (1 + 4 * ch)
         return n + (ch if head else 0)

@@ -53,9 +53,10 @@ int jsx_device_sm_count(int* out);
 #define JSX_LAUNCH_PDL 1
 int jsx_set_launch_flags(int flags);
 int jsx_get_launch_flags(void);
-/* Reads and clears the device error words of the streaming GEMV and of the
- * whole-step kernel: a bounded pipeline or grid-barrier wait that gave up (the
- * kernel then finished without its result) reports JSX_ETIMEDOUT.
+/* Reads and clears the device error words of the streaming GEMV, of the
+ * whole-step kernel and of the tensor-core projections: a bounded pipeline or
+ * grid-barrier wait that gave up (the kernel then finished without its
+ * result) reports JSX_ETIMEDOUT.
  * Synchronous (a device copy). */
 int jsx_device_error(int* status);
 
@@ -156,6 +157,41 @@ int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, flo
                       const void* w_vocab, int vocab_local, int vocab_offset, int M, int hidden,
                       void* logits_out, int32_t* ids_out, void* workspace,
                       size_t workspace_bytes, void* stream);
+
+/* ---- tensor-core projections for 9..32 tokens -------------------------------
+ * The same five projections as above (same argument meaning, same packed
+ * weights, same epilogues and error behaviour) computed on the tcgen05 tensor
+ * cores: weight tiles of 128 rows x 64 K are the MMA's A operand, the M <= 32
+ * token rows its B operand, both loaded by TMA, fp32 accumulation in TMEM,
+ * K split across CTAs and the split partials summed in split order by a
+ * second kernel that runs the epilogue.  They replace the same reference
+ * call sites as the GEMV entry points (layers/linear.py:57-82 and :116-145,
+ * models/glm4.py:118-120, :47-49, :193, layers/embedding.py:79-92) for
+ * batches where one weight element feeds 2*M >= 18 flops.  Sums are fp32
+ * like the GEMV path but in a different order, so results agree with it to
+ * fp32 rounding, not bitwise.
+ * workspace: jsx_tc_workspace_size(M, K, N) bytes, 16-byte aligned; for
+ * jsx_tc_lmhead_argmax its first 512 bytes must be zero on the first call
+ * (they are left zero). */
+int jsx_tc_workspace_size(int M, int K, int N, size_t* bytes);
+int jsx_tc_linear(const void* x, const void* gamma, float eps, const void* w_nk, const void* bias,
+                  void* y, int M, int K, int N, void* workspace, size_t workspace_bytes,
+                  void* stream);
+int jsx_tc_qkv_rope_cache(const void* h, const void* ln_gamma, float eps, const void* w_qkv,
+                          const void* b_qkv, const float* inv_freq, const int32_t* positions,
+                          void* q_out, void* k_cache, void* v_cache, int M, int tokens_per_seq,
+                          int K, int nq, int nkv, int head_dim, int rotary_dim, int max_seq,
+                          void* workspace, size_t workspace_bytes, void* stream);
+int jsx_tc_gate_up_swiglu(const void* h, const void* ln_gamma, float eps, const void* w_gu,
+                          void* act, int M, int K, int I, void* workspace,
+                          size_t workspace_bytes, void* stream);
+int jsx_tc_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h, int M,
+                                int K_local, int N, void* workspace, size_t workspace_bytes,
+                                void* stream);
+int jsx_tc_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, float eps,
+                         const void* w_vocab, int vocab_local, int vocab_offset, int M,
+                         int hidden, void* logits_out, int32_t* ids_out, void* workspace,
+                         size_t workspace_bytes, void* stream);
 
 /* ---- whole decode step ------------------------------------------------------
  * One cooperative kernel runs a full GLM-4 decode step for batch <= 8 on this

@@ -41,6 +41,8 @@ def test_abi_version(jsx):
     ("jsx_comm_create", (2, 2, 8, 4096, 0, None)),
     ("jsx_moe_gate", (None, None, None, None, None, 1, 8, 512, 4, 1.0, 1, None)),
     ("jsx_set_launch_flags", (0x10,)),
+    ("jsx_tc_linear", (None, None, 0.0, None, None, None, 16, 64, 8, None, 0, None)),
+    ("jsx_tc_workspace_size", (33, 4096, 4096, None)),
 ])
 def test_invalid_arguments_are_rejected_on_the_host(jsx, call, args):
     lib = jsx._lib
@@ -63,3 +65,19 @@ def test_workspace_size_queries(jsx):
     assert n.value >= 256 + 8 * 8
     with pytest.raises(lib.JsxError):
         lib.call("jsx_lmhead_workspace_size", 9, ctypes.byref(n))
+
+
+def test_tc_workspace_size(jsx):
+    """Split partials [splits][M][N] fp32 after a 1 KB header and the normalised
+    activations; the plan depends on the shape only (about 592 CTAs, >= 4 K blocks a split)."""
+    lib = jsx._lib
+    n = ctypes.c_size_t(0)
+    lib.call("jsx_tc_workspace_size", 32, 4096, 4608, ctypes.byref(n))
+    tiles, kblocks = 36, 64
+    splits = min(-(-592 // tiles), kblocks // 4)
+    assert splits == 16
+    assert n.value == 1024 + 32 * 4096 * 2 + splits * 32 * 4608 * 4
+    lib.call("jsx_tc_workspace_size", 9, 13696, 4096, ctypes.byref(n))
+    assert n.value == 1024 + 32 * 13696 * 2 + 19 * 9 * 4096 * 4
+    with pytest.raises(lib.JsxError):
+        lib.call("jsx_tc_workspace_size", 0, 64, 64, ctypes.byref(n))
