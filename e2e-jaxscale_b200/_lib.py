@@ -56,6 +56,7 @@ SIGNATURES = {
     "jsx_lmhead_workspace_size": [I, P],
     "jsx_lmhead_argmax": [P, P, P, F, P, I, I, I, I, P, P, P, SZ, P],
     "jsx_tc_workspace_size": [I, I, I, P],
+    "jsx_tc_set_trace": [P],
     "jsx_tc_linear": [P, P, F, P, P, P, I, I, I, P, SZ, P],
     "jsx_tc_qkv_rope_cache": [P, P, F, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P, SZ, P],
     "jsx_tc_gate_up_swiglu": [P, P, F, P, P, I, I, I, P, SZ, P],

@@ -94,6 +94,60 @@ __global__ void k_rmsnorm(const bf16* __restrict__ x, const bf16* __restrict__ g
     yr[i] = __float2bfloat16_rn((__bfloat162float(xr[i]) * r) * __bfloat162float(g[i]));
 }
 
+// Vectorised form for hidden % 8 == 0 and 16-byte aligned rows: one CTA of 128
+// threads per row, the row held in registers (up to kNormVec 16-byte vectors
+// per thread, hidden <= 128 * 8 * kNormVec), so x and gamma cross the memory
+// system once.  Same per-element formula as k_rmsnorm.
+constexpr int kNormThreads = 128;
+constexpr int kNormVec = 8;
+__global__ void __launch_bounds__(kNormThreads) k_rmsnorm_vec(const bf16* __restrict__ x,
+                                                              const bf16* __restrict__ g,
+                                                              bf16* __restrict__ y, int hidden, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const int nvec = hidden >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)blockIdx.x * hidden);
+  const uint4* gv = reinterpret_cast<const uint4*>(g);
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)blockIdx.x * hidden);
+  pdl_wait();
+  uint4 xv[kNormVec], gw[kNormVec];
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int v = threadIdx.x + j * kNormThreads;
+    xv[j] = v < nvec ? xr[v] : make_uint4(0, 0, 0, 0);
+    gw[j] = v < nvec ? gv[v] : make_uint4(0, 0, 0, 0);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    float f[8];
+    unpack8(xv[j], f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss = fmaf(f[e], f[e], ss);
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kNormThreads / 32; ++w) t += red[w];
+  const float r = 1.0f / sqrtf(t / (float)hidden + eps);
+#pragma unroll
+  for (int j = 0; j < kNormVec; ++j) {
+    const int v = threadIdx.x + j * kNormThreads;
+    if (v < nvec) {
+      float f[8], q[8];
+      unpack8(xv[j], f);
+      unpack8(gw[j], q);
+      uint4 o;
+      o.x = pack2((f[0] * r) * q[0], (f[1] * r) * q[1]);
+      o.y = pack2((f[2] * r) * q[2], (f[3] * r) * q[3]);
+      o.z = pack2((f[4] * r) * q[4], (f[5] * r) * q[5]);
+      o.w = pack2((f[6] * r) * q[6], (f[7] * r) * q[7]);
+      yr[v] = o;
+    }
+  }
+}
+
 // ---- embedding (layers/embedding.py:35-51) -----------------------------------------
 // jnp.take's default out-of-bounds mode fills with NaN; the same happens here
 // (no out-of-range read).
@@ -216,6 +270,12 @@ extern "C" int jsx_pack_gate_up(const void* w_gate, const void* w_up, void* w_gu
 extern "C" int jsx_rmsnorm(const void* x, const void* gamma, void* y, int rows, int hidden, float eps,
                            void* stream) {
   JSX_REQUIRE(x && gamma && y && rows >= 1 && hidden >= 1, "bad rmsnorm arguments");
+  if (hidden % 8 == 0 && hidden <= kNormThreads * 8 * kNormVec && aligned16(x) && aligned16(gamma) &&
+      aligned16(y)) {
+    JSX_CUDA(launch_kernel(k_rmsnorm_vec, dim3(rows), dim3(kNormThreads), 0, (cudaStream_t)stream,
+                           (const bf16*)x, (const bf16*)gamma, (bf16*)y, hidden, eps));
+    return JSX_OK;
+  }
   JSX_CUDA(launch_kernel(k_rmsnorm, dim3(rows), dim3(256), 0, (cudaStream_t)stream,
                          (const bf16*)x, (const bf16*)gamma, (bf16*)y, hidden, eps));
   return JSX_OK;

@@ -7,21 +7,36 @@
 // the B operand (N = 32, zero-filled by TMA beyond the real token count), both
 // K-major bf16 with the 128-byte swizzle, fp32 accumulation in TMEM.
 //
-//   k_tc_gemm       one CTA per (128-row tile, K split): warp 0 / lane 0 loads
-//                   the A (16 KB) and B (4 KB) boxes of each 64-wide K block
-//                   with cp.async.bulk.tensor into a 4-stage ring; warp 1 /
-//                   lane 0 issues 4 tcgen05.mma (K = 16 each) per stage and
-//                   hands the stage back with tcgen05.commit; the 4 warps then
-//                   read their 32 TMEM lanes (tcgen05.ld 32x32b.x32 = one weight
-//                   row x 32 tokens per thread) and store fp32 split partials.
-//   k_tc_rows       sums the split partials of each row pair in split order and
-//                   runs the same pair epilogues as the GEMV kernels (bias,
-//                   RoPE + KV write, SwiGLU, residual + tensor-parallel
-//                   all-reduce, LM-head argmax).
+// Work split.  A tile of 128 weight rows is computed by one thread-block
+// cluster of S CTAs (S = 1..8); CTA r of the cluster takes the r-th slice of
+// K.  Clusters are persistent: cluster c handles tiles c, c + #clusters, ...
+// Inside a CTA the warps specialise:
+//   warp 0 / lane 0   TMA producer: the A (16 KB) and B (4 KB) boxes of each
+//                     64-wide K block into an 8-stage ring, running ahead
+//                     across tiles;
+//   warp 1 / lane 0   MMA issuer: 4 tcgen05.mma (K = 16) per stage into one of
+//                     two TMEM accumulators (double buffer, 2 x 32 columns);
+//                     tcgen05.commit hands stages and accumulators back;
+//   warps 2..5        epilogue: tcgen05.ld 32x32b.x32 (thread = one weight row
+//                     x 32 tokens) into a shared-memory exchange buffer; the
+//                     S partial tiles of the cluster are then read through
+//                     distributed shared memory and summed in rank order by
+//                     the CTA that owns the rows (CTA r finishes row pairs
+//                     [64 r / S, 64 (r+1) / S) of the tile), which runs the
+//                     row-pair epilogue of the GEMV kernels (bias, RoPE + KV
+//                     write, SwiGLU, residual add, LM-head argmax).
+// The exchange buffers are double-buffered and handed over with mbarriers in
+// the peers' shared memory (arrive.release.cluster / try_wait.acquire.cluster),
+// so the epilogue of tile i overlaps the main loop of tile i + 1.
+//
+// Across tensor-parallel ranks the row-parallel projection writes its summed
+// rank-local fp32 rows to the workspace and k_tc_rows_allreduce pushes them to
+// every peer (P2P stores), waits for the peers' flags and adds the residual.
 //
 // No multicast anywhere.  Every mbarrier wait is time-bounded; on a timeout the
-// kernel sets its error word (jsx_device_error), drains its own copies and MMAs
-// (bounded) and frees its TMEM before returning.
+// kernel sets its error word (jsx_device_error), the other roles of the CTA
+// stop at their next wait, copies and MMAs in flight are drained (bounded) and
+// TMEM is freed before the CTA exits.
 #include <cuda.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -38,14 +53,25 @@ namespace jsx {
 constexpr int kTcBM = 128;  // weight rows per tile (MMA M)
 constexpr int kTcBN = 32;   // tokens per tile (MMA N)
 constexpr int kTcBK = 64;   // K per stage: one 128-byte swizzle row of bf16
-constexpr int kTcStages = 4;
-constexpr int kTcThreads = 128;
+constexpr int kTcStages = 8;
+constexpr int kTcThreads = 192;
 constexpr int kTcMaxM = 32;
+constexpr int kTcMaxCluster = 8;
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;
 constexpr uint32_t kTcBBytes = kTcBN * kTcBK * 2;
 constexpr uint32_t kTcStageBytes = kTcABytes + kTcBBytes;
-constexpr size_t kTcSmem = (size_t)kTcStages * kTcStageBytes + 1024 /* align */ + 256 /* barriers */;
+constexpr uint32_t kTcRingBytes = kTcStages * kTcStageBytes;
+constexpr uint32_t kTcXBytes = kTcMaxM * kTcBM * 4;  // one exchange buffer: [32 tokens][128 rows] fp32
+constexpr uint32_t kTcTmemCols = 64;                  // two 32-column fp32 accumulators
+constexpr size_t kTcSmem = (size_t)kTcRingBytes + 2 * kTcXBytes + 1024 /* align */ + 1024 /* barriers */;
 constexpr long long kTcWaitCycles = 4000000000ll;  // ~2 s at the 1965 MHz max clock
+
+// workspace layout (bytes): kernel-done counter and argmax keys (zero between
+// calls), normalised activations [32][K] bf16, rank-local rows [M][N] fp32
+// (row-parallel projection across ranks)
+constexpr size_t kTcOffDone = 0;
+constexpr size_t kTcOffKeys = 256;
+constexpr size_t kTcOffXn = 1024;
 
 static __device__ uint32_t g_tc_error;
 
@@ -61,9 +87,19 @@ int read_clear_tc_error(uint32_t* out) {
 }
 
 struct TcArgs {
-  float* part;  // [splits][M][N]
-  int M, N, K, kblocks, splits, tiles;
+  float* part;     // [M][N] fp32 rank-local rows (store_only)
+  uint32_t* done;  // CTAs finished (LM head)
+  int M, N, K, kblocks, S, tiles;
+  int store_only;  // write the summed rows only (k_tc_rows_allreduce finishes)
+  uint64_t* trace; // null, or [grid][8] %globaltimer stamps (jsx_tc_set_trace)
 };
+
+// Per-CTA timeline: 0 entry, 1 producer issued its first ring of loads,
+// 2 producer done, 3 MMA saw its first full stage, 4 MMA issued its last
+// commit, 5 epilogue received its first accumulator, 6 epilogue done, 7 exit.
+__device__ __forceinline__ void tc_stamp(const TcArgs& t, int k) {
+  if (t.trace) t.trace[(size_t)blockIdx.x * 8 + k] = globaltimer();
+}
 
 __device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -73,26 +109,82 @@ __device__ __forceinline__ void tc_mbar_init(uint64_t* b, uint32_t n) {
 __device__ __forceinline__ void tc_expect_tx(uint64_t* b, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(b)), "r"(bytes) : "memory");
 }
+__device__ __forceinline__ void tc_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_u32(b)) : "memory");
+}
+template <bool kCluster>
 __device__ __forceinline__ bool tc_try_wait(uint64_t* b, uint32_t parity) {
   uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(s_u32(b)), "r"(parity)
-      : "memory");
+  if constexpr (kCluster) {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(s_u32(b)), "r"(parity)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(s_u32(b)), "r"(parity)
+        : "memory");
+  }
   return ok != 0;
 }
-// Bounded wait; false (and the error word set) on timeout.
-__device__ __forceinline__ bool tc_wait(uint64_t* b, uint32_t parity) {
-  if (tc_try_wait(b, parity)) return true;
+// Bounded wait.  false when the CTA's abort flag is up (another role gave up)
+// or after ~2 s (then the error word and the abort flag are set).  abort may
+// be null: drains that must finish regardless (still time-bounded).
+// kCluster: acquire at cluster scope (barriers that peers arrive on).
+template <bool kCluster = false>
+__device__ __forceinline__ bool tc_wait(uint64_t* b, uint32_t parity, volatile uint32_t* abort) {
+  if (tc_try_wait<kCluster>(b, parity)) return true;
   const long long t0 = clock64();
   for (uint32_t it = 1;; ++it) {
-    if (tc_try_wait(b, parity)) return true;
-    if ((it & 63u) == 0 && clock64() - t0 > kTcWaitCycles) {
-      atomicOr(&g_tc_error, 1u);
-      return false;
+    if (tc_try_wait<kCluster>(b, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (abort && *abort) return false;
+      if (clock64() - t0 > kTcWaitCycles) {
+        atomicOr(&g_tc_error, 1u);
+        if (abort) *abort = 1u;
+        return false;
+      }
     }
   }
+}
+
+// ---- cluster primitives ------------------------------------------------------
+__device__ __forceinline__ uint32_t cl_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cl_id() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cl_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// this CTA's shared address -> the same offset in cluster CTA `rank`
+__device__ __forceinline__ uint32_t cl_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cl_arrive_remote(uint32_t caddr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
+}
+__device__ __forceinline__ float2 cl_ld2(uint32_t caddr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(caddr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void cl_fence() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ void cl_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -102,11 +194,15 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
 
 // Shared-memory matrix descriptor of a K-major, 128-byte-swizzled operand tile
 // (8-row swizzle atoms of 1024 bytes stacked along the M/N dimension):
 // start address, leading byte offset 16 B (unused with this swizzle), stride
 // byte offset 1024 B, descriptor version 1, layout type 2 (128-byte swizzle).
+// Advancing K by 16 elements inside the 128-byte row adds 32 bytes to the start.
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   uint64_t d = 0;
   d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
@@ -136,6 +232,24 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
+// Barriers over the 4 epilogue warps (named barrier 1, 128 threads; the warps
+// are converged first).  epi_all also ANDs a predicate across them, so a wait
+// that gave up in one thread makes every epilogue thread leave together.
+__device__ __forceinline__ void epi_sync() {
+  __syncwarp();
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+__device__ __forceinline__ bool epi_all(bool ok) {
+  __syncwarp();
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
   asm volatile(
@@ -151,193 +265,268 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-__global__ void __launch_bounds__(kTcThreads, 2) k_tc_gemm(const __grid_constant__ CUtensorMap tw,
-                                                           const __grid_constant__ CUtensorMap tx, TcArgs a) {
+template <int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ CUtensorMap tw,
+                                                           const __grid_constant__ CUtensorMap tx, const TcArgs t,
+                                                           const GemvArgs a, const CommDev c) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcStages * kTcStageBytes);
+  float* xbuf = reinterpret_cast<float*>(smem + kTcRingBytes);  // [2][32][128]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTcRingBytes + 2 * kTcXBytes);
   uint64_t* empty = full + kTcStages;
-  uint64_t* accf = empty + kTcStages;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* accf = empty + kTcStages;  // [2] accumulator ready (MMA -> epilogue)
+  uint64_t* acce = accf + 2;           // [2] accumulator drained (epilogue -> MMA)
+  uint64_t* xfull = acce + 2;          // [2] every cluster CTA has written its exchange buffer
+  uint64_t* xempty = xfull + 2;        // [2] every cluster CTA has read this CTA's exchange buffer
+  uint64_t* fin = xempty + 2;          // all MMAs of the CTA complete
+  unsigned long long* best = reinterpret_cast<unsigned long long*>(fin + 1);  // [32] LM-head keys
+  uint32_t* misc = reinterpret_cast<uint32_t*>(best + kTcMaxM);               // tmem base, abort
+  volatile uint32_t* abort_flag = misc + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tile = blockIdx.x % a.tiles, split = blockIdx.x / a.tiles;
-  const int kb0 = (int)((long long)split * a.kblocks / a.splits);
-  const int kb1 = (int)((long long)(split + 1) * a.kblocks / a.splits);
-  const int nkb = kb1 - kb0;
-  const int n0 = tile * kTcBM;
+  const int S = t.S;
+  const uint32_t rank = cl_rank(), cid = cl_id(), ncl = cl_count();
+  const int kb0 = (int)((long long)rank * t.kblocks / S);
+  const int kb1 = (int)((long long)(rank + 1) * t.kblocks / S);
+  if (threadIdx.x == 0) tc_stamp(t, 0);
 
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(tmem_slot)),
-                 "r"(32)
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(s_u32(misc)),
+                 "r"(kTcTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (threadIdx.x == 32) {
+  if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       tc_mbar_init(full + s, 1);
       tc_mbar_init(empty + s, 1);
     }
-    tc_mbar_init(accf, 1);
+    for (int b = 0; b < 2; ++b) {
+      tc_mbar_init(accf + b, 1);
+      tc_mbar_init(acce + b, 4);
+      tc_mbar_init(xfull + b, (uint32_t)S);
+      tc_mbar_init(xempty + b, (uint32_t)S);
+    }
+    tc_mbar_init(fin, 1);
+    misc[1] = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  if (threadIdx.x < kTcMaxM) best[threadIdx.x] = 0ull;
   tc_fence_before();
   __syncthreads();
+  cl_sync_all();  // peers' barriers are initialised before any remote arrive
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
+  const uint32_t tmem = misc[0];
 
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer ----
-    int i = 0;
-    for (; i < nkb; ++i) {
-      const int s = i % kTcStages;
-      if (i >= kTcStages && !tc_wait(empty + s, ((i / kTcStages) - 1) & 1)) break;
-      unsigned char* st = smem + (size_t)s * kTcStageBytes;
-      tc_expect_tx(full + s, kTcStageBytes);
-      tma_load_2d(st, &tw, (kb0 + i) * kTcBK, n0, full + s);
-      tma_load_2d(st + kTcABytes, &tx, (kb0 + i) * kTcBK, 0, full + s);
-    }
-    // drain: the last loads issued must land before the CTA can exit
-    const int first = i > kTcStages ? i - kTcStages : 0;
-    for (int j = first; j < i; ++j) tc_wait(full + j % kTcStages, (j / kTcStages) & 1);
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer ----
-    for (int i = 0; i < nkb; ++i) {
-      const int s = i % kTcStages;
-      if (!tc_wait(full + s, (i / kTcStages) & 1)) break;
-      tc_fence_after();
-      const uint32_t sa = s_u32(smem + (size_t)s * kTcStageBytes);
-      const uint32_t sb = sa + kTcABytes;
-#pragma unroll
-      for (int kk = 0; kk < kTcBK / 16; ++kk)
-        tc_mma(tmem, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32), (i | kk) != 0 ? 1u : 0u);
-      tc_commit(empty + s);
-    }
-    tc_commit(accf);  // fires when every MMA issued above has completed
-  }
-  __syncwarp();
-
-  // ---- epilogue: thread = one weight row, 32 token columns ----
-  const bool ok = tc_wait(accf, 0);
-  tc_fence_after();
-  float v[32];
-  tc_ld32(tmem + ((uint32_t)(warp * 32) << 16), v);
-  const int row = n0 + warp * 32 + lane;
-  if (ok && row < a.N) {
-    float* dst = a.part + (size_t)split * a.M * a.N + row;
-#pragma unroll
-    for (int t = 0; t < 32; ++t)
-      if (t < a.M) dst[(size_t)t * a.N] = v[t];
-  }
-  tc_fence_before();
-  __syncthreads();
   if (warp == 0) {
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(32) : "memory");
-  }
-}
-
-// ---- row-pair epilogue over the split partials ----------------------------
-struct TcRowArgs {
-  GemvArgs ga;        // epilogue fields (bias, q/k/v/cache/rope, h, act, logits, keys ...)
-  const float* part;  // [splits][M][N]
-  int splits;
-};
-
-template <int EPI>
-__global__ void __launch_bounds__(256) k_tc_rows(TcRowArgs r, CommDev c) {
-  const GemvArgs& a = r.ga;
-  __shared__ unsigned long long best_s[kTcMaxM];
-  __shared__ bool is_last;
-  const int M = a.M, NB = a.N >> 1;
-  const int p0 = (int)((long long)blockIdx.x * NB / gridDim.x);
-  const int p1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
-  const bool multi = (EPI == EPI_ROWAR || EPI == EPI_LMHEAD) && c.world > 1;
-  uint32_t epoch = 0;
-  int par = 0;
-  if (EPI == EPI_ROWAR && multi) {
-    epoch = read_epoch(c);
-    par = epoch & 1;
-  }
-  if (EPI == EPI_LMHEAD && threadIdx.x < kTcMaxM) best_s[threadIdx.x] = 0ull;
-  __syncthreads();
-  const size_t plane = (size_t)M * a.N;
-  for (int e = threadIdx.x; e < (p1 - p0) * M; e += blockDim.x) {
-    const int m = e / (p1 - p0), g = p0 + (e - m * (p1 - p0));
-    const float* src = r.part + (size_t)m * a.N + 2 * g;
-    float v0 = 0.f, v1 = 0.f;
-    for (int s = 0; s < r.splits; ++s) {
-      const float2 t = *reinterpret_cast<const float2*>(src + s * plane);
-      v0 += t.x;
-      v1 += t.y;
-    }
-    const unsigned long long k = epi_pair<EPI>(a, c, multi, par, g, m, v0, v1);
-    if (EPI == EPI_LMHEAD) atomicMax(best_s + m, k);
-  }
-
-  if constexpr (EPI == EPI_ROWAR) {
-    if (multi) {
-      __threadfence_system();
-      __syncthreads();
-      if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
-      if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
-      __syncthreads();
-      const int rows = 2 * (p1 - p0);
-      for (int e = threadIdx.x; e < rows * M; e += blockDim.x) {
-        const int m = e / rows, row = 2 * p0 + (e - (e / rows) * rows);
-        float sum = 0.f;
-        for (int src = 0; src < c.world; ++src) sum += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
-        bf16* hp = a.h + (size_t)m * a.N + row;
-        *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(sum));
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        if (atomicAdd(c.state + kDone, 1u) == gridDim.x - 1) {
-          c.state[kDone] = 0u;
-          __threadfence();
-          c.state[kCalls] = epoch;
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      tma_prefetch_map(&tw);
+      tma_prefetch_map(&tx);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = cid; tile < t.tiles && ok; tile += ncl) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % kTcStages;
+          if (it >= (uint32_t)kTcStages && !tc_wait(empty + s, ((it / kTcStages) - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = smem + (size_t)s * kTcStageBytes;
+          tc_expect_tx(full + s, kTcStageBytes);
+          tma_load_2d(st, &tw, kb * kTcBK, tile * kTcBM, full + s);
+          tma_load_2d(st + kTcABytes, &tx, kb * kTcBK, 0, full + s);
+          if (it + 1 == (uint32_t)kTcStages) tc_stamp(t, 1);
         }
       }
+      tc_stamp(t, 2);
+      // every copy issued must land before the CTA exits
+      const uint32_t first = it > (uint32_t)kTcStages ? it - kTcStages : 0u;
+      for (uint32_t j = first; j < it; ++j) tc_wait(full + j % kTcStages, (j / kTcStages) & 1, nullptr);
     }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t it = 0, ai = 0;
+      bool ok = true;
+      for (int tile = cid; tile < t.tiles && ok; tile += ncl, ++ai) {
+        const uint32_t b = ai & 1;
+        if (ai >= 2 && !tc_wait(acce + b, ((ai >> 1) - 1) & 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + b * kTcBN;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % kTcStages;
+          if (!tc_wait(full + s, (it / kTcStages) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (it == 0) tc_stamp(t, 3);
+          tc_fence_after();
+          const uint32_t sa = s_u32(smem + (size_t)s * kTcStageBytes);
+          const uint32_t sb = sa + kTcABytes;
+#pragma unroll
+          for (int kk = 0; kk < kTcBK / 16; ++kk)
+            tc_mma(d, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32),
+                   (kb != kb0 || kk != 0) ? 1u : 0u);
+          tc_commit(empty + s);
+        }
+        if (ok) tc_commit(accf + b);
+      }
+      tc_stamp(t, 4);
+      tc_commit(fin);  // arrives once every MMA issued above has completed
+      tc_wait(fin, 0, nullptr);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int et = threadIdx.x - 64;
+    const int r = 32 * q + lane;  // tile row held after tcgen05.ld
+    const int pp0 = (int)(rank * 64 / S), np = (int)((rank + 1) * 64 / S) - pp0;  // row pairs finished here
+    uint32_t ai = 0;
+    for (int tile = cid; tile < t.tiles; tile += ncl, ++ai) {
+      const uint32_t b = ai & 1;
+      if (!epi_all(tc_wait(accf + b, (ai >> 1) & 1, abort_flag))) break;
+      if (ai == 0 && et == 0) tc_stamp(t, 5);
+      tc_fence_after();
+      float v[32];
+      tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + b * kTcBN, v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc_arrive(acce + b);
+
+      // this CTA's partial tile -> exchange buffer b (free once every peer read item ai - 2)
+      if (ai >= 2 && !epi_all(tc_wait<true>(xempty + b, ((ai >> 1) - 1) & 1, abort_flag))) break;
+      float* xb = xbuf + b * (kTcMaxM * kTcBM);
+#pragma unroll
+      for (int m = 0; m < 32; ++m)
+        if (m < t.M) xb[m * kTcBM + r] = v[m];
+      cl_fence();
+      epi_sync();
+      if (et < S) cl_arrive_remote(cl_map(s_u32(xfull + b), (uint32_t)et));
+      if (!epi_all(tc_wait<true>(xfull + b, (ai >> 1) & 1, abort_flag))) break;
+
+      // finish row pairs [pp0, pp0 + np) for every token: sum the S partials in rank order
+      uint32_t src[kTcMaxCluster];
+#pragma unroll
+      for (int s = 0; s < kTcMaxCluster; ++s) src[s] = s < S ? cl_map(s_u32(xb), (uint32_t)s) : 0u;
+      for (int e = et; e < np * t.M; e += 128) {
+        const int m = e / np, p = pp0 + (e - m * np);
+        const uint32_t off = (uint32_t)(m * kTcBM + 2 * p) * 4u;
+        float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+        for (int s = 0; s < kTcMaxCluster; ++s) {
+          if (s < S) {
+            const float2 f = cl_ld2(src[s] + off);
+            v0 += f.x;
+            v1 += f.y;
+          }
+        }
+        const int row0 = tile * kTcBM + 2 * p;
+        if (row0 < t.N) {
+          if (t.store_only) {
+            t.part[(size_t)m * t.N + row0] = v0;
+            t.part[(size_t)m * t.N + row0 + 1] = v1;
+          } else {
+            const unsigned long long key = epi_pair<EPI>(a, c, false, 0, row0 >> 1, m, v0, v1);
+            if (EPI == EPI_LMHEAD && key) atomicMax(best + m, key);
+          }
+        }
+      }
+      epi_sync();  // every read of the peers' buffers is complete
+      if (et < S) cl_arrive_remote(cl_map(s_u32(xempty + b), (uint32_t)et));
+    }
+    if (et == 0) tc_stamp(t, 6);
+    __syncwarp();
   }
 
+  // ---------------- teardown ----------------
+  tc_fence_before();
+  __syncthreads();
+  cl_sync_all();  // no CTA leaves while a peer may still read its exchange buffers
+  if (threadIdx.x == 0) tc_stamp(t, 7);
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols)
+                 : "memory");
+  }
   if constexpr (EPI == EPI_LMHEAD) {
-    __syncthreads();
-    if (threadIdx.x < M && best_s[threadIdx.x]) atomicMax(a.keys + threadIdx.x, best_s[threadIdx.x]);
+    if (threadIdx.x < t.M && best[threadIdx.x]) atomicMax(a.keys + threadIdx.x, best[threadIdx.x]);
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(a.done, 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) misc[2] = (atomicAdd(t.done, 1u) == gridDim.x - 1) ? 1u : 0u;
     __syncthreads();
-    if (!is_last) return;
+    if (!misc[2]) return;
     __threadfence();
-    __shared__ unsigned long long fin[kTcMaxM];
-    if (threadIdx.x < M) fin[threadIdx.x] = atomicAdd(a.keys + threadIdx.x, 0ull);
+    unsigned long long* fk = best;  // reuse: final keys [32]
+    if (threadIdx.x < t.M) fk[threadIdx.x] = atomicAdd(a.keys + threadIdx.x, 0ull);
     __syncthreads();
-    if (multi) {
+    if (c.world > 1) {
       const uint32_t ep = read_epoch(c);
       const int pr = ep & 1;
-      if (threadIdx.x < M)
-        for (int d = 0; d < c.world; ++d) key_ptr(c, d, pr, c.rank)[threadIdx.x] = fin[threadIdx.x];
+      if (threadIdx.x < t.M)
+        for (int d = 0; d < c.world; ++d) key_ptr(c, d, pr, c.rank)[threadIdx.x] = fk[threadIdx.x];
       __threadfence_system();
       __syncthreads();
       if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, kMaxCtas, c.rank), ep);
       if (threadIdx.x < c.world) wait_flag(c, kMaxCtas, threadIdx.x, ep);
       __syncthreads();
-      if (threadIdx.x < M) {
-        unsigned long long b = 0ull;
+      if (threadIdx.x < t.M) {
+        unsigned long long bk = 0ull;
         for (int s = 0; s < c.world; ++s) {
           const unsigned long long k = __ldcg(key_ptr(c, c.rank, pr, s) + threadIdx.x);
-          b = k > b ? k : b;
+          bk = k > bk ? k : bk;
         }
-        fin[threadIdx.x] = b;
+        fk[threadIdx.x] = bk;
       }
       __syncthreads();
       if (threadIdx.x == 0) c.state[kCalls] = ep;
     }
-    if (threadIdx.x < M) {
-      a.ids[threadIdx.x] = (int32_t)argmax_key_index(fin[threadIdx.x]);
+    if (threadIdx.x < t.M) {
+      a.ids[threadIdx.x] = (int32_t)argmax_key_index(fk[threadIdx.x]);
       a.keys[threadIdx.x] = 0ull;
     }
-    if (threadIdx.x == 0) *a.done = 0u;
+    if (threadIdx.x == 0) *t.done = 0u;
+  }
+}
+
+// ---- row-parallel projection across ranks: NVLink all-reduce + residual --------
+// CTA b owns row pairs [p0, p1); pushes this rank's fp32 rows to every rank's
+// slot, releases its flag on every rank, waits for the peers' flags, sums the
+// slots in rank order and adds the residual (the GEMV kernels' protocol,
+// comm.cuh).
+__global__ void __launch_bounds__(256) k_tc_rows_allreduce(GemvArgs a, const float* __restrict__ part, CommDev c) {
+  const int M = a.M, NB = a.N >> 1;
+  const int p0 = (int)((long long)blockIdx.x * NB / gridDim.x);
+  const int p1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
+  const uint32_t epoch = read_epoch(c);
+  const int par = epoch & 1;
+  for (int e = threadIdx.x; e < (p1 - p0) * M; e += blockDim.x) {
+    const int m = e / (p1 - p0), g = p0 + (e - m * (p1 - p0));
+    const float2 v = __ldcg(reinterpret_cast<const float2*>(part + (size_t)m * a.N + 2 * g));
+    epi_pair<EPI_ROWAR>(a, c, true, par, g, m, v.x, v.y);
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
+  if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
+  __syncthreads();
+  const int rows = 2 * (p1 - p0);
+  for (int e = threadIdx.x; e < rows * M; e += blockDim.x) {
+    const int m = e / rows, row = 2 * p0 + (e - (e / rows) * rows);
+    float sum = 0.f;
+    for (int src = 0; src < c.world; ++src) sum += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+    bf16* hp = a.h + (size_t)m * a.N + row;
+    *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(sum));
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(c.state + kDone, 1u) == gridDim.x - 1) {
+      c.state[kDone] = 0u;
+      __threadfence();
+      c.state[kCalls] = epoch;
+    }
   }
 }
 
@@ -378,33 +567,82 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int K, int box
   return JSX_OK;
 }
 
+static cudaLaunchConfig_t tc_config(int grid, int S, cudaStream_t s, cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = s;
+  attr->id = cudaLaunchAttributeClusterDimension;
+  attr->val.clusterDim.x = S;
+  attr->val.clusterDim.y = 1;
+  attr->val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+// Clusters of S CTAs that fit on the device at once (one CTA per SM), per
+// device; without a device, 148 / S (a B200).
+static int max_clusters(int S) {
+  static int cache[64][kTcMaxCluster + 1] = {};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148 / S;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev][S] == 0) {
+    int n = 0;
+    auto kern = k_tc_gemm<EPI_LINEAR>;
+    cudaLaunchAttribute attr;
+    cudaLaunchConfig_t cfg = tc_config(S, S, nullptr, &attr);
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
+      cudaGetLastError();
+      n = sm_count() / S;
+    }
+    cache[dev][S] = n > 0 ? n : 1;
+  }
+  return cache[dev][S];
+}
+
 struct TcPlan {
-  int tiles, kblocks, splits;
-  size_t xn_off, part_off, bytes;
+  int tiles, kblocks, S, clusters;
+  size_t part_off, bytes;
 };
 
-// K splits: about 4 CTAs per B200 SM (148 SMs, 2 resident CTAs each: two
-// waves), at least 4 K blocks per split.  The plan depends only on the shape,
-// so the workspace size and the summation order are the same on every device.
-constexpr int kTcTargetCtas = 4 * 148;
+// Cluster size S = 1..min(8, K blocks): the smallest modelled time
+//   waves x (K blocks per CTA x 20 KB + 16 KB of per-tile cost),
+// waves = ceil(tiles / clusters resident at once); ties keep the smaller S.
 static TcPlan tc_plan(int M, int K, int N) {
   TcPlan p;
   p.tiles = (N + kTcBM - 1) / kTcBM;
   p.kblocks = (K + kTcBK - 1) / kTcBK;
-  const int target = kTcTargetCtas;
-  int splits = (target + p.tiles - 1) / p.tiles;
-  int cap = p.kblocks / 4;
-  if (cap < 1) cap = 1;
-  if (splits > cap) splits = cap;
-  if (splits < 1) splits = 1;
-  p.splits = splits;
-  p.xn_off = 1024;
-  p.part_off = p.xn_off + (((size_t)kTcMaxM * K * 2 + 1023) & ~(size_t)1023);
-  p.bytes = p.part_off + (size_t)splits * M * N * sizeof(float);
+  const int smax = p.kblocks < kTcMaxCluster ? p.kblocks : kTcMaxCluster;
+  long long best_cost = -1;
+  p.S = 1;
+  p.clusters = 1;
+  for (int s = 1; s <= smax; ++s) {
+    const int cl = max_clusters(s);
+    const long long waves = (p.tiles + cl - 1) / cl;
+    const long long per = (p.kblocks + s - 1) / s;
+    const long long cost = waves * (per * 20480 + 16384);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      p.S = s;
+      p.clusters = cl < p.tiles ? cl : p.tiles;
+    }
+  }
+  p.part_off = kTcOffXn + (((size_t)kTcMaxM * K * 2 + 1023) & ~(size_t)1023);
+  p.bytes = p.part_off + (size_t)M * N * sizeof(float);
   return p;
 }
 
 CommDev comm_view(jsx_comm* comm);
+
+static uint64_t* g_trace_buf = nullptr;  // jsx_tc_set_trace
 
 template <int EPI>
 static int tc_run(jsx_comm* comm, GemvArgs ga, void* workspace, size_t workspace_bytes, cudaStream_t s) {
@@ -423,39 +661,52 @@ static int tc_run(jsx_comm* comm, GemvArgs ga, void* workspace, size_t workspace
     JSX_REQUIRE(ga.M <= c.max_tokens && (EPI != EPI_ROWAR || ga.N <= c.hidden),
                 "M=%d N=%d exceed the comm buffer", ga.M, ga.N);
   }
+  if (EPI == EPI_LMHEAD) {
+    ga.done = (uint32_t*)(ws + kTcOffDone);
+    ga.keys = (unsigned long long*)(ws + kTcOffKeys);
+  }
   // activations: RMS-normalised copy when a gain is given (layers/normalization.py:31-37)
   const void* x = ga.x;
   if (ga.gamma) {
-    const int st = jsx_rmsnorm(ga.x, ga.gamma, ws + p.xn_off, ga.M, ga.K, ga.eps, s);
+    const int st = jsx_rmsnorm(ga.x, ga.gamma, ws + kTcOffXn, ga.M, ga.K, ga.eps, s);
     if (st) return st;
-    x = ws + p.xn_off;
+    x = ws + kTcOffXn;
   }
   CUtensorMap tw, tx;
   int st = make_map(&tw, ga.w, ga.N, ga.K, kTcBM);
   if (st) return st;
   st = make_map(&tx, x, ga.M, ga.K, kTcBN);
   if (st) return st;
+  const bool across_ranks = EPI == EPI_ROWAR && c.world > 1;
   TcArgs ta;
   ta.part = (float*)(ws + p.part_off);
-  ta.M = ga.M; ta.N = ga.N; ta.K = ga.K; ta.kblocks = p.kblocks; ta.splits = p.splits; ta.tiles = p.tiles;
-  JSX_CUDA(cudaFuncSetAttribute(k_tc_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
-  k_tc_gemm<<<p.tiles * p.splits, kTcThreads, kTcSmem, s>>>(tw, tx, ta);
-  JSX_LAUNCHED("k_tc_gemm");
-  TcRowArgs ra;
-  ra.ga = ga;
-  ra.part = ta.part;
-  ra.splits = p.splits;
-  int grid = 2 * sm_count();
-  if (EPI == EPI_ROWAR && grid > kMaxCtas) grid = kMaxCtas;
-  if (grid > ga.N / 2) grid = ga.N / 2;
-  k_tc_rows<EPI><<<grid, 256, 0, s>>>(ra, c);
-  JSX_LAUNCHED("k_tc_rows");
+  ta.done = (uint32_t*)(ws + kTcOffDone);
+  ta.M = ga.M; ta.N = ga.N; ta.K = ga.K; ta.kblocks = p.kblocks; ta.S = p.S; ta.tiles = p.tiles;
+  ta.store_only = across_ranks ? 1 : 0;
+  ta.trace = g_trace_buf;
+  auto kern = k_tc_gemm<EPI>;
+  JSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
+  cudaLaunchAttribute attr;
+  const cudaLaunchConfig_t cfg = tc_config(p.clusters * p.S, p.S, s, &attr);
+  JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, tw, tx, ta, ga, c));
+  if (across_ranks) {
+    int rgrid = 2 * sm_count();
+    if (rgrid > kMaxCtas) rgrid = kMaxCtas;
+    if (rgrid > ga.N / 2) rgrid = ga.N / 2;
+    k_tc_rows_allreduce<<<rgrid, 256, 0, s>>>(ga, ta.part, c);
+    JSX_LAUNCHED("k_tc_rows_allreduce");
+  }
   return JSX_OK;
 }
 
 }  // namespace jsx
 
 using namespace jsx;
+
+extern "C" int jsx_tc_set_trace(uint64_t* buf) {
+  g_trace_buf = buf;
+  return JSX_OK;
+}
 
 extern "C" int jsx_tc_workspace_size(int M, int K, int N, size_t* bytes) {
   JSX_REQUIRE(bytes && M >= 1 && M <= kTcMaxM && K >= 8 && N >= 2, "bad arguments");
@@ -516,8 +767,6 @@ extern "C" int jsx_tc_lmhead_argmax(jsx_comm* comm, const void* h, const void* n
   GemvArgs a = {};
   a.x = (const bf16*)h; a.gamma = (const bf16*)norm_gamma; a.eps = eps; a.w = (const bf16*)w_vocab;
   a.M = M; a.K = hidden; a.N = vocab_local; a.y = (bf16*)logits_out; a.vocab_offset = vocab_offset;
-  a.done = (uint32_t*)workspace;                                    // header: done counter
-  a.keys = (unsigned long long*)((char*)workspace + 256);          // then M argmax keys
   a.ids = ids_out;
   return tc_run<EPI_LMHEAD>(comm, a, workspace, workspace_bytes, (cudaStream_t)stream);
 }

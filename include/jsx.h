@@ -174,6 +174,12 @@ int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, flo
  * jsx_tc_lmhead_argmax its first 512 bytes must be zero on the first call
  * (they are left zero). */
 int jsx_tc_workspace_size(int M, int K, int N, size_t* bytes);
+/* Profiling aid (no reference counterpart): when buf is non-NULL, every later
+ * jsx_tc_* launch of this process stamps %globaltimer (ns) per CTA into
+ * buf[cta * 8 + k], k = 0 entry, 1 first ring of loads issued, 2 loads done,
+ * 3 first stage consumed, 4 last MMA issued, 5 first accumulator read,
+ * 6 epilogue done, 7 exit; buf holds 8 x (SM count) u64.  NULL turns it off. */
+int jsx_tc_set_trace(uint64_t* buf);
 int jsx_tc_linear(const void* x, const void* gamma, float eps, const void* w_nk, const void* bias,
                   void* y, int M, int K, int N, void* workspace, size_t workspace_bytes,
                   void* stream);

@@ -68,16 +68,15 @@ def test_workspace_size_queries(jsx):
 
 
 def test_tc_workspace_size(jsx):
-    """Split partials [splits][M][N] fp32 after a 1 KB header and the normalised
-    activations; the plan depends on the shape only (about 592 CTAs, >= 4 K blocks a split)."""
+    """256 B done counter + argmax keys, the normalised activations [32][K] bf16
+    (from byte 1024, rounded to 1 KB), then the rank-local fp32 rows [M][N]."""
     lib = jsx._lib
     n = ctypes.c_size_t(0)
     lib.call("jsx_tc_workspace_size", 32, 4096, 4608, ctypes.byref(n))
-    tiles, kblocks = 36, 64
-    splits = min(-(-592 // tiles), kblocks // 4)
-    assert splits == 16
-    assert n.value == 1024 + 32 * 4096 * 2 + splits * 32 * 4608 * 4
+    assert n.value == 1024 + 32 * 4096 * 2 + 32 * 4608 * 4
     lib.call("jsx_tc_workspace_size", 9, 13696, 4096, ctypes.byref(n))
-    assert n.value == 1024 + 32 * 13696 * 2 + 19 * 9 * 4096 * 4
+    assert n.value == 1024 + 32 * 13696 * 2 + 9 * 4096 * 4
+    lib.call("jsx_tc_workspace_size", 3, 100, 8, ctypes.byref(n))
+    assert n.value == 1024 + 7168 + 3 * 8 * 4      # 32 x 100 x 2 = 6400 -> 7168
     with pytest.raises(lib.JsxError):
         lib.call("jsx_tc_workspace_size", 0, 64, 64, ctypes.byref(n))
