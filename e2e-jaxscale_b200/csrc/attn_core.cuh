@@ -64,13 +64,92 @@ __host__ __device__ __forceinline__ AttnLayout attn_layout(int B, int nq, int nk
   return L;
 }
 
+// Tensor-core item shape: a group of 16 query heads (the MMA's M) with
+// head_dim 128 (GLM-4: 32 query heads over 2 kv heads).  Shared rows are padded
+// to 136 bf16 (272 bytes) so the 8 row addresses of an ldmatrix hit distinct banks.
+constexpr int kMmaHeads = 16;
+constexpr int kMmaHd = 128;
+constexpr int kRowPad = kMmaHd + 8;   // bf16 per q/K/V row in shared memory
+constexpr int kPPad = kChunk + 8;     // bf16 per probability row
+__host__ __device__ __forceinline__ bool attn_use_mma(int gi, int hd) { return gi == kMmaHeads && hd == kMmaHd; }
+
 // Shared bytes of one item: q (fp32), scores/probabilities, padded K rows, V
-// rows; the combine reuses the K/V area.
+// rows; the combine reuses the K/V area.  Tensor-core items: q, K, V (bf16,
+// padded rows), fp32 scores, bf16 probabilities; the combine reuses all but q.
 __host__ __device__ __forceinline__ size_t attn_smem(int gi, int hd, int splits) {
+  const size_t combine = ((size_t)2 * splits * gi + 2 * gi) * 4;
+  if (attn_use_mma(gi, hd)) {
+    const size_t work = (size_t)2 * kChunk * kRowPad * 2 + (size_t)kMmaHeads * kChunk * 4 +
+                        (size_t)kMmaHeads * kPPad * 2;
+    return (size_t)kMmaHeads * kRowPad * 2 + (work > combine ? work : combine);
+  }
   const int hw = hd / 2;
   const size_t stage = (size_t)kChunk * (hw + 1) * 4 + (size_t)kChunk * hw * 4;
-  const size_t combine = ((size_t)2 * splits * gi + 2 * gi) * 4;
   return (size_t)gi * hd * 4 + (size_t)gi * kChunk * 4 + (stage > combine ? stage : combine);
+}
+
+// Completion of one item: the item that completes the set of splits of group
+// vb merges them (flash-decoding combine).  Weights w_t[h] = exp(m_t - M) / L
+// are formed once in shared memory (`scratch`, free once the item's own work is
+// done), then every output element is a short dot product over the splits.
+template <int NT>
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int b, int head0, int cur, float* scratch) {
+  __shared__ bool is_last;
+  const int gi = a.gi, hd = a.hd, tid = threadIdx.x;
+  const int stride = split_stride(gi, hd);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = atomicAdd(a.cnt + vb, 1u) == (uint32_t)(a.splits - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+
+  const int used = (cur + kChunk) / kChunk;
+  const float* pb = a.part + (size_t)vb * a.splits * stride;
+  float* wm = scratch;                       // [used][gi] m, then weights
+  float* wl = wm + a.splits * gi;            // [used][gi] l
+  float* Mg = wl + a.splits * gi;            // [gi]
+  float* Lg = Mg + gi;                       // [gi]
+  for (int i = tid; i < used * gi; i += NT) {
+    const int t = i / gi, h = i - (i / gi) * gi;
+    wm[i] = __ldcg(pb + (size_t)t * stride + gi * hd + h);
+    wl[i] = __ldcg(pb + (size_t)t * stride + gi * hd + gi + h);
+  }
+  __syncthreads();
+  for (int h = tid; h < gi; h += NT) {
+    float M = -INFINITY;
+    for (int t = 0; t < used; ++t) M = fmaxf(M, wm[t * gi + h]);
+    float L = 0.f;
+    for (int t = 0; t < used; ++t) L = fmaf(wl[t * gi + h], expf(wm[t * gi + h] - M), L);
+    Mg[h] = M;
+    Lg[h] = L;
+  }
+  __syncthreads();
+  for (int i = tid; i < used * gi; i += NT) {
+    const int h = i - (i / gi) * gi;
+    wm[i] = expf(wm[i] - Mg[h]) / Lg[h];
+  }
+  __syncthreads();
+  bf16* ob = a.out + ((size_t)b * a.nq + head0) * hd;
+  const int nv = (gi * hd) >> 2;
+  for (int i = tid; i < nv; i += NT) {
+    const int e = i << 2, h = e / hd;
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int t = 0; t < used; ++t) {
+      const float w = wm[t * gi + h];
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)t * stride + e));
+      o.x = fmaf(v.x, w, o.x);
+      o.y = fmaf(v.y, w, o.y);
+      o.z = fmaf(v.z, w, o.z);
+      o.w = fmaf(v.w, w, o.w);
+    }
+    uint2 packed;
+    packed.x = pack2(o.x, o.y);
+    packed.y = pack2(o.z, o.w);
+    *reinterpret_cast<uint2*>(ob + e) = packed;
+  }
+  if (tid == 0) a.cnt[vb] = 0u;
 }
 
 // One work item: cache rows [64 s, 64 s + 64) of item group vb (sequence b,
@@ -90,7 +169,6 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
   float* ps = qs + gi * hd;                                         // [gi][kChunk]
   uint32_t* ks = reinterpret_cast<uint32_t*>(ps + gi * kChunk);     // [kChunk][hw+1] (padded)
   uint32_t* vs = ks + kChunk * (hw + 1);                            // [kChunk][hw]
-  __shared__ bool is_last;
 
   const int b = vb / (a.nkv * a.hg);
   const int kvh = (vb / a.hg) % a.nkv, j = vb % a.hg;
@@ -202,62 +280,179 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
     }
   }
 
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(a.cnt + vb, 1u) == (uint32_t)(a.splits - 1);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
+  attn_finish<NT>(a, vb, b, head0, cur, reinterpret_cast<float*>(ks));
+}
 
-  // Combine the splits holding rows [0, cur]: weights w_t[h] = exp(m_t - M) / L
-  // are formed once in shared memory (the staging buffers are free now), then
-  // every output element is a short dot product over the splits.
-  const int used = (cur + kChunk) / kChunk;
-  const float* pb = a.part + (size_t)vb * a.splits * stride;
-  float* wm = reinterpret_cast<float*>(ks);  // [used][gi] m, then weights
-  float* wl = wm + a.splits * gi;            // [used][gi] l
-  float* Mg = wl + a.splits * gi;            // [gi]
-  float* Lg = Mg + gi;                       // [gi]
-  for (int i = tid; i < used * gi; i += NT) {
-    const int t = i / gi, h = i - (i / gi) * gi;
-    wm[i] = __ldcg(pb + (size_t)t * stride + gi * hd + h);
-    wl[i] = __ldcg(pb + (size_t)t * stride + gi * hd + gi + h);
+// ---- tensor-core item (mma.sync m16n8k16, bf16 in, fp32 accumulate) ----------
+// At batch >= 8 each CTA serves all 16 query heads of a kv head from one copy of
+// the split's K/V rows; the CUDA-core form then spends its time on shared-memory
+// reads (one load per FMA).  Here S = Q K^T and O = P V are m16n8k16 MMAs with
+// the 16 heads as M: every K/V element is read from shared memory once per
+// item.  The probabilities enter P.V rounded to bf16 (the reference also rounds
+// them to bf16 before its P.V product); m and l stay fp32.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+template <int NT, bool kCoherent, bool kEager>
+__device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, unsigned char* smem_raw) {
+  constexpr int NW = NT / 32;
+  constexpr int RW = kChunk / NW;   // score rows per warp (16 or 8)
+  constexpr int NS = RW / 8;        // n8 score tiles per warp
+  constexpr int DW = kMmaHd / NW;   // output dims per warp (32 or 16)
+  constexpr int NO = DW / 8;        // n8 output tiles per warp
+  static_assert(NW == 4 || NW == 8, "4 or 8 warps");
+  const int G = a.nq / a.nkv;
+  const int stride = split_stride(kMmaHeads, kMmaHd);
+  bf16* qs = reinterpret_cast<bf16*>(smem_raw);  // [16][kRowPad]
+  bf16* ks = qs + kMmaHeads * kRowPad;            // [64][kRowPad]
+  bf16* vs = ks + kChunk * kRowPad;               // [64][kRowPad]
+  float* ss = reinterpret_cast<float*>(vs + kChunk * kRowPad);  // [16][64] scores
+  bf16* ps = reinterpret_cast<bf16*>(ss + kMmaHeads * kChunk);  // [16][kPPad] probabilities
+
+  const int b = vb / (a.nkv * a.hg);
+  const int kvh = (vb / a.hg) % a.nkv, j = vb % a.hg;
+  const int head0 = kvh * G + j * kMmaHeads;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  __syncthreads();  // a CTA may run several items back to back over the same shared memory
+
+  const int p0 = s * kChunk;
+  int cur = a.pos[b];
+  const int rows = kEager ? min(kChunk, a.max_seq - p0) : max(0, min(kChunk, min(cur, a.max_seq - 1) + 1 - p0));
+  if (cur > a.max_seq - 1) cur = a.max_seq - 1;
+  if (cur < 0) cur = 0;
+  int n = cur + 1 - p0;  // rows of this split inside [0, cur]
+  if (n > kChunk) n = kChunk;
+  const bf16* qg = a.q + ((size_t)b * a.nq + head0) * kMmaHd;
+  for (int i = tid; i < kMmaHeads * 16; i += NT) {
+    const int h = i >> 4, c = i & 15;
+    const uint4* src = reinterpret_cast<const uint4*>(qg + h * kMmaHd) + c;
+    *reinterpret_cast<uint4*>(qs + h * kRowPad + c * 8) = kCoherent ? __ldcg(src) : *src;
   }
-  __syncthreads();
-  for (int h = tid; h < gi; h += NT) {
-    float M = -INFINITY;
-    for (int t = 0; t < used; ++t) M = fmaxf(M, wm[t * gi + h]);
-    float L = 0.f;
-    for (int t = 0; t < used; ++t) L = fmaf(wl[t * gi + h], expf(wm[t * gi + h] - M), L);
-    Mg[h] = M;
-    Lg[h] = L;
-  }
-  __syncthreads();
-  for (int i = tid; i < used * gi; i += NT) {
-    const int h = i - (i / gi) * gi;
-    wm[i] = expf(wm[i] - Mg[h]) / Lg[h];
-  }
-  __syncthreads();
-  bf16* ob = a.out + ((size_t)b * a.nq + head0) * hd;
-  const int nv = (gi * hd) >> 2;
-  for (int i = tid; i < nv; i += NT) {
-    const int e = i << 2, h = e / hd;
-    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int t = 0; t < used; ++t) {
-      const float w = wm[t * gi + h];
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(pb + (size_t)t * stride + e));
-      o.x = fmaf(v.x, w, o.x);
-      o.y = fmaf(v.y, w, o.y);
-      o.z = fmaf(v.z, w, o.z);
-      o.w = fmaf(v.w, w, o.w);
+  // K/V rows: rows at or past n are stored as zeros (masked probabilities are
+  // exactly 0 and must not meet non-finite cache contents)
+  const size_t row_stride = (size_t)a.nkv * kMmaHd;
+  const bf16* kb = a.kc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
+  const bf16* vbp = a.vc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
+  for (int i = tid; i < kChunk * 16; i += NT) {
+    const int r = i >> 4, c = i & 15;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (r < rows) {
+      const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)r * row_stride) + c;
+      const uint4* vp = reinterpret_cast<const uint4*>(vbp + (size_t)r * row_stride) + c;
+      kv = kCoherent ? __ldcg(kp) : *kp;
+      vv = kCoherent ? __ldcg(vp) : *vp;
     }
-    uint2 packed;
-    packed.x = pack2(o.x, o.y);
-    packed.y = pack2(o.z, o.w);
-    *reinterpret_cast<uint2*>(ob + e) = packed;
+    if (r >= n) {
+      kv = make_uint4(0, 0, 0, 0);
+      vv = make_uint4(0, 0, 0, 0);
+    }
+    *reinterpret_cast<uint4*>(ks + r * kRowPad + c * 8) = kv;
+    *reinterpret_cast<uint4*>(vs + r * kRowPad + c * 8) = vv;
   }
-  if (tid == 0) a.cnt[vb] = 0u;
+  float* part = a.part + ((size_t)vb * a.splits + s) * stride;
+  __syncthreads();
+
+  if (n > 0) {
+    const int g = lane >> 2, t4 = lane & 3;
+    // S = Q K^T for rows [RW warp, RW warp + RW)
+    float sc[NS][4];
+#pragma unroll
+    for (int jn = 0; jn < NS; ++jn) sc[jn][0] = sc[jn][1] = sc[jn][2] = sc[jn][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kMmaHd / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(smem_addr(qs + (lane & 15) * kRowPad + 16 * kk + (lane >> 4) * 8), a0, a1, a2, a3);
+#pragma unroll
+      for (int jn = 0; jn < NS; ++jn) {
+        uint32_t b0, b1;
+        ldsm_x2(smem_addr(ks + (RW * warp + 8 * jn + (lane & 7)) * kRowPad + 16 * kk + ((lane >> 3) & 1) * 8),
+                b0, b1);
+        mma_bf16_16816(sc[jn], a0, a1, a2, a3, b0, b1);
+      }
+    }
+#pragma unroll
+    for (int jn = 0; jn < NS; ++jn) {
+      const int r = RW * warp + 8 * jn + 2 * t4;
+      ss[g * kChunk + r] = r < n ? sc[jn][0] * a.scale : -INFINITY;
+      ss[g * kChunk + r + 1] = r + 1 < n ? sc[jn][1] * a.scale : -INFINITY;
+      ss[(g + 8) * kChunk + r] = r < n ? sc[jn][2] * a.scale : -INFINITY;
+      ss[(g + 8) * kChunk + r + 1] = r + 1 < n ? sc[jn][3] * a.scale : -INFINITY;
+    }
+    __syncthreads();
+    // softmax pieces per head: m, e = exp(s - m) (bf16 for the MMA), l (fp32)
+    for (int h = warp; h < kMmaHeads; h += NW) {
+      float v[kRowBlocks];
+      float m = -INFINITY;
+#pragma unroll
+      for (int rb = 0; rb < kRowBlocks; ++rb) {
+        v[rb] = ss[h * kChunk + rb * 32 + lane];
+        m = fmaxf(m, v[rb]);
+      }
+      m = warp_max(m);
+      float l = 0.f;
+#pragma unroll
+      for (int rb = 0; rb < kRowBlocks; ++rb) {
+        const float e = (rb * 32 + lane < n) ? expf(v[rb] - m) : 0.f;
+        ps[h * kPPad + rb * 32 + lane] = __float2bfloat16_rn(e);
+        l += e;
+      }
+      l = warp_sum(l);
+      if (lane == 0) {
+        part[kMmaHeads * kMmaHd + h] = m;
+        part[kMmaHeads * kMmaHd + kMmaHeads + h] = l;
+      }
+    }
+    __syncthreads();
+    // O = P V for dims [DW warp, DW warp + DW)
+    float o[NO][4];
+#pragma unroll
+    for (int jn = 0; jn < NO; ++jn) o[jn][0] = o[jn][1] = o[jn][2] = o[jn][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kChunk / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      ldsm_x4(smem_addr(ps + (lane & 15) * kPPad + 16 * kk + (lane >> 4) * 8), a0, a1, a2, a3);
+#pragma unroll
+      for (int jn = 0; jn < NO; ++jn) {
+        uint32_t b0, b1;
+        ldsm_x2_t(smem_addr(vs + (16 * kk + (lane & 7) + ((lane >> 3) & 1) * 8) * kRowPad + DW * warp + 8 * jn),
+                  b0, b1);
+        mma_bf16_16816(o[jn], a0, a1, a2, a3, b0, b1);
+      }
+    }
+#pragma unroll
+    for (int jn = 0; jn < NO; ++jn) {
+      const int d = DW * warp + 8 * jn + 2 * t4;
+      *reinterpret_cast<float2*>(part + g * kMmaHd + d) = make_float2(o[jn][0], o[jn][1]);
+      *reinterpret_cast<float2*>(part + (g + 8) * kMmaHd + d) = make_float2(o[jn][2], o[jn][3]);
+    }
+  }
+  attn_finish<NT>(a, vb, b, head0, cur, reinterpret_cast<float*>(ks));
+}
+
+// The item body for the group shape: tensor-core form for 16-head groups of
+// head_dim 128, CUDA-core form otherwise.
+template <int NT, bool kCoherent, bool kEager>
+__device__ __forceinline__ void attn_item_any(const AttnArgs& a, int s, int vb, unsigned char* smem_raw) {
+  if (attn_use_mma(a.gi, a.hd)) attn_item_mma<NT, kCoherent, kEager>(a, s, vb, smem_raw);
+  else attn_item<NT, kCoherent, kEager>(a, s, vb, smem_raw);
 }
 
 }  // namespace jsx

@@ -290,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     at.kc = reinterpret_cast<const bf16*>(L.k_cache);
     at.vc = reinterpret_cast<const bf16*>(L.v_cache);
     for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
-      attn_item<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
+      attn_item_any<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden);
     grid_wait(bar, gen);
