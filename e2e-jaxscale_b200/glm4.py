@@ -33,6 +33,9 @@ from .weights import PackedLayer, RandomLayerSource, pack_layer
 
 CHUNK = K.MAX_DECODE_TOKENS
 TC_CHUNK = K.TC_MAX_TOKENS
+# smallest batch whose projections run on the tensor cores (jsx_tc_*); smaller
+# batches stream the weights through the CUDA-core GEMV / whole-step kernel
+TC_MIN_BATCH = int(os.environ.get("JSX_TC_MIN_BATCH", "3"))
 
 
 class DecodeState:
@@ -55,11 +58,11 @@ class DecodeState:
         self.lm_ws = K.lmhead_workspace(CHUNK, dev)
         self.logits = (torch.zeros(batch, model.V_l, dtype=torch.bfloat16, device=dev)
                        if want_logits else None)
+        # batches from TC_MIN_BATCH run the projections on the tensor cores
+        self.tc = batch >= TC_MIN_BATCH or batch > CHUNK
         self.step_args = None
-        if batch <= CHUNK and model.layers:
+        if not self.tc and model.layers:
             self._build_step_args(model)
-        # batches above the GEMV width run the projections on the tensor cores
-        self.tc = batch > CHUNK
         self.tc_ws = None
         if self.tc and model.layers:
             lp, H = model.layers[0], c.hidden_size
@@ -215,8 +218,9 @@ class GLM4ForCausalLM:
 
     def step(self, st: DecodeState, head: bool = True) -> None:
         """One token per sequence at st.pos; st.ids <- greedy tokens (head), st.pos += 1.
-        Batch <= 8 runs the whole step as one kernel (jsx_decode_step) unless
-        self.fused_step is False; larger batches chain the per-op kernels."""
+        Small batches run the whole step as one kernel (jsx_decode_step) unless
+        self.fused_step is False; batches from TC_MIN_BATCH chain the tensor-core
+        projections and the attention kernel."""
         if self.fused_step and st.step_args is not None:
             st.step_args.head = 1 if head else 0
             K.decode_step(self.comm, st.step_args)
@@ -227,13 +231,16 @@ class GLM4ForCausalLM:
         st.pos.add_(1)
 
     def kernels_per_step(self, batch: int, head: bool = True) -> int:
-        if self.fused_step and batch <= CHUNK:
+        tc = batch >= TC_MIN_BATCH or batch > CHUNK
+        if self.fused_step and not tc:
             return 1
-        if batch > CHUNK:
-            # per layer: rmsnorm + GEMM + epilogue (qkv, gate_up), GEMM + epilogue (o, down), attention
+        if tc:
+            # per layer and 32-token chunk: RMSNorm + GEMM (qkv, gate_up), GEMM (o, down; plus the
+            # NVLink all-reduce kernel when tp > 1); attention once per layer; LM head RMSNorm + GEMM
             ch = math.ceil(batch / TC_CHUNK)
-            n = 1 + self.config.num_hidden_layers * (1 + 10 * ch)
-            return n + (3 * ch if head else 0)
+            per = 6 + (2 if self.tp > 1 else 0)
+            n = 1 + self.config.num_hidden_layers * (1 + per * ch)
+            return n + (2 * ch if head else 0)
         ch = math.ceil(batch / CHUNK)
         n = 1 + self.config.num_hidden_layers * (1 + 4 * ch)
         return n + (ch if head else 0)

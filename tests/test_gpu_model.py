@@ -162,8 +162,14 @@ def test_config0_glm4_9b_two_layers(jsx, ref, cuda):
     print("near-tie flips (step, seq, margin, bound):", flips)
 
 
+@pytest.fixture
+def gemv_batches(monkeypatch):
+    """Keep batches up to 8 on the CUDA-core GEMV / whole-step path."""
+    monkeypatch.setattr(importlib.import_module("e2e-jaxscale_b200.glm4"), "TC_MIN_BATCH", 1 << 30)
+
+
 @pytest.mark.parametrize("B", [1, 3, 8])
-def test_fused_step_matches_per_op_kernels(jsx, ref, cuda, B):
+def test_fused_step_matches_per_op_kernels(jsx, ref, cuda, gemv_batches, B):
     """The whole-step kernel (jsx_decode_step) gives exactly the per-op kernels' results:
     the same per-row work and reduction order, only without the launches between them."""
     rc = small_cfg(ref)
@@ -198,7 +204,7 @@ def test_fused_step_matches_per_op_kernels(jsx, ref, cuda, B):
     assert status.value == 0
 
 
-def test_fused_step_batch8_full_width(jsx, ref, cuda):
+def test_fused_step_batch8_full_width(jsx, ref, cuda, gemv_batches):
     """Batch 8 at the GLM-4-9B widths (down_proj K = 13696): the activations fill
     219 KB of shared memory, one CTA per SM; fused and per-op steps agree exactly."""
     rc = ref.GLMConfig(num_hidden_layers=1, vocab_size=2048)
