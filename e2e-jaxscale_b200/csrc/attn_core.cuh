@@ -84,9 +84,17 @@ __host__ __device__ __forceinline__ size_t attn_smem(int gi, int hd, int splits)
     return (size_t)kMmaHeads * kRowPad * 2 + (work > combine ? work : combine);
   }
   const int hw = hd / 2;
-  const size_t stage = (size_t)kChunk * (hw + 1) * 4 + (size_t)kChunk * hw * 4;
+  const size_t stage = (size_t)kChunk * (hw + 1) * 4 + (size_t)2 * kChunk * hw * 4;
   return (size_t)gi * hd * 4 + (size_t)gi * kChunk * 4 + (stage > combine ? stage : combine);
 }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// 16-byte global -> shared copy; src_bytes < 16 zero-fills the rest (0: no read)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(dst)), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // Completion of one item: the item that completes the set of splits of group
 // vb merges them (flash-decoding combine).  Weights w_t[h] = exp(m_t - M) / L
@@ -186,15 +194,22 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
   const size_t row_stride = (size_t)a.nkv * hd;  // elements between consecutive cache rows
   const bf16* kb = a.kc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * hd;
   const bf16* vbp = a.vc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * hd;
+  // K and V rows arrive by cp.async (cp.async.cg reads through L2: coherent
+  // with other CTAs' writes), every copy of the thread in flight at once; K
+  // lands unpadded in kraw and each thread repacks its own chunks into the
+  // padded rows the score loop reads.
+  uint32_t* kraw = vs + kChunk * hw;  // [kChunk][hw]
   for (int i = tid; i < rows * hq; i += NT) {
     const int r = i / hq, c = i - (i / hq) * hq;
-    const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)r * row_stride) + c;
-    const uint4* vp = reinterpret_cast<const uint4*>(vbp + (size_t)r * row_stride) + c;
-    const uint4 kv = kCoherent ? __ldcg(kp) : *kp;
-    const uint4 vv = kCoherent ? __ldcg(vp) : *vp;
+    cp_async16(kraw + r * hw + 4 * c, kb + (size_t)r * row_stride + 8 * c, 16u);
+    cp_async16(vs + r * hw + 4 * c, vbp + (size_t)r * row_stride + 8 * c, 16u);
+  }
+  cp_async_wait_all();
+  for (int i = tid; i < rows * hq; i += NT) {
+    const int r = i / hq, c = i - (i / hq) * hq;
+    const uint4 kv = *reinterpret_cast<const uint4*>(kraw + r * hw + 4 * c);
     uint32_t* kd = ks + r * (hw + 1) + 4 * c;
     kd[0] = kv.x; kd[1] = kv.y; kd[2] = kv.z; kd[3] = kv.w;
-    reinterpret_cast<uint4*>(vs + r * hw)[c] = vv;
   }
   if (cur > a.max_seq - 1) cur = a.max_seq - 1;
   if (cur < 0) cur = 0;
@@ -309,7 +324,6 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint3
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 template <int NT, bool kCoherent, bool kEager>
 __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, unsigned char* smem_raw) {
@@ -340,32 +354,36 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
   if (cur < 0) cur = 0;
   int n = cur + 1 - p0;  // rows of this split inside [0, cur]
   if (n > kChunk) n = kChunk;
+  // q, K and V arrive by cp.async (cp.async.cg reads through L2: coherent with
+  // other CTAs' writes), every copy of the thread in flight at once.  Rows past
+  // the staged ones are zero-filled; with eager staging the rows at or past n
+  // are zeroed after the copies land (masked probabilities are exactly 0 and
+  // must not meet non-finite cache contents).
   const bf16* qg = a.q + ((size_t)b * a.nq + head0) * kMmaHd;
   for (int i = tid; i < kMmaHeads * 16; i += NT) {
     const int h = i >> 4, c = i & 15;
-    const uint4* src = reinterpret_cast<const uint4*>(qg + h * kMmaHd) + c;
-    *reinterpret_cast<uint4*>(qs + h * kRowPad + c * 8) = kCoherent ? __ldcg(src) : *src;
+    cp_async16(qs + h * kRowPad + c * 8, qg + h * kMmaHd + c * 8, 16u);
   }
-  // K/V rows: rows at or past n are stored as zeros (masked probabilities are
-  // exactly 0 and must not meet non-finite cache contents)
   const size_t row_stride = (size_t)a.nkv * kMmaHd;
   const bf16* kb = a.kc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
   const bf16* vbp = a.vc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
+  const int live_rows = kEager ? rows : min(rows, n);
   for (int i = tid; i < kChunk * 16; i += NT) {
     const int r = i >> 4, c = i & 15;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (r < rows) {
-      const uint4* kp = reinterpret_cast<const uint4*>(kb + (size_t)r * row_stride) + c;
-      const uint4* vp = reinterpret_cast<const uint4*>(vbp + (size_t)r * row_stride) + c;
-      kv = kCoherent ? __ldcg(kp) : *kp;
-      vv = kCoherent ? __ldcg(vp) : *vp;
+    const bool live = r < live_rows;
+    const size_t off = (size_t)(live ? r : 0) * row_stride + c * 8;
+    cp_async16(ks + r * kRowPad + c * 8, kb + off, live ? 16u : 0u);
+    cp_async16(vs + r * kRowPad + c * 8, vbp + off, live ? 16u : 0u);
+  }
+  cp_async_wait_all();
+  if (kEager) {
+    for (int i = tid; i < kChunk * 16; i += NT) {
+      const int r = i >> 4, c = i & 15;
+      if (r >= n && r < rows) {
+        *reinterpret_cast<uint4*>(ks + r * kRowPad + c * 8) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(vs + r * kRowPad + c * 8) = make_uint4(0, 0, 0, 0);
+      }
     }
-    if (r >= n) {
-      kv = make_uint4(0, 0, 0, 0);
-      vv = make_uint4(0, 0, 0, 0);
-    }
-    *reinterpret_cast<uint4*>(ks + r * kRowPad + c * 8) = kv;
-    *reinterpret_cast<uint4*>(vs + r * kRowPad + c * 8) = vv;
   }
   float* part = a.part + ((size_t)vb * a.splits + s) * stride;
   __syncthreads();
