@@ -39,7 +39,7 @@ extern "C" int jsx_comm_create(int rank, int world, int max_tokens, int hidden, 
   }
   JSX_CUDA(cudaGetDevice(&c->device));
   const size_t flags = round256((size_t)(kMaxCtas + 1) * world * sizeof(uint32_t));
-  const size_t data = round256((size_t)2 * world * max_tokens * hidden * sizeof(float));
+  const size_t data = round256((size_t)2 * world * max_tokens * hidden * sizeof(unsigned long long));
   const size_t keys = round256((size_t)2 * world * max_tokens * sizeof(unsigned long long));
   c->bytes = flags + data + keys;
   c->dev.off_data = flags;

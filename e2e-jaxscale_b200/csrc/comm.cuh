@@ -1,8 +1,14 @@
 // Tensor-parallel group: device view of the symmetric NVLink buffers.
 //
 // Every rank owns one buffer with the same layout; peers write into it with
-// plain P2P stores (CUDA IPC mappings), then publish with a release store of
-// the call's epoch into a flag.  Waiters acquire-load their own flags.
+// plain P2P stores (CUDA IPC mappings).
+//
+// Row-parallel partials travel as 8-byte "LL" words, the fp32 value in the low
+// half and the call's epoch in the high half, written with one 8-byte store:
+// a reader that sees the epoch it waits for has the value too, so no fence or
+// separate flag sits between a push and its use (the store's single-copy
+// atomicity carries the ordering).  The LM-head key exchange (64-bit keys, no
+// room for a tag) publishes with a release store of the epoch into a flag.
 //
 // Epochs come from a per-rank device counter (`state[kCalls]`) that the last
 // CTA of every collective kernel advances, so the protocol needs no host
@@ -30,7 +36,7 @@ struct CommDev {
   int world;
   int max_tokens;
   int hidden;
-  size_t off_data;        // float [2][world][max_tokens][hidden]
+  size_t off_data;        // u64 LL words [2][world][max_tokens][hidden]
   size_t off_keys;        // u64   [2][world][max_tokens]
   unsigned long long timeout_ns;
 };
@@ -38,8 +44,8 @@ struct CommDev {
 __device__ __forceinline__ uint32_t* flag_ptr(const CommDev& c, int r, int row, int src) {
   return reinterpret_cast<uint32_t*>(c.base[r]) + (size_t)row * c.world + src;
 }
-__device__ __forceinline__ float* data_ptr(const CommDev& c, int r, int par, int src, int m) {
-  return reinterpret_cast<float*>(c.base[r] + c.off_data) +
+__device__ __forceinline__ unsigned long long* data_ptr(const CommDev& c, int r, int par, int src, int m) {
+  return reinterpret_cast<unsigned long long*>(c.base[r] + c.off_data) +
          ((size_t)(par * c.world + src) * c.max_tokens + m) * c.hidden;
 }
 __device__ __forceinline__ unsigned long long* key_ptr(const CommDev& c, int r, int par, int src) {
@@ -67,6 +73,34 @@ __device__ __forceinline__ void wait_flag(const CommDev& c, int row, int src, ui
       }
     }
     __nanosleep(32);
+  }
+}
+
+// Push one partial value to a peer's (or this rank's) slot.
+__device__ __forceinline__ void ll_put(unsigned long long* slot, float v, uint32_t epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(slot), "l"(w) : "memory");
+}
+
+// The value of a slot once it carries `epoch`.  Bounded: after the comm
+// timeout (or at once when an earlier wait of this rank gave up) the error
+// word is set and 0 is returned; the host reports JSX_ETIMEDOUT.
+__device__ __forceinline__ float ll_get(const CommDev& c, const unsigned long long* slot, uint32_t epoch) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(slot) : "memory");
+  if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
+  if (*reinterpret_cast<volatile uint32_t*>(c.state + kError)) return 0.f;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(slot) : "memory");
+    if ((uint32_t)(w >> 32) == epoch) return __uint_as_float((uint32_t)w);
+    if ((it & 15u) == 0) {
+      if (globaltimer() - t0 > c.timeout_ns || it > (1u << 28)) {
+        atomicOr(c.state + kError, 1u);
+        return 0.f;
+      }
+      __nanosleep(20);
+    }
   }
 }
 

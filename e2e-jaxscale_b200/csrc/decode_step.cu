@@ -114,7 +114,7 @@ __device__ __forceinline__ void prefetch(Batch& bt, const bf16* w, int K, int N)
 
 // One GEMV phase (bt holds the first batch of this warp's first group).
 template <int M, int EPI>
-__device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c, bool multi, int par,
+__device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c, bool multi, uint32_t epoch,
                                            const bf16* xs, Batch& bt, unsigned long long (&best)[M]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = ga.K >> 3, ngroups = ga.N / kRows, G = gridDim.x;
@@ -152,7 +152,7 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c,
           bf16* hp = ga.h + (size_t)m * ga.N + row;
           *hp = __float2bfloat16_rn(__bfloat162float(__ldcg(hp)) + rbf(v));
         } else {
-          for (int d = 0; d < c.world; ++d) data_ptr(c, d, par, c.rank, m)[row] = v;
+          for (int d = 0; d < c.world; ++d) ll_put(data_ptr(c, d, epoch & 1, c.rank, m) + row, v, epoch);
         }
       }
     } else if constexpr (EPI == EPI_LMHEAD) {
@@ -175,16 +175,12 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c,
   }
 }
 
-// Row-parallel exchange of one all-reduce phase: publish this CTA's partial
-// rows to every rank, wait for the peers' and add the rank-ordered sum.
+// Row-parallel exchange of one all-reduce phase: the rows this CTA computed,
+// read from every rank's LL slots once they carry the phase's epoch, summed in
+// rank order and added to the residual.
 template <int M>
-__device__ __forceinline__ void allreduce_rows(const GemvArgs& ga, const CommDev& c, uint32_t epoch, int par) {
+__device__ __forceinline__ void allreduce_rows(const GemvArgs& ga, const CommDev& c, uint32_t epoch) {
   const int ngroups = ga.N / kRows, G = gridDim.x;
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
-  if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
-  __syncthreads();
   const int my_groups = (ngroups - (int)blockIdx.x + G - 1) / G;
   const int entries = my_groups * kRows * M;
   for (int e = threadIdx.x; e < entries; e += blockDim.x) {
@@ -193,7 +189,7 @@ __device__ __forceinline__ void allreduce_rows(const GemvArgs& ga, const CommDev
     const int r = rem / M, m = rem - (rem / M) * M;
     const int row = (blockIdx.x + G * gl) * kRows + r;
     float s = 0.f;
-    for (int src = 0; src < c.world; ++src) s += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+    for (int src = 0; src < c.world; ++src) s += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
     bf16* hp = ga.h + (size_t)m * ga.N + row;
     *hp = __float2bfloat16_rn(__bfloat162float(__ldcg(hp)) + rbf(s));
   }
@@ -282,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.nq = a.n_heads; ga.nkv = a.n_kv_heads; ga.hd = a.head_dim; ga.rot = a.rotary_dim;
       ga.max_seq = a.max_seq; ga.tps = 1;
       stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_QKV>(ga, c, multi, 0, xs, bt, best);
+      gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best);
     }
     grid_sync(bar, gen);
   trace_mark(a.trace, tn);
@@ -304,8 +300,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.h = reinterpret_cast<bf16*>(a.h);
       const uint32_t ep = epoch0 + 2u * l;
       stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep & 1, xs, bt, best);
-      if (multi) allreduce_rows<M>(ga, c, ep, ep & 1);
+      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
+      if (multi) allreduce_rows<M>(ga, c, ep);
     }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter);
@@ -321,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.M = M; ga.K = a.hidden; ga.N = 2 * a.inter;
       ga.y = reinterpret_cast<bf16*>(a.act);
       stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0, xs, bt, best);
+      gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0u, xs, bt, best);
     }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden);
@@ -336,8 +332,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.h = reinterpret_cast<bf16*>(a.h);
       const uint32_t ep = epoch0 + 2u * l + 1u;
       stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep & 1, xs, bt, best);
-      if (multi) allreduce_rows<M>(ga, c, ep, ep & 1);
+      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
+      if (multi) allreduce_rows<M>(ga, c, ep);
     }
     grid_arrive(bar, gen);
     if (l + 1 < a.n_layers)
@@ -370,7 +366,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     ga.y = reinterpret_cast<bf16*>(a.logits);
     ga.vocab_offset = a.vocab_offset;
     stage_x<M, false, true>(ga, xs);
-    gemv_phase<M, EPI_LMHEAD>(ga, c, multi, 0, xs, bt, best);
+    gemv_phase<M, EPI_LMHEAD>(ga, c, multi, 0u, xs, bt, best);
   }
   if (lane == 0) {
 #pragma unroll

@@ -54,11 +54,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
 
   const bool multi = (EPI == EPI_ROWAR || EPI == EPI_LMHEAD) && c.world > 1;
   uint32_t epoch = 0;
-  int par = 0;
-  if (EPI == EPI_ROWAR && multi) {
-    epoch = read_epoch(c);
-    par = epoch & 1;
-  }
+  if (EPI == EPI_ROWAR && multi) epoch = read_epoch(c);
 
   stage_x<M>(a, xs);
   const uint4* xv = reinterpret_cast<const uint4*>(xs);
@@ -109,7 +105,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
           bf16* hp = a.h + (size_t)m * a.N + row;
           *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(v));
         } else {
-          for (int d = 0; d < c.world; ++d) data_ptr(c, d, par, c.rank, m)[row] = v;
+          for (int d = 0; d < c.world; ++d) ll_put(data_ptr(c, d, epoch & 1, c.rank, m) + row, v, epoch);
         }
       }
     } else if constexpr (EPI == EPI_LMHEAD) {
@@ -134,12 +130,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
 
   if constexpr (EPI == EPI_ROWAR) {
     if (multi) {
-      // publish this CTA's partial tile to every rank, then gather
-      __threadfence_system();
-      __syncthreads();
-      if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
-      if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
-      __syncthreads();
+      // gather this CTA's rows from every rank's LL slots (rank order)
       const int my_groups = (ngroups - (int)blockIdx.x + grid - 1) / grid;
       const int entries = my_groups * kRows * M;
       for (int e = threadIdx.x; e < entries; e += blockDim.x) {
@@ -148,7 +139,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
         const int r = rem / M, m = rem - (rem / M) * M;
         const int row = (blockIdx.x + grid * gl) * kRows + r;
         float s = 0.f;
-        for (int src = 0; src < c.world; ++src) s += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+        for (int src = 0; src < c.world; ++src) s += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
         bf16* hp = a.h + (size_t)m * a.N + row;
         *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(s));
       }
@@ -380,11 +371,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_gemv_stream(GemvArgs a, C
   pdl_wait();
   const bool multi = (EPI == EPI_ROWAR || EPI == EPI_LMHEAD) && c.world > 1;
   uint32_t epoch = 0;
-  int par = 0;
-  if (EPI == EPI_ROWAR && multi) {
-    epoch = read_epoch(c);
-    par = epoch & 1;
-  }
+  if (EPI == EPI_ROWAR && multi) epoch = read_epoch(c);
   stage_x<M, true>(a, xs);
 
   const uint4* xv = reinterpret_cast<const uint4*>(xs);
@@ -425,7 +412,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_gemv_stream(GemvArgs a, C
       for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
     if (ok && lane < M && !abort_flag) {
       const unsigned long long k =
-          epi_pair<EPI>(a, c, multi, par, pair, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
+          epi_pair<EPI>(a, c, multi, epoch, pair, lane, pick<M>(acc, 0, lane), pick<M>(acc, 1, lane));
       best = k > best ? k : best;
     }
   };
@@ -468,16 +455,12 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_gemv_stream(GemvArgs a, C
 
   if constexpr (EPI == EPI_ROWAR) {
     if (multi) {
-      __threadfence_system();
-      consumer_sync();
-      if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
-      if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
-      consumer_sync();
       const int rows = 2 * (b1 - b0);
       for (int e = threadIdx.x; e < rows * M; e += kThreads) {
         const int m = e / rows, row = 2 * b0 + (e - (e / rows) * rows);
         float sum = 0.f;
-        for (int src = 0; src < c.world; ++src) sum += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+        for (int src = 0; src < c.world; ++src)
+          sum += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
         bf16* hp = a.h + (size_t)m * a.N + row;
         *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(sum));
       }

@@ -244,7 +244,7 @@ __device__ __forceinline__ void epi_swiglu(const GemvArgs& a, int g, const float
 // argmax key of the pair (LM head) or 0.
 template <int EPI>
 __device__ __forceinline__ unsigned long long epi_pair(const GemvArgs& a, const CommDev& c, bool multi,
-                                                       int par, int g, int m, float v0, float v1) {
+                                                       uint32_t epoch, int g, int m, float v0, float v1) {
   const int r0 = 2 * g;
   if constexpr (EPI == EPI_LINEAR) {
     float y0 = rbf(v0), y1 = rbf(v1);
@@ -265,9 +265,9 @@ __device__ __forceinline__ unsigned long long epi_pair(const GemvArgs& a, const 
       hp[1] = __float2bfloat16_rn(__bfloat162float(hp[1]) + rbf(v1));
     } else {
       for (int d = 0; d < c.world; ++d) {
-        float* dst = data_ptr(c, d, par, c.rank, m) + r0;
-        dst[0] = v0;
-        dst[1] = v1;
+        unsigned long long* dst = data_ptr(c, d, epoch & 1, c.rank, m) + r0;
+        ll_put(dst, v0, epoch);
+        ll_put(dst + 1, v1, epoch);
       }
     }
   } else if constexpr (EPI == EPI_LMHEAD) {

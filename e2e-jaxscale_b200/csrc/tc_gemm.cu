@@ -31,7 +31,8 @@
 //
 // Across tensor-parallel ranks the row-parallel projection writes its summed
 // rank-local fp32 rows to the workspace and k_tc_rows_allreduce pushes them to
-// every peer (P2P stores), waits for the peers' flags and adds the residual.
+// every peer as epoch-tagged LL words (P2P stores, comm.cuh), sums the ranks'
+// words in rank order and adds the residual.
 //
 // No multicast anywhere.  Every mbarrier wait is time-bounded; on a timeout the
 // kernel sets its error word (jsx_device_error), the other roles of the CTA
@@ -429,7 +430,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
             t.part[(size_t)m * t.N + row0] = v0;
             t.part[(size_t)m * t.N + row0 + 1] = v1;
           } else {
-            const unsigned long long key = epi_pair<EPI>(a, c, false, 0, row0 >> 1, m, v0, v1);
+            const unsigned long long key = epi_pair<EPI>(a, c, false, 0u, row0 >> 1, m, v0, v1);
             if (EPI == EPI_LMHEAD && key) atomicMax(best + m, key);
           }
         }
@@ -493,30 +494,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
 
 // ---- row-parallel projection across ranks: NVLink all-reduce + residual --------
 // CTA b owns row pairs [p0, p1); pushes this rank's fp32 rows to every rank's
-// slot, releases its flag on every rank, waits for the peers' flags, sums the
-// slots in rank order and adds the residual (the GEMV kernels' protocol,
-// comm.cuh).
+// LL slots, then reads its rows from every rank's slots once they carry the
+// call's epoch, sums them in rank order and adds the residual (comm.cuh).
 __global__ void __launch_bounds__(256) k_tc_rows_allreduce(GemvArgs a, const float* __restrict__ part, CommDev c) {
   const int M = a.M, NB = a.N >> 1;
   const int p0 = (int)((long long)blockIdx.x * NB / gridDim.x);
   const int p1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
   const uint32_t epoch = read_epoch(c);
-  const int par = epoch & 1;
   for (int e = threadIdx.x; e < (p1 - p0) * M; e += blockDim.x) {
     const int m = e / (p1 - p0), g = p0 + (e - m * (p1 - p0));
     const float2 v = __ldcg(reinterpret_cast<const float2*>(part + (size_t)m * a.N + 2 * g));
-    epi_pair<EPI_ROWAR>(a, c, true, par, g, m, v.x, v.y);
+    epi_pair<EPI_ROWAR>(a, c, true, epoch, g, m, v.x, v.y);
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x < c.world) st_release_sys(flag_ptr(c, threadIdx.x, blockIdx.x, c.rank), epoch);
-  if (threadIdx.x < c.world) wait_flag(c, blockIdx.x, threadIdx.x, epoch);
-  __syncthreads();
   const int rows = 2 * (p1 - p0);
   for (int e = threadIdx.x; e < rows * M; e += blockDim.x) {
     const int m = e / rows, row = 2 * p0 + (e - (e / rows) * rows);
     float sum = 0.f;
-    for (int src = 0; src < c.world; ++src) sum += __ldcg(data_ptr(c, c.rank, par, src, m) + row);
+    for (int src = 0; src < c.world; ++src) sum += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
     bf16* hp = a.h + (size_t)m * a.N + row;
     *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(sum));
   }

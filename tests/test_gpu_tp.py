@@ -1,7 +1,8 @@
 """Tensor parallelism on 2 GPUs (skipped with fewer): one spawned process per
 GPU, jsx_comm over CUDA IPC, the fused row-parallel all-reduce and the
-vocab-sharded LM-head argmax checked against the oracle, a TP=2 model against
-the oracle's teacher-forced logits, and a peer that never arrives: the waiting
+vocab-sharded LM-head argmax checked against the oracle (GEMV and tensor-core
+forms), TP=2 models at batch 2 (whole-step kernel) and batch 6 (tensor-core
+projections) against the oracle's teacher-forced logits, and a peer that never arrives: the waiting
 rank's kernel gives up after the comm timeout, jsx_comm_check reports
 JSX_ETIMEDOUT and the context stays usable.  NVLS is off (NCCL_NVLS_ENABLE=0);
 the kernels use plain peer stores."""
@@ -117,6 +118,58 @@ def _worker(rank, world, port, q):
         model.comm.check()
         out["model_errs"] = errs
 
+        # (e) tensor-core row-parallel projection + all-reduce and LM head at 12 tokens
+        M2, K2, N2 = 12, 2048, 512
+        x2 = ref.bf16(rng.standard_normal((M2, K2)))
+        w2 = ref.bf16(rng.standard_normal((K2, N2)) * 0.02)
+        h2 = ref.bf16(rng.standard_normal((M2, N2)))
+        c4 = mesh.comm(32, N2, timeout_s=2.0)
+        tws = K.tc_workspace(M2, [(K2 // world, N2), (H, Vl)], dev)
+        hd2 = _bf(h2, dev)
+        K.tc_row_linear_allreduce(c4, _bf(ref.shard_columns(x2, world, rank), dev),
+                                  K.pack_transpose(_bf(ref.shard_rows(w2, world, rank), dev)), hd2, tws)
+        hh2 = ref.bf16(rng.standard_normal((M2, H)) * 2)
+        ids2 = torch.empty(M2, dtype=torch.int32, device=dev)
+        lg2 = torch.empty(M2, Vl, dtype=torch.bfloat16, device=dev)
+        K.tc_lmhead_argmax(c4, _bf(hh2, dev), None, 0.0, _bf(wl[rank * Vl:(rank + 1) * Vl], dev), rank * Vl, ids2,
+                           tws, lg2)
+        torch.cuda.synchronize()
+        c4.check()
+        want2 = ref.bf16(h2 + ref.row_parallel_reference([ref.shard_columns(x2, world, r) for r in range(world)],
+                                                          [ref.shard_rows(w2, world, r) for r in range(world)]))
+        got2 = hd2.float().cpu().numpy()
+        out["tc_ar_err"] = float(np.max(np.abs(got2 - want2)) / np.max(np.abs(want2)))
+        allh2 = [torch.empty_like(hd2.cpu()) for _ in range(world)]
+        dist.all_gather(allh2, hd2.cpu())
+        out["tc_ar_identical"] = all(torch.equal(allh2[0], t) for t in allh2)
+        parts2 = [torch.empty(M2, Vl) for _ in range(world)]
+        dist.all_gather(parts2, lg2.float().cpu())
+        out["tc_lm_ids"] = ids2.cpu().tolist()
+        out["tc_lm_ids_want"] = np.argmax(torch.cat(parts2, dim=1).numpy(), axis=-1).tolist()
+        c4.close()
+
+        # (f) TP=2 model at batch 6 (tensor-core projections), teacher-forced against the oracle
+        prompt6 = np.random.default_rng(2).integers(0, 1000, (6, 4))
+        rec6 = []
+        toks6 = ref.greedy_generate(params, prompt6, 3, max_cache_len=16, record=rec6)[:, 4:]
+        st6 = jsx.DecodeState(model, 6, 16, want_logits=True)
+        assert st6.tc
+        errs6 = []
+        for s in range(4):
+            st6.ids.copy_(torch.from_numpy(prompt6[:, s].astype(np.int32)))
+            model.step(st6, head=(s == 3))
+        for t in range(3):
+            parts = [torch.empty(6, 1000 // world) for _ in range(world)]
+            dist.all_gather(parts, st6.logits.float().cpu())
+            lg = torch.cat(parts, dim=1).numpy()
+            errs6.append(float(np.max(np.abs(lg - rec6[t][0])) / np.max(np.abs(rec6[t][0]))))
+            if t < 2:
+                st6.ids.copy_(torch.from_numpy(toks6[:, t].astype(np.int32)))
+                model.step(st6, head=True)
+        torch.cuda.synchronize()
+        model.comm.check()
+        out["tc_model_errs"] = errs6
+
         # (d) a peer that never arrives: rank 1 skips the call
         dist.barrier()
         c3 = jsx.mesh.Comm(rank, world, 8, 64, group=None, timeout_s=0.5)
@@ -163,5 +216,9 @@ def test_tensor_parallel_two_gpus():
         assert res[r]["ar_identical"]
         assert res[r]["lm_ids"] == res[r]["lm_ids_want"]
         assert max(res[r]["model_errs"]) <= 2e-2, res[r]["model_errs"]
+        assert res[r]["tc_ar_err"] <= 1e-2
+        assert res[r]["tc_ar_identical"]
+        assert res[r]["tc_lm_ids"] == res[r]["tc_lm_ids_want"]
+        assert max(res[r]["tc_model_errs"]) <= 2e-2, res[r]["tc_model_errs"]
     assert res[0]["timeout_status"] == 3  # JSX_ETIMEDOUT
     assert res[0]["after_timeout"] == 8 * 64.0
