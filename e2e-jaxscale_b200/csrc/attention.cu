@@ -25,7 +25,6 @@ namespace jsx {
 __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   pdl_wait();
-  pdl_launch_dependents();
   attn_item_any<kAttnThreads, false, false>(a, blockIdx.x, blockIdx.y, smem_raw);
 }
 

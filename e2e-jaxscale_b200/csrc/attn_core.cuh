@@ -105,6 +105,9 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int b, in
   __shared__ bool is_last;
   const int gi = a.gi, hd = a.hd, tid = threadIdx.x;
   const int stride = split_stride(gi, hd);
+  // the next kernel may launch once every item has reached this point (only
+  // the merges remain), not earlier: its CTAs would take SMs from later items
+  pdl_launch_dependents();
   __threadfence();
   __syncthreads();
   if (tid == 0) is_last = atomicAdd(a.cnt + vb, 1u) == (uint32_t)(a.splits - 1);

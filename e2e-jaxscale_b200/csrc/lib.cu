@@ -39,7 +39,7 @@ int sm_count() {
 int launch_flags() {
   if (g_launch_flags < 0) {
     const char* env = getenv("JSX_PDL");
-    g_launch_flags = (env && env[0] == '1') ? JSX_LAUNCH_PDL : 0;
+    g_launch_flags = (env && env[0] == '0') ? 0 : JSX_LAUNCH_PDL;
   }
   return g_launch_flags;
 }

@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kNormThreads) k_rmsnorm_vec(const bf16* __rest
   const uint4* gv = reinterpret_cast<const uint4*>(g);
   uint4* yr = reinterpret_cast<uint4*>(y + (size_t)blockIdx.x * hidden);
   pdl_wait();
+  pdl_launch_dependents();
   uint4 xv[kNormVec], gw[kNormVec];
 #pragma unroll
   for (int j = 0; j < kNormVec; ++j) {

@@ -318,16 +318,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   cl_sync_all();  // peers' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = misc[0];
+  // Programmatic dependent launch: the next kernel may start its own prologue
+  // (and weight stream) on SMs this grid frees.  Weights do not depend on the
+  // previous kernel; everything it writes (activations, residual, caches) is
+  // touched only after griddepcontrol.wait below.
+  pdl_launch_dependents();
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
     if (lane == 0) {
       tma_prefetch_map(&tw);
       tma_prefetch_map(&tx);
+      // the first ring of weight tiles goes out before the wait for the
+      // previous kernel; their activation tiles follow it
+      const int nkb = kb1 - kb0;
+      const int pre = ((int)cid < t.tiles) ? (nkb < kTcStages ? nkb : kTcStages) : 0;
+      for (int i = 0; i < pre; ++i) {
+        tc_expect_tx(full + i, kTcStageBytes);
+        tma_load_2d(smem + (size_t)i * kTcStageBytes, &tw, (kb0 + i) * kTcBK, (int)cid * kTcBM, full + i);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem + (size_t)i * kTcStageBytes + kTcABytes, &tx, (kb0 + i) * kTcBK, 0, full + i);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = cid; tile < t.tiles && ok; tile += ncl) {
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          if (it < (uint32_t)pre) continue;  // issued above
           const int s = it % kTcStages;
           if (it >= (uint32_t)kTcStages && !tc_wait(empty + s, ((it / kTcStages) - 1) & 1, abort_flag)) {
             ok = false;
@@ -385,6 +402,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     const int et = threadIdx.x - 64;
     const int r = 32 * q + lane;  // tile row held after tcgen05.ld
     const int pp0 = (int)(rank * 64 / S), np = (int)((rank + 1) * 64 / S) - pp0;  // row pairs finished here
+    pdl_wait();  // the epilogue reads and writes what earlier kernels use
     uint32_t ai = 0;
     for (int tile = cid; tile < t.tiles; tile += ncl, ++ai) {
       const uint32_t b = ai & 1;
@@ -443,6 +461,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
   }
 
   // ---------------- teardown ----------------
+  pdl_wait();
   tc_fence_before();
   __syncthreads();
   cl_sync_all();  // no CTA leaves while a peer may still read its exchange buffers
@@ -497,6 +516,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
 // LL slots, then reads its rows from every rank's slots once they carry the
 // call's epoch, sums them in rank order and adds the residual (comm.cuh).
 __global__ void __launch_bounds__(256) k_tc_rows_allreduce(GemvArgs a, const float* __restrict__ part, CommDev c) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int M = a.M, NB = a.N >> 1;
   const int p0 = (int)((long long)blockIdx.x * NB / gridDim.x);
   const int p1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
@@ -561,18 +582,22 @@ static int make_map(CUtensorMap* map, const void* base, int rows, int K, int box
   return JSX_OK;
 }
 
-static cudaLaunchConfig_t tc_config(int grid, int S, cudaStream_t s, cudaLaunchAttribute* attr) {
+// Cluster launch of k_tc_gemm; programmatic dependent launch when the
+// library's launch flags ask for it (attr holds 2 entries).
+static cudaLaunchConfig_t tc_config(int grid, int S, cudaStream_t s, cudaLaunchAttribute* attr, bool pdl) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = kTcSmem;
   cfg.stream = s;
-  attr->id = cudaLaunchAttributeClusterDimension;
-  attr->val.clusterDim.x = S;
-  attr->val.clusterDim.y = 1;
-  attr->val.clusterDim.z = 1;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl ? 2 : 1;
   return cfg;
 }
 
@@ -590,8 +615,8 @@ static int max_clusters(int S) {
   if (cache[dev][S] == 0) {
     int n = 0;
     auto kern = k_tc_gemm<EPI_LINEAR>;
-    cudaLaunchAttribute attr;
-    cudaLaunchConfig_t cfg = tc_config(S, S, nullptr, &attr);
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = tc_config(S, S, nullptr, attr, false);
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem) != cudaSuccess ||
         cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n < 1) {
       cudaGetLastError();
@@ -680,15 +705,14 @@ static int tc_run(jsx_comm* comm, GemvArgs ga, void* workspace, size_t workspace
   ta.trace = g_trace_buf;
   auto kern = k_tc_gemm<EPI>;
   JSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTcSmem));
-  cudaLaunchAttribute attr;
-  const cudaLaunchConfig_t cfg = tc_config(p.clusters * p.S, p.S, s, &attr);
+  cudaLaunchAttribute attr[2];
+  const cudaLaunchConfig_t cfg = tc_config(p.clusters * p.S, p.S, s, attr, (launch_flags() & JSX_LAUNCH_PDL) != 0);
   JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, tw, tx, ta, ga, c));
   if (across_ranks) {
     int rgrid = 2 * sm_count();
     if (rgrid > kMaxCtas) rgrid = kMaxCtas;
     if (rgrid > ga.N / 2) rgrid = ga.N / 2;
-    k_tc_rows_allreduce<<<rgrid, 256, 0, s>>>(ga, ta.part, c);
-    JSX_LAUNCHED("k_tc_rows_allreduce");
+    JSX_CUDA(launch_kernel(k_tc_rows_allreduce, dim3(rgrid), dim3(256), 0, s, ga, ta.part, c));
   }
   return JSX_OK;
 }

@@ -47,8 +47,8 @@ const char* jsx_last_error(void);
 int jsx_device_sm_count(int* out);
 /* Launch flags for every later launch of this process.  JSX_LAUNCH_PDL (1):
  * programmatic dependent launch — each kernel streams its first weight tiles
- * while the previous kernel in the stream drains (default: the JSX_PDL
- * environment variable, "1" = on).  No reference counterpart (XLA schedules
+ * while the previous kernel in the stream drains (default on; the JSX_PDL
+ * environment variable "0" turns it off).  No reference counterpart (XLA schedules
  * its own fusions). */
 #define JSX_LAUNCH_PDL 1
 int jsx_set_launch_flags(int flags);

@@ -104,12 +104,15 @@ def test_graph_replay_matches_eager(jsx, ref, cuda):
     assert np.array_equal(out[:, :6], prompt)
 
 
-def test_pdl_launches_match(jsx, ref, cuda):
+@pytest.mark.parametrize("B", [1, 6])
+def test_pdl_launches_match(jsx, ref, cuda, B):
+    """Programmatic dependent launch changes only when kernels start, not what they
+    compute: the whole-step kernel (batch 1) and the tensor-core chain (batch 6)."""
     rc = small_cfg(ref)
     params = ref.init_params(rc, seed=4)
     model = jsx.GLM4ForCausalLM(to_model_config(jsx, rc), jsx.create_mesh(1))
     model.load_state(params)
-    prompt = np.random.default_rng(6).integers(0, rc.vocab_size, (1, 5))
+    prompt = np.random.default_rng(6).integers(0, rc.vocab_size, (B, 5))
     K = jsx.kernels
     prev = K.pdl_enabled()
     try:
