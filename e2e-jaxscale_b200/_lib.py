@@ -63,6 +63,9 @@ SIGNATURES = {
     "jsx_tc_row_linear_allreduce": [P, P, P, P, I, I, I, P, SZ, P],
     "jsx_tc_lmhead_argmax": [P, P, P, F, P, I, I, I, I, P, P, P, SZ, P],
     "jsx_moe_gate": [P, P, P, P, P, I, I, I, I, F, I, P],
+    "jsx_moe_experts_workspace_size": [I, I, I, I, I, P],
+    "jsx_moe_experts": [P, P, P, P, I, I, I, I, I, I, P, P, P, P, SZ, P],
+    "jsx_row_linear_allreduce_add": [P, P, P, P, P, I, I, I, P],
     "jsx_decode_step_workspace_size": [P, P],
     "jsx_decode_step": [P, P, P],
     "jsx_comm_create": [I, I, I, I, U64, P],

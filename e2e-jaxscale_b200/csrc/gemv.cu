@@ -100,7 +100,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
       if (lane < kRows * M) {
         const int r = lane / M, m = lane - (lane / M) * M;
         const int row = g * kRows + r;
-        const float v = pick<M>(acc, r, m);
+        float v = pick<M>(acc, r, m);
+        if (a.addend) v += ldbf(a.addend + (size_t)m * a.N + row);
         if (!multi) {
           bf16* hp = a.h + (size_t)m * a.N + row;
           *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(v));
@@ -718,13 +719,15 @@ extern "C" int jsx_gate_up_swiglu(const void* h, const void* ln_gamma, float eps
   return launch_gemv<EPI_SWIGLU>(a, c, (cudaStream_t)stream, 1 << 30);
 }
 
-extern "C" int jsx_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h,
-                                        int M, int K_local, int N, void* stream) {
+extern "C" int jsx_row_linear_allreduce_add(jsx_comm* comm, const void* x, const void* w_nk,
+                                            const void* addend, void* h, int M, int K_local, int N,
+                                            void* stream) {
   int st = check_common(x, w_nk, M, K_local, N);
   if (st) return st;
   JSX_REQUIRE(h != nullptr, "null residual");
   GemvArgs a = {};
   a.x = (const bf16*)x; a.w = (const bf16*)w_nk; a.M = M; a.K = K_local; a.N = N; a.h = (bf16*)h;
+  a.addend = (const bf16*)addend;
   CommDev c = {};
   c.world = 1;
   if (comm) {
@@ -734,6 +737,11 @@ extern "C" int jsx_row_linear_allreduce(jsx_comm* comm, const void* x, const voi
                 "M=%d N=%d exceed the comm buffer (%d tokens x %d)", M, N, c.max_tokens, c.hidden);
   }
   return launch_gemv<EPI_ROWAR>(a, c, (cudaStream_t)stream, kMaxCtas);
+}
+
+extern "C" int jsx_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h,
+                                        int M, int K_local, int N, void* stream) {
+  return jsx_row_linear_allreduce_add(comm, x, w_nk, nullptr, h, M, K_local, N, stream);
 }
 
 extern "C" int jsx_lmhead_workspace_size(int M, size_t* bytes) {

@@ -37,6 +37,7 @@ struct GemvArgs {
   int nq, nkv, hd, rot, max_seq, tps;
   // EPI_ROWAR
   bf16* h;            // residual [M][N]
+  const bf16* addend; // [M][N] added to this rank's partial before the all-reduce, or null
   // EPI_LMHEAD
   int vocab_offset;
   unsigned long long* keys;  // [M] workspace (zero on entry, left zero)
@@ -259,6 +260,10 @@ __device__ __forceinline__ unsigned long long epi_pair(const GemvArgs& a, const 
   } else if constexpr (EPI == EPI_SWIGLU) {
     swiglu_store(a, g, m, v0, v1);
   } else if constexpr (EPI == EPI_ROWAR) {
+    if (a.addend) {
+      v0 += ldbf(a.addend + (size_t)m * a.N + r0);
+      v1 += ldbf(a.addend + (size_t)m * a.N + r0 + 1);
+    }
     if (!multi) {
       bf16* hp = a.h + (size_t)m * a.N + r0;
       hp[0] = __float2bfloat16_rn(__bfloat162float(hp[0]) + rbf(v0));

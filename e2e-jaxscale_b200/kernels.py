@@ -281,6 +281,41 @@ def tc_lmhead_argmax(comm, h, norm_gamma, eps, w_vocab, vocab_offset, ids_out, w
          vocab_offset, M, H, _p(logits_out), _p(ids_out), _p(workspace), workspace.numel(), _stream())
 
 
+def row_linear_allreduce_add(comm, x, w_nk, addend, h):
+    """h = bf16(h + bf16(sum over ranks of (x_r @ W_r + addend_r))); addend may be None."""
+    _need(x, "x")
+    _need(w_nk, "w_nk")
+    _opt(addend, "addend")
+    _need(h, "h")
+    N, K_ = w_nk.shape
+    M = x.numel() // K_
+    handle = None if comm is None else comm.handle
+    call("jsx_row_linear_allreduce_add", handle, _p(x), _p(w_nk), _p(addend), _p(h), M, K_, N, _stream())
+
+
+def moe_workspace(N, K_, E, H, I, device) -> torch.Tensor:
+    n = ctypes.c_size_t(0)
+    call("jsx_moe_experts_workspace_size", N, K_, E, H, I, ctypes.byref(n))
+    return torch.zeros(n.value, dtype=torch.uint8, device=device)
+
+
+def moe_experts(x, topk_w, topk_idx, w_gu, w_d, out, workspace, owner=None, rank=0):
+    """Routed partial of this rank's experts (include/jsx.h jsx_moe_experts).
+    w_gu [E, 2I, H] (packed per expert), w_d [E, H, I]; owner: int32 [E] device tensor or None."""
+    _need(x, "x")
+    _need(topk_w, "topk_w")
+    _need(topk_idx, "topk_idx", torch.int32)
+    _need(w_gu, "w_gu")
+    _need(w_d, "w_d")
+    _need(out, "out")
+    _need(workspace, "workspace", torch.uint8)
+    _opt(owner, "owner", torch.int32)
+    N, H = x.shape
+    E, I2, _ = w_gu.shape
+    call("jsx_moe_experts", _p(x), _p(topk_w), _p(topk_idx), _p(owner), rank, N, topk_idx.shape[1], E, H,
+         I2 // 2, _p(w_gu), _p(w_d), _p(out), _p(workspace), workspace.numel(), _stream())
+
+
 def moe_gate(x, w_nk, k, scale, norm=True, correction_bias=None, logits_given=False):
     """Router of layers/moe.py:54-79.  With logits_given, x holds bf16 logits [N, E]."""
     _need(x, "x")

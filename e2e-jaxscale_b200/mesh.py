@@ -131,6 +131,44 @@ class Mesh:
                                     group=self.group("tensor"), timeout_s=timeout_s)
         return self._comms[key]
 
+    @property
+    def moe_rank(self) -> int:
+        """Index of this rank among the expert x tensor ranks of its data replica."""
+        return self.coords.get("expert", 0) * self.tp + self.coords["tensor"]
+
+    @property
+    def moe_world(self) -> int:
+        return self.ep * self.tp
+
+    def comm_moe(self, max_tokens: int, hidden: int, timeout_s: float = 5.0) -> Comm | None:
+        """Comm over the expert x tensor ranks of this data replica (None for one rank):
+        the MoE layer's single exchange (psum over "expert" and the shared expert's
+        tensor all-reduce, layers/moe.py:230 and :110-113)."""
+        if self.moe_world == 1:
+            return None
+        key = ("moe", max_tokens, hidden)
+        if key not in self._comms:
+            self._comms[key] = Comm(self.moe_rank, self.moe_world, max_tokens, hidden,
+                                    group=self.group_moe(), timeout_s=timeout_s)
+        return self._comms[key]
+
+    def group_moe(self):
+        """torch.distributed group of the expert x tensor ranks sharing this rank's data index."""
+        if "moe" in self._groups:
+            return self._groups["moe"]
+        if not dist.is_initialized() or self.moe_world == 1:
+            self._groups["moe"] = None
+            return None
+        mine = None
+        span = self.ep * self.tp
+        for d in range(self.dp):
+            ranks = list(range(d * span, (d + 1) * span))
+            g = dist.new_group(ranks)
+            if self.rank in ranks:
+                mine = g
+        self._groups["moe"] = mine
+        return mine
+
     def close(self) -> None:
         for c in self._comms.values():
             c.close()

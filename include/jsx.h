@@ -145,6 +145,13 @@ int jsx_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_ca
  * single rank (TP=1). */
 int jsx_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h,
                              int M, int K_local, int N, void* stream);
+/* The same with a per-rank addend[M][N] (bf16, may be NULL) summed into this
+ * rank's fp32 partial before the all-reduce: h = bf16(h + bf16(sum over ranks
+ * of (x_r @ W_r + addend_r))).  The MoE layer passes its routed-expert partial
+ * here, so the reference's psum("expert") (layers/moe.py:230) and the shared
+ * expert's tensor-parallel all-reduce (layers/moe.py:110-113) are one exchange. */
+int jsx_row_linear_allreduce_add(jsx_comm* comm, const void* x, const void* w_nk, const void* addend,
+                                 void* h, int M, int K_local, int N, void* stream);
 
 /* Final norm + LM head + greedy argmax (models/glm4.py:193, :251-252,
  * layers/embedding.py:79-92, runner.py:281/:297).  The vocabulary is
@@ -252,6 +259,19 @@ int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args, void* stre
  * weights = uncorrected probabilities renormalised (+1e-20) when norm != 0,
  * times scale, rounded to bf16.  x[N][H], w_nk[E][H], topk_w[N][k] bf16,
  * topk_idx[N][k] int32.  E <= 256, k <= 8. */
+/* MoE experts of one rank (layers/moe.py:194-267, _forward_ep / _topk_local_forward):
+ * x[N][H] normalised hidden states, topk_w[N][K] bf16 and topk_idx[N][K] from
+ * jsx_moe_gate; expert_owner[E] (device int32) names the rank that computes each
+ * expert (NULL: this rank computes all).  w_gate_up [E][2I][H] (per expert
+ * jsx_pack_gate_up), w_down [E][H][I] (per expert jsx_pack_transpose).
+ * out[N][H] = this rank's routed partial: per token, k = 0..K-1 in order over
+ * the owned experts, out = bf16(out + bf16(bf16(silu(x Wg) * (x Wu)) Wd * w_k)).
+ * N <= 32, K <= 8, E <= 256; workspace of jsx_moe_experts_workspace_size bytes. */
+int jsx_moe_experts_workspace_size(int N, int K, int E, int H, int I, size_t* bytes);
+int jsx_moe_experts(const void* x, const void* topk_w, const int32_t* topk_idx,
+                    const int32_t* expert_owner, int rank, int N, int K, int E, int H, int I,
+                    const void* w_gate_up, const void* w_down, void* out, void* workspace,
+                    size_t workspace_bytes, void* stream);
 int jsx_moe_gate(const void* x, const void* w_nk, const float* correction_bias, void* topk_w,
                  int32_t* topk_idx, int N, int H, int E, int k, float scale, int norm,
                  void* stream);

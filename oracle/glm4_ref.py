@@ -351,3 +351,36 @@ def moe_gate(x, w, k, scale, norm=True, correction_bias=None):
         wts = wts / (wts.sum(axis=-1, keepdims=True, dtype=np.float32) + np.float32(1e-20))
     wts = wts * np.float32(scale)
     return bf16(wts), idx
+
+
+# ---------------------------------------------------------------------------
+# MoE experts (layers/moe.py:247-267) and the MoE layer (layers/moe.py:156-192)
+# ---------------------------------------------------------------------------
+
+def moe_experts(x, tk_w, tk_i, gate_w, up_w, down_w):
+    """_topk_local_forward (layers/moe.py:247-267): for k = 0..K-1 in order, each
+    token's k-th expert SwiGLU with bf16 einsums (fp32 accumulate), then
+    output = bf16(output + bf16(expert_out * w_k)).  x [N, H], tk_w [N, K] bf16,
+    tk_i [N, K], gate_w/up_w [E, H, I], down_w [E, I, H]."""
+    x = bf16(x)
+    N, H = x.shape
+    out = np.zeros((N, H), np.float32)
+    for k in range(tk_i.shape[1]):
+        ids = np.asarray(tk_i[:, k])
+        g = bf16(np.einsum("nh,nhi->ni", x, np.asarray(gate_w, np.float32)[ids], dtype=np.float32))
+        u = bf16(np.einsum("nh,nhi->ni", x, np.asarray(up_w, np.float32)[ids], dtype=np.float32))
+        act = bf16(silu(g) * u)
+        eo = bf16(np.einsum("ni,nih->nh", act, np.asarray(down_w, np.float32)[ids], dtype=np.float32))
+        out = bf16(out + bf16(eo * np.asarray(tk_w[:, k:k + 1], np.float32)))
+    return out
+
+
+def moe_layer(x, router_w, correction_bias, k, scale, norm, gate_w, up_w, down_w, sh_g, sh_u, sh_d):
+    """MoELayer.__call__ without expert parallelism (layers/moe.py:156-192): router,
+    routed experts, shared SwiGLU expert (layers/moe.py:110-113), bf16 sum."""
+    lead = x.shape[:-1]
+    xf = bf16(x).reshape(-1, x.shape[-1])
+    w, i = moe_gate(xf, router_w, k, scale, norm, correction_bias)
+    routed = moe_experts(xf, w, i, gate_w, up_w, down_w)
+    shared = linear(bf16(silu(linear(xf, sh_g)) * linear(xf, sh_u)), sh_d)
+    return bf16(routed + shared).reshape(*lead, -1)

@@ -1,5 +1,6 @@
 """Generates tests/golden/reference_golden.npz by executing the REFERENCE's own
-source files (layers/*.py, models/glm4.py, runner.py of sdh1014/e2e-JaxScale)
+source files (layers/*.py incl. the MoE layer, models/glm4.py, runner.py of
+sdh1014/e2e-JaxScale)
 on the CPU through the numpy stand-in under tests/golden/jaxshim/ (JAX and Flax
 are not installable here).  The fixture pins the oracle (oracle/glm4_ref.py)
 to the reference's composition of operations: where it rounds to bf16, adds
@@ -153,6 +154,31 @@ def main():
                     kv_caches=kv, cache_position=np.array([7], np.int32))
     out.update(model_prompt=prompt, model_gen=np.asarray(gen), model_prefill_logits=lg[:, -1],
                model_decode_logits=lg2[:, -1], model_params_sha256=np.array(params_checksum(p)))
+
+    # MoELayer without expert parallelism (layers/moe.py:156-192, _topk_local_forward
+    # :247-267, SharedExpertMLP :110-113), 8 experts, top-4.  A mesh object whose
+    # "expert" axis has size 1 selects the local path.
+    from jax.sharding import Mesh
+    from layers.moe import MoELayer  # reference
+    mesh1 = Mesh()
+    mesh1.shape = {"expert": 1}
+    E, Hm, Im, Is = 8, 128, 64, 64
+    moe = MoELayer(Hm, Im, Is, E, 4, 1.8, True, mesh1, dtype=BF)
+    moe.gate.weight.weight.value = rnd((Hm, E), 0.05)
+    moe.gate.e_score_correction_bias.value = (rng.standard_normal(E).astype(np.float32) * np.float32(1e-3))
+    moe.expert_gate_weight.value = rnd((E, Hm, Im), 0.05)
+    moe.expert_up_weight.value = rnd((E, Hm, Im), 0.05)
+    moe.expert_down_weight.value = rnd((E, Im, Hm), 0.05)
+    moe.shared_experts.gate_proj.weight.value = rnd((Hm, Is), 0.05)
+    moe.shared_experts.up_proj.weight.value = rnd((Hm, Is), 0.05)
+    moe.shared_experts.down_proj.weight.value = rnd((Is, Hm), 0.05)
+    xm = rnd((2, 5, Hm))
+    out.update(moel_x=xm, moel_router=moe.gate.weight.weight.value,
+               moel_bias=moe.gate.e_score_correction_bias.value,
+               moel_eg=moe.expert_gate_weight.value, moel_eu=moe.expert_up_weight.value,
+               moel_ed=moe.expert_down_weight.value, moel_sg=moe.shared_experts.gate_proj.weight.value,
+               moel_su=moe.shared_experts.up_proj.weight.value, moel_sd=moe.shared_experts.down_proj.weight.value,
+               moel_y=moe(xm))
 
     ser = {}
     for k_, v in out.items():

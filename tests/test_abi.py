@@ -80,3 +80,13 @@ def test_tc_workspace_size(jsx):
     assert n.value == 1024 + 7168 + 3 * 8 * 4      # 32 x 100 x 2 = 6400 -> 7168
     with pytest.raises(lib.JsxError):
         lib.call("jsx_tc_workspace_size", 0, 64, 64, ctypes.byref(n))
+
+
+def test_moe_experts_workspace_and_limits(jsx):
+    lib = jsx._lib
+    n = ctypes.c_size_t(0)
+    lib.call("jsx_moe_experts_workspace_size", 32, 4, 64, 2048, 1536, ctypes.byref(n))
+    P = 32 * 4
+    assert n.value >= 65 * 4 + 3 * P * 4 + P * 1536 * 2 + P * 2048 * 2
+    with pytest.raises(lib.JsxError):   # 33 tokens per call
+        lib.call("jsx_moe_experts", 1, 1, 1, None, 0, 33, 4, 64, 2048, 1536, 1, 1, 1, 1, 1 << 30, None)

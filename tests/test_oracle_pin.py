@@ -82,3 +82,11 @@ def test_greedy_generation_and_logits(ref, g):
     assert np.array_equal(gen, g["model_gen"])
     same(record[0][0], g["model_prefill_logits"])
     same(record[1][0], g["model_decode_logits"])
+
+
+def test_moe_layer(ref, g):
+    """MoELayer without expert parallelism: router, top-4 experts accumulated in k
+    order in bf16 (_topk_local_forward), shared SwiGLU expert, bf16 sum."""
+    y = ref.moe_layer(g["moel_x"], g["moel_router"], g["moel_bias"], 4, 1.8, True, g["moel_eg"], g["moel_eu"],
+                      g["moel_ed"], g["moel_sg"], g["moel_su"], g["moel_sd"])
+    same(y, g["moel_y"])
