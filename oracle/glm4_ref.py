@@ -384,3 +384,55 @@ def moe_layer(x, router_w, correction_bias, k, scale, norm, gate_w, up_w, down_w
     routed = moe_experts(xf, w, i, gate_w, up_w, down_w)
     shared = linear(bf16(silu(linear(xf, sh_g)) * linear(xf, sh_u)), sh_d)
     return bf16(routed + shared).reshape(*lead, -1)
+
+
+# ---------------------------------------------------------------------------
+# MLA attention (layers/mla_attention.py:101-193), expanded per-head cache
+# ---------------------------------------------------------------------------
+
+@dataclass
+class MLAParams:
+    q_a: np.ndarray        # [H, q_lora]
+    q_a_ln: np.ndarray     # [q_lora]
+    q_b: np.ndarray        # [q_lora, nh * (nope + rope)]
+    kv_a: np.ndarray       # [H, kv_lora + rope]
+    kv_a_ln: np.ndarray    # [kv_lora]
+    kv_b: np.ndarray       # [kv_lora, nh * (nope + v)]
+    o: np.ndarray          # [nh * v, H]
+
+
+def mla_attention(p: MLAParams, x, positions, mask, kv, cache_position, nh, nope, rope_d, vdim, eps,
+                  inv_freq):
+    """MLAAttention.__call__: low-rank q (q_a -> RMSNorm -> q_b) and kv (kv_a -> split
+    latent | shared rope key -> RMSNorm on the latent -> kv_b), neox RoPE on the rope
+    slice of q and on the shared key (broadcast to every head), concatenation, cache
+    write, scores = bf16(bf16(q k^T) * scale) + mask, fp32 softmax, bf16
+    probabilities, bf16(P v), o_proj.  x [B, S, H]; kv = (k [B, L, nh, nope+rope],
+    v [B, L, nh, vdim]) updated in place; returns the output [B, S, H]."""
+    B, S, _ = x.shape
+    kv_lora = p.kv_a_ln.shape[0]
+    qc = rmsnorm(linear(x, p.q_a), p.q_a_ln, eps)
+    q = linear(qc, p.q_b).reshape(B, S, nh, nope + rope_d)
+    kvc = linear(x, p.kv_a)
+    kv_lat, k_rope_sh = kvc[..., :kv_lora], kvc[..., kv_lora:]
+    kvb = linear(rmsnorm(kv_lat, p.kv_a_ln, eps), p.kv_b).reshape(B, S, nh, nope + vdim)
+    k_nope, v = kvb[..., :nope], kvb[..., nope:]
+    k_rope = np.broadcast_to(k_rope_sh[:, :, None, :], (B, S, nh, rope_d))
+    qr, kr = rope(np.asarray(positions).reshape(-1), q[..., nope:].reshape(-1, nh, rope_d),
+                  k_rope.reshape(-1, nh, rope_d), inv_freq)
+    q = np.concatenate([q[..., :nope], qr.reshape(B, S, nh, rope_d)], axis=-1)
+    k = np.concatenate([k_nope, kr.reshape(B, S, nh, rope_d)], axis=-1)
+    kc, vc = kv
+    start = min(max(int(np.asarray(cache_position)[0]), 0), kc.shape[1] - S)
+    kc[:, start:start + S] = k
+    vc[:, start:start + S] = v
+    scale = np.float32((nope + rope_d) ** -0.5)
+    scores = bf16(np.einsum("bshd,blhd->bhsl", q, kc, dtype=np.float32))
+    scores = bf16(scores * scale)
+    if mask is not None:
+        scores = bf16(scores + np.asarray(mask, np.float32))
+    m = scores.max(axis=-1, keepdims=True)
+    e = np.exp(scores - m)
+    probs = bf16(e / e.sum(axis=-1, keepdims=True, dtype=np.float32))
+    out = bf16(np.einsum("bhsl,blhd->bshd", probs, vc, dtype=np.float32)).reshape(B, S, nh * vdim)
+    return linear(out, p.o)

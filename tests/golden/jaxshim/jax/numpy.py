@@ -60,3 +60,14 @@ def einsum(spec, *ops, preferred_element_type=None, precision=None):
     out_dtype = _np.result_type(*[o.dtype for o in ops])
     r = _np.einsum(spec, *[_np.asarray(o, _np.float32) for o in ops], dtype=_np.float32)
     return r.astype(preferred_element_type or out_dtype)
+
+
+transpose = _np.transpose
+swapaxes = _np.swapaxes
+
+
+def matmul(a, b, preferred_element_type=None, precision=None):
+    """jnp.matmul on bf16 operands: fp32-accumulated product, result in the operands' dtype."""
+    out_dtype = _np.result_type(a.dtype, b.dtype)
+    r = _np.matmul(_np.asarray(a, _np.float32), _np.asarray(b, _np.float32))
+    return r.astype(preferred_element_type or out_dtype)

@@ -180,6 +180,28 @@ def main():
                moel_su=moe.shared_experts.up_proj.weight.value, moel_sd=moe.shared_experts.down_proj.weight.value,
                moel_y=moe(xm))
 
+    # MLAAttention (layers/mla_attention.py): prefill into an expanded per-head cache,
+    # then one decode step; 4 heads, q_lora 96, kv_lora 64, nope 48 + rope 16, v 64.
+    from layers.mla_attention import MLAAttention  # reference
+    mla = MLAAttention(256, 4, 96, 64, 48, 16, 64, 4096, 1000000.0, eps, None, dtype=BF)
+    for name, shp in {"q_a_proj": (256, 96), "q_b_proj": (96, 4 * 64), "kv_a_proj_with_mqa": (256, 64 + 16),
+                      "kv_b_proj": (64, 4 * (48 + 64)), "o_proj": (4 * 64, 256)}.items():
+        getattr(mla, name).weight.value = rnd(shp, 0.05)
+        out[f"mla_{name}"] = getattr(mla, name).weight.value
+    mla.q_a_layernorm.scale.value = rnd((96,), 1.0)
+    mla.kv_a_layernorm.scale.value = rnd((64,), 1.0)
+    out.update(mla_q_a_ln=mla.q_a_layernorm.scale.value, mla_kv_a_ln=mla.kv_a_layernorm.scale.value)
+    B, S, L = 2, 5, 12
+    hm = rnd((B, S, 256))
+    from layers.kv_cache import KVCache  # reference
+    cache = KVCache(k=np.zeros((B, L, 4, 64), BF), v=np.zeros((B, L, 4, 64), BF))
+    ym, cm = mla(hm, runner.make_positions(S, B), runner.make_prefill_mask(S, L, dtype=BF), kv_cache=cache,
+                 cache_position=np.arange(S, dtype=np.int32))
+    hm2 = rnd((B, 1, 256))
+    ym2, cm2 = mla(hm2, np.full((B, 1), S, np.int32), runner.make_decode_mask(S, L, dtype=BF), kv_cache=cm,
+                   cache_position=np.array([S], np.int32))
+    out.update(mla_h=hm, mla_y=ym, mla_h2=hm2, mla_y2=ym2, mla_k=cm2.k, mla_v=cm2.v)
+
     ser = {}
     for k_, v in out.items():
         v = np.asarray(v)

@@ -2,7 +2,8 @@
 GPU, jsx_comm over CUDA IPC, the fused row-parallel all-reduce and the
 vocab-sharded LM-head argmax checked against the oracle (GEMV and tensor-core
 forms), TP=2 models at batch 2 (whole-step kernel) and batch 6 (tensor-core
-projections) against the oracle's teacher-forced logits, and a peer that never arrives: the waiting
+projections) against the oracle's teacher-forced logits, an expert-parallel MoE
+layer (EP=2) against the oracle's MoELayer, and a peer that never arrives: the waiting
 rank's kernel gives up after the comm timeout, jsx_comm_check reports
 JSX_ETIMEDOUT and the context stays usable.  NVLS is off (NCCL_NVLS_ENABLE=0);
 the kernels use plain peer stores."""
@@ -170,6 +171,37 @@ def _worker(rank, world, port, q):
         model.comm.check()
         out["tc_model_errs"] = errs6
 
+        # (g) MoE layer with expert parallelism over the 2 ranks (EP=2, TP=1): each rank
+        #     computes its experts; the routed partials and the shared expert's halves meet in
+        #     one all-reduce.  Against the oracle's MoELayer (no EP) on the same inputs.
+        moe_mod = importlib.import_module("e2e-jaxscale_b200.layers.moe")
+        mesh_ep = jsx.create_mesh(tp=1, ep=world)
+        Em, Hm, Im, Ism = 16, 256, 128, 256
+        r2 = np.random.default_rng(5)
+        pm = {n: ref.bf16(r2.standard_normal(shp, dtype=np.float32) * np.float32(0.05)) for n, shp in
+              dict(router=(Hm, Em), eg=(Em, Hm, Im), eu=(Em, Hm, Im), ed=(Em, Im, Hm), sg=(Hm, Ism),
+                   su=(Hm, Ism), sd=(Ism, Hm)).items()}
+        layer = moe_mod.MoELayer(Hm, Im, Ism, Em, 4, 1.8, True, mesh_ep)
+        layer.gate.weight.weight.value = pm["router"]
+        layer.expert_gate_weight.value, layer.expert_up_weight.value = pm["eg"], pm["eu"]
+        layer.expert_down_weight.value = pm["ed"]
+        layer.shared_experts.gate_proj.weight.value = pm["sg"]
+        layer.shared_experts.up_proj.weight.value = pm["su"]
+        layer.shared_experts.down_proj.weight.value = pm["sd"]
+        xm = ref.bf16(r2.standard_normal((1, 6, Hm), dtype=np.float32))
+        ym = layer(_bf(xm, dev))
+        torch.cuda.synchronize()
+        mesh_ep.comm_moe(K.MAX_DECODE_TOKENS, Hm).check()
+        wantm = ref.moe_layer(xm, pm["router"], None, 4, 1.8, True, pm["eg"], pm["eu"], pm["ed"], pm["sg"],
+                              pm["su"], pm["sd"])
+        gm = ym.float().cpu().numpy()
+        out["moe_err"] = float(np.max(np.abs(gm - wantm)) / np.max(np.abs(wantm)))
+        out["moe_cos"] = float(np.sum(gm * wantm) / (np.linalg.norm(gm) * np.linalg.norm(wantm)))
+        allm = [torch.empty_like(ym.cpu()) for _ in range(world)]
+        dist.all_gather(allm, ym.cpu())
+        out["moe_identical"] = all(torch.equal(allm[0], t) for t in allm)
+        mesh_ep.close()
+
         # (d) a peer that never arrives: rank 1 skips the call
         dist.barrier()
         c3 = jsx.mesh.Comm(rank, world, 8, 64, group=None, timeout_s=0.5)
@@ -220,5 +252,7 @@ def test_tensor_parallel_two_gpus():
         assert res[r]["tc_ar_identical"]
         assert res[r]["tc_lm_ids"] == res[r]["tc_lm_ids_want"]
         assert max(res[r]["tc_model_errs"]) <= 2e-2, res[r]["tc_model_errs"]
+        assert res[r]["moe_err"] <= 2e-2 and res[r]["moe_cos"] >= 0.999, (res[r]["moe_err"], res[r]["moe_cos"])
+        assert res[r]["moe_identical"]
     assert res[0]["timeout_status"] == 3  # JSX_ETIMEDOUT
     assert res[0]["after_timeout"] == 8 * 64.0

@@ -90,3 +90,24 @@ def test_moe_layer(ref, g):
     y = ref.moe_layer(g["moel_x"], g["moel_router"], g["moel_bias"], 4, 1.8, True, g["moel_eg"], g["moel_eu"],
                       g["moel_ed"], g["moel_sg"], g["moel_su"], g["moel_sd"])
     same(y, g["moel_y"])
+
+
+def test_mla_attention_prefill_then_decode(ref, g):
+    """MLAAttention: low-rank q/kv with latent RMSNorms, RoPE on the rope slice and the
+    shared key, expanded per-head cache, bf16 scores, fp32 softmax."""
+    p = ref.MLAParams(q_a=g["mla_q_a_proj"], q_a_ln=g["mla_q_a_ln"], q_b=g["mla_q_b_proj"],
+                      kv_a=g["mla_kv_a_proj_with_mqa"], kv_a_ln=g["mla_kv_a_ln"], kv_b=g["mla_kv_b_proj"],
+                      o=g["mla_o_proj"])
+    B, S, L = 2, 5, 12
+    kc = np.zeros((B, L, 4, 64), np.float32)
+    vc = np.zeros((B, L, 4, 64), np.float32)
+    inv = ref.rope_inv_freq(16, theta=1000000.0, partial=1.0)
+    pos = np.broadcast_to(np.arange(S), (B, S))
+    y = ref.mla_attention(p, g["mla_h"], pos, ref.make_prefill_mask(S, L), (kc, vc), np.arange(S), 4, 48, 16, 64,
+                          1.5625e-07, inv)
+    same(y, g["mla_y"])
+    y2 = ref.mla_attention(p, g["mla_h2"], np.full((B, 1), S), ref.make_decode_mask(S, L), (kc, vc), [S], 4, 48,
+                           16, 64, 1.5625e-07, inv)
+    same(y2, g["mla_y2"])
+    same(kc, g["mla_k"])
+    same(vc, g["mla_v"])
