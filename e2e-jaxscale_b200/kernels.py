@@ -316,6 +316,18 @@ def moe_experts(x, topk_w, topk_idx, w_gu, w_d, out, workspace, owner=None, rank
          I2 // 2, _p(w_gu), _p(w_d), _p(out), _p(workspace), workspace.numel(), _stream())
 
 
+def mla_rope_cache(q_in, kv_in, k_rope, inv_freq, positions, q_out, k_cache, v_cache, nh, nope, rope, vdim,
+                   tokens_per_seq=1):
+    for t, n in ((q_in, "q_in"), (kv_in, "kv_in"), (k_rope, "k_rope"), (q_out, "q_out"), (k_cache, "k_cache"),
+                 (v_cache, "v_cache")):
+        _need(t, n)
+    _need(inv_freq, "inv_freq", torch.float32)
+    _need(positions, "positions", torch.int32)
+    M = positions.numel()
+    call("jsx_mla_rope_cache", _p(q_in), _p(kv_in), _p(k_rope), _p(inv_freq), _p(positions), _p(q_out),
+         _p(k_cache), _p(v_cache), M, tokens_per_seq, nh, nope, rope, vdim, k_cache.shape[1], _stream())
+
+
 def moe_gate(x, w_nk, k, scale, norm=True, correction_bias=None, logits_given=False):
     """Router of layers/moe.py:54-79.  With logits_given, x holds bf16 logits [N, E]."""
     _need(x, "x")

@@ -259,6 +259,19 @@ int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args, void* stre
  * weights = uncorrected probabilities renormalised (+1e-20) when norm != 0,
  * times scale, rounded to bf16.  x[N][H], w_nk[E][H], topk_w[N][k] bf16,
  * topk_idx[N][k] int32.  E <= 256, k <= 8. */
+/* MLA (layers/mla_attention.py:139-172): neox RoPE (rotary_dim = rope) on the
+ * rope slice of every query head and on the shared rope key, concatenation
+ * [nope | rope], and the expanded per-head cache write.
+ *   q_in [M][nh][nope+rope] (q_b output), kv_in [M][nh][nope+vdim] (kv_b
+ *   output), k_rope [M][rope] (the rope columns of kv_a_proj_with_mqa),
+ *   inv_freq [rope/2], positions [M] (angle and cache slot), token m of
+ *   sequence m / tokens_per_seq; q_out [M][nh][nope+rope],
+ *   k_cache [B][max_seq][nh][nope+rope], v_cache [B][max_seq][nh][vdim]. */
+int jsx_mla_rope_cache(const void* q_in, const void* kv_in, const void* k_rope, const float* inv_freq,
+                       const int32_t* positions, void* q_out, void* k_cache, void* v_cache, int M,
+                       int tokens_per_seq, int nh, int nope, int rope, int vdim, int max_seq,
+                       void* stream);
+
 /* MoE experts of one rank (layers/moe.py:194-267, _forward_ep / _topk_local_forward):
  * x[N][H] normalised hidden states, topk_w[N][K] bf16 and topk_idx[N][K] from
  * jsx_moe_gate; expert_owner[E] (device int32) names the rank that computes each
