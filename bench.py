@@ -342,21 +342,31 @@ def run_gpu(args) -> None:
             trafkey = f"decode_step_tp{args.gpus}_b{B}"
             # per-phase breakdown from the kernel's %globaltimer trace (CTA 0, after each grid barrier)
             nl = c.num_hidden_layers
-            tr = torch.zeros(2 + 5 * nl, dtype=torch.int64, device=dev)
+            tr = torch.zeros(2 + 13 * nl, dtype=torch.int64, device=dev)
             st.step_args.trace = tr.data_ptr()
-            acc = None
+            acc, sub = None, None
             for _ in range(8):
                 model.step(st, head=True)
-                d = np.diff(tr.cpu().numpy().astype(np.float64)) / 1e3
+                t = tr.cpu().numpy().astype(np.float64)
+                d = np.diff(t[:2 + 5 * nl]) / 1e3
                 acc = d if acc is None else acc + d
+                # attention of head group 0, relative to the start of the attention phase
+                start = t[1:1 + 5 * nl:5]
+                s5 = (t[2 + 5 * nl:].reshape(nl, 8)[:, :7] - start[:, None]) / 1e3
+                sub = s5 if sub is None else sub + s5
             st.step_args.trace = None
             acc /= 8
+            sub /= 8
             per = acc[:5 * nl].reshape(nl, 5)
             names = ["qkv", "attention", "o_proj_allreduce", "gate_up", "down_allreduce"]
             phase_us = {n: float(per[:, i].mean()) for i, n in enumerate(names)}
             phase_us["lm_head"] = float(acc[5 * nl])
+            phase_us["attention_group0_us"] = {k: float(sub[:, i].mean()) for i, k in enumerate(
+                ["split0_start", "split0_staged", "split0_scored", "split0_softmax", "split0_pv_done",
+                 "split0_counted", "merge_done"])}
             phase_us["note"] = ("mean us per layer (lm_head: once per step) between grid barriers, each "
-                                "phase including its barrier; CTA 0 %globaltimer over 8 eager steps")
+                                "phase including its barrier; CTA 0 %globaltimer over 8 eager steps; "
+                                "attention_group0_us: head group 0 from the start of the attention phase")
         else:
             # dominant op: fused gate/up + SwiGLU, one call per layer's weights (every layer once:
             # 40 x 224 MB streams past the L2 between two calls on the same weights)

@@ -28,7 +28,13 @@ struct AttnArgs {
   float scale;
   float* part;     // [B*nkv*hg][splits][split_stride(gi)]: acc [gi][hd], then m [gi], l [gi] (padded)
   uint32_t* cnt;   // [B*nkv*hg], zero on entry, left zero
+  uint64_t* trace; // null, or 8 %globaltimer stamps of group 0: item (0, 0) start, staged,
+                   // scores, softmax, P.V done, completion counted; the group's merge done
 };
+
+__device__ __forceinline__ void attn_stamp(const AttnArgs& a, int vb, int s, int k) {
+  if (a.trace != nullptr && vb == 0 && (s == 0 || k == 6) && threadIdx.x == 0) a.trace[k] = globaltimer();
+}
 
 // floats per split record: the accumulator tile, then (m, l) per head, padded so
 // every record starts on a 16-byte boundary (float4 reads in the combine)
@@ -101,7 +107,8 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 // are formed once in shared memory (`scratch`, free once the item's own work is
 // done), then every output element is a short dot product over the splits.
 template <int NT>
-__device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int b, int head0, int cur, float* scratch) {
+__device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int s, int b, int head0, int cur,
+                                            float* scratch) {
   __shared__ bool is_last;
   const int gi = a.gi, hd = a.hd, tid = threadIdx.x;
   const int stride = split_stride(gi, hd);
@@ -112,6 +119,7 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int b, in
   __syncthreads();
   if (tid == 0) is_last = atomicAdd(a.cnt + vb, 1u) == (uint32_t)(a.splits - 1);
   __syncthreads();
+  attn_stamp(a, vb, s, 5);
   if (!is_last) return;
   __threadfence();
 
@@ -161,6 +169,7 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int b, in
     *reinterpret_cast<uint2*>(ob + e) = packed;
   }
   if (tid == 0) a.cnt[vb] = 0u;
+  attn_stamp(a, vb, 0, 6);
 }
 
 // One work item: cache rows [64 s, 64 s + 64) of item group vb (sequence b,
@@ -186,6 +195,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
   const int head0 = kvh * G + j * gi;  // first query head of the item
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __syncthreads();  // a CTA may run several items back to back over the same shared memory
+  attn_stamp(a, vb, s, 0);
 
   // q, the item's K/V rows and the position are loaded together: the rows are
   // staged whether or not they are inside the context (masked below)
@@ -220,6 +230,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
   if (n > kChunk) n = kChunk;
   float* part = a.part + ((size_t)vb * a.splits + s) * stride;
   __syncthreads();
+  attn_stamp(a, vb, s, 1);
 
   if (n > 0) {
     // scores: one (head, 32-row block) task per warp pass, one row per lane;
@@ -240,6 +251,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
       ps[h * kChunk + r] = r < n ? ((d0 + d1) + (d2 + d3)) * a.scale : -INFINITY;
     }
     __syncthreads();
+    attn_stamp(a, vb, s, 2);
     // softmax pieces of the split: per head max m, e = exp(s - m), sum l
     for (int h = warp; h < gi; h += NW) {
       float v[kRowBlocks];
@@ -264,6 +276,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
       }
     }
     __syncthreads();
+    attn_stamp(a, vb, s, 3);
     // P.V: each thread owns up to 4 (head, dim-pair) outputs and walks the rows
     // once for all of them (independent accumulators)
     for (int base = tid; base < gi * hw; base += 4 * NT) {
@@ -298,7 +311,8 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
     }
   }
 
-  attn_finish<NT>(a, vb, b, head0, cur, reinterpret_cast<float*>(ks));
+  attn_stamp(a, vb, s, 4);
+  attn_finish<NT>(a, vb, s, b, head0, cur, reinterpret_cast<float*>(ks));
 }
 
 // ---- tensor-core item (mma.sync m16n8k16, bf16 in, fp32 accumulate) ----------
@@ -349,6 +363,7 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
   const int head0 = kvh * G + j * kMmaHeads;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __syncthreads();  // a CTA may run several items back to back over the same shared memory
+  attn_stamp(a, vb, s, 0);
 
   const int p0 = s * kChunk;
   int cur = a.pos[b];
@@ -390,6 +405,7 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
   }
   float* part = a.part + ((size_t)vb * a.splits + s) * stride;
   __syncthreads();
+  attn_stamp(a, vb, s, 1);
 
   if (n > 0) {
     const int g = lane >> 2, t4 = lane & 3;
@@ -465,7 +481,8 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
       *reinterpret_cast<float2*>(part + (g + 8) * kMmaHd + d) = make_float2(o[jn][2], o[jn][3]);
     }
   }
-  attn_finish<NT>(a, vb, b, head0, cur, reinterpret_cast<float*>(ks));
+  attn_stamp(a, vb, s, 4);
+  attn_finish<NT>(a, vb, s, b, head0, cur, reinterpret_cast<float*>(ks));
 }
 
 // The item body for the group shape: tensor-core form for 16-head groups of

@@ -59,38 +59,36 @@ __device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Grid barrier in two halves: count bar[0], generation bar[1].  grid_arrive:
-// thread 0 of each CTA publishes the CTA's writes and arrives; the last
-// arrival resets the count and releases the next generation.  grid_wait: wait
-// for that generation.  The next phase's weight prefetch is issued between the
-// halves, so it neither delays the arrival (a fence would wait for it) nor
-// waits for the release.  `gen` lives in thread 0 only.
+// Grid barrier in two halves over one monotonic count bar[0] (zero when a
+// launch starts).  grid_arrive: thread 0 of each CTA publishes the CTA's
+// writes with a release reduction (no round trip); grid_wait: wait until the
+// count reaches (barriers passed + 1) x grid.  The next phase's weight prefetch
+// is issued between the halves.  grid_exit: the last CTA out of the kernel (it
+// counts its exit like an arrival, after every wait of every CTA) resets the
+// count for the next launch.  `gen` (barriers passed) lives in thread 0 only.
 __device__ __forceinline__ void grid_arrive(uint32_t* bar, uint32_t gen) {
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    if (atomicAdd(bar, 1u) == gridDim.x - 1) {
-      bar[0] = 0u;
-      __threadfence();
-      st_release_gpu(bar + 1, gen + 1u);
-    }
-  }
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
 }
 
 __device__ __forceinline__ void grid_wait(uint32_t* bar, uint32_t& gen) {
   if (threadIdx.x == 0) {
-    const uint32_t target = gen + 1u;
+    const uint32_t target = (gen + 1u) * gridDim.x;
     const long long t0 = clock64();
     uint32_t it = 0;
-    while ((int)(ld_acquire_gpu(bar + 1) - target) < 0) {
+    while ((int)(ld_acquire_gpu(bar) - target) < 0) {
       if ((++it & 63u) == 0 && clock64() - t0 > kBarrierLimitCycles) {
         atomicOr(&g_step_error, 1u);
         break;
       }
     }
-    gen = target;
+    gen = gen + 1u;
   }
   __syncthreads();
+}
+
+__device__ __forceinline__ void grid_exit(uint32_t* bar, uint32_t gen) {
+  if (threadIdx.x == 0 && atomicAdd(bar, 1u) == (gen + 1u) * gridDim.x - 1u) atomicExch(bar, 0u);
 }
 
 __device__ __forceinline__ void grid_sync(uint32_t* bar, uint32_t& gen) {
@@ -213,7 +211,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   const bool multi = c.world > 1;
   int tn = 0;
   uint32_t gen = 0;
-  if (threadIdx.x == 0) gen = ld_acquire_gpu(bar + 1);
   const uint32_t epoch0 = multi ? read_epoch(c) : 0u;
   const int qdim = a.n_heads * a.head_dim;
   const int qkv_rows = (a.n_heads + 2 * a.n_kv_heads) * a.head_dim;
@@ -283,6 +280,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     grid_sync(bar, gen);
   trace_mark(a.trace, tn);
     // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
+    at.trace = a.trace ? a.trace + (2 + 5 * a.n_layers) + 8 * l : nullptr;
     at.kc = reinterpret_cast<const bf16*>(L.k_cache);
     at.vc = reinterpret_cast<const bf16*>(L.v_cache);
     for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
@@ -352,6 +350,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       if (a.advance) a.positions[threadIdx.x] += 1;
       if (threadIdx.x == 0 && multi) c.state[kCalls] = last_epoch;
     }
+    grid_exit(bar, gen);
     return;
   }
 
@@ -382,6 +381,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   __syncthreads();
   if (threadIdx.x == 0) is_last = atomicAdd(lm_done, 1u) == gridDim.x - 1;
   __syncthreads();
+  grid_exit(bar, gen);
   if (!is_last) return;
   __threadfence();
   if (threadIdx.x < M) fin[threadIdx.x] = atomicAdd(keys + threadIdx.x, 0ull);

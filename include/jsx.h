@@ -247,8 +247,11 @@ typedef struct {
   void* logits;                    /* [batch][vocab_local] or NULL */
   void* workspace;                 /* jsx_decode_step_workspace_size bytes, zeroed once */
   size_t workspace_bytes;
-  uint64_t* trace;                 /* NULL, or [2 + 5 n_layers] u64: %globaltimer (ns) after the
-                                      embedding, after each phase of each layer, and at the end */
+  uint64_t* trace;                 /* NULL, or [2 + 13 n_layers] u64: %globaltimer (ns) after the
+                                      embedding, after each phase of each layer, and at the end;
+                                      then per layer 8 attention stamps of head group 0: split 0
+                                      started, staged, scored, softmax, P.V done, counted; the
+                                      merge done; one spare */
 } jsx_decode_step_args;
 
 int jsx_decode_step_workspace_size(const jsx_decode_step_args* args, size_t* bytes);
