@@ -77,7 +77,9 @@ constexpr int kMmaHeads = 16;
 constexpr int kMmaHd = 128;
 constexpr int kRowPad = kMmaHd + 8;   // bf16 per q/K/V row in shared memory
 constexpr int kPPad = kChunk + 8;     // bf16 per probability row
-__host__ __device__ __forceinline__ bool attn_use_mma(int gi, int hd) { return gi == kMmaHeads && hd == kMmaHd; }
+__host__ __device__ __forceinline__ bool attn_use_mma(int gi, int hd) {
+  return gi >= 1 && gi <= kMmaHeads && hd == kMmaHd;
+}
 
 // Shared bytes of one item: q (fp32), scores/probabilities, padded K rows, V
 // rows; the combine reuses the K/V area.  Tensor-core items: q, K, V (bf16,
@@ -316,12 +318,12 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int s, int vb, unsi
 }
 
 // ---- tensor-core item (mma.sync m16n8k16, bf16 in, fp32 accumulate) ----------
-// At batch >= 8 each CTA serves all 16 query heads of a kv head from one copy of
-// the split's K/V rows; the CUDA-core form then spends its time on shared-memory
-// reads (one load per FMA).  Here S = Q K^T and O = P V are m16n8k16 MMAs with
-// the 16 heads as M: every K/V element is read from shared memory once per
-// item.  The probabilities enter P.V rounded to bf16 (the reference also rounds
-// them to bf16 before its P.V product); m and l stay fp32.
+// S = Q K^T and O = P V are m16n8k16 MMAs with the item's query heads as M (a
+// group of gi <= 16 heads, padded with zero rows to 16): every K/V element is
+// read from shared memory once per item instead of once per head and output as
+// in the CUDA-core form (which measured 7 us of shared-memory-bound compute per
+// 64-row item at 4 heads).  The probabilities enter P.V rounded to bf16 (the
+// reference also rounds them to bf16 before its P.V product); m and l stay fp32.
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -350,9 +352,9 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
   constexpr int DW = kMmaHd / NW;   // output dims per warp (32 or 16)
   constexpr int NO = DW / 8;        // n8 output tiles per warp
   static_assert(NW == 4 || NW == 8, "4 or 8 warps");
-  const int G = a.nq / a.nkv;
-  const int stride = split_stride(kMmaHeads, kMmaHd);
-  bf16* qs = reinterpret_cast<bf16*>(smem_raw);  // [16][kRowPad]
+  const int G = a.nq / a.nkv, gi = a.gi;
+  const int stride = split_stride(gi, kMmaHd);
+  bf16* qs = reinterpret_cast<bf16*>(smem_raw);  // [16][kRowPad], rows >= gi zero
   bf16* ks = qs + kMmaHeads * kRowPad;            // [64][kRowPad]
   bf16* vs = ks + kChunk * kRowPad;               // [64][kRowPad]
   float* ss = reinterpret_cast<float*>(vs + kChunk * kRowPad);  // [16][64] scores
@@ -360,7 +362,7 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
 
   const int b = vb / (a.nkv * a.hg);
   const int kvh = (vb / a.hg) % a.nkv, j = vb % a.hg;
-  const int head0 = kvh * G + j * kMmaHeads;
+  const int head0 = kvh * G + j * gi;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   __syncthreads();  // a CTA may run several items back to back over the same shared memory
   attn_stamp(a, vb, s, 0);
@@ -380,7 +382,7 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
   const bf16* qg = a.q + ((size_t)b * a.nq + head0) * kMmaHd;
   for (int i = tid; i < kMmaHeads * 16; i += NT) {
     const int h = i >> 4, c = i & 15;
-    cp_async16(qs + h * kRowPad + c * 8, qg + h * kMmaHd + c * 8, 16u);
+    cp_async16(qs + h * kRowPad + c * 8, qg + (h < gi ? h : 0) * kMmaHd + c * 8, h < gi ? 16u : 0u);
   }
   const size_t row_stride = (size_t)a.nkv * kMmaHd;
   const bf16* kb = a.kc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
@@ -434,8 +436,9 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
       ss[(g + 8) * kChunk + r + 1] = r + 1 < n ? sc[jn][3] * a.scale : -INFINITY;
     }
     __syncthreads();
+    attn_stamp(a, vb, s, 2);
     // softmax pieces per head: m, e = exp(s - m) (bf16 for the MMA), l (fp32)
-    for (int h = warp; h < kMmaHeads; h += NW) {
+    for (int h = warp; h < gi; h += NW) {
       float v[kRowBlocks];
       float m = -INFINITY;
 #pragma unroll
@@ -453,11 +456,12 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
       }
       l = warp_sum(l);
       if (lane == 0) {
-        part[kMmaHeads * kMmaHd + h] = m;
-        part[kMmaHeads * kMmaHd + kMmaHeads + h] = l;
+        part[gi * kMmaHd + h] = m;
+        part[gi * kMmaHd + gi + h] = l;
       }
     }
     __syncthreads();
+    attn_stamp(a, vb, s, 3);
     // O = P V for dims [DW warp, DW warp + DW)
     float o[NO][4];
 #pragma unroll
@@ -477,16 +481,16 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
 #pragma unroll
     for (int jn = 0; jn < NO; ++jn) {
       const int d = DW * warp + 8 * jn + 2 * t4;
-      *reinterpret_cast<float2*>(part + g * kMmaHd + d) = make_float2(o[jn][0], o[jn][1]);
-      *reinterpret_cast<float2*>(part + (g + 8) * kMmaHd + d) = make_float2(o[jn][2], o[jn][3]);
+      if (g < gi) *reinterpret_cast<float2*>(part + g * kMmaHd + d) = make_float2(o[jn][0], o[jn][1]);
+      if (g + 8 < gi) *reinterpret_cast<float2*>(part + (g + 8) * kMmaHd + d) = make_float2(o[jn][2], o[jn][3]);
     }
   }
   attn_stamp(a, vb, s, 4);
   attn_finish<NT>(a, vb, s, b, head0, cur, reinterpret_cast<float*>(ks));
 }
 
-// The item body for the group shape: tensor-core form for 16-head groups of
-// head_dim 128, CUDA-core form otherwise.
+// The item body for the group shape: tensor-core form for head_dim 128 (groups
+// of up to 16 heads), CUDA-core form otherwise.
 template <int NT, bool kCoherent, bool kEager>
 __device__ __forceinline__ void attn_item_any(const AttnArgs& a, int s, int vb, unsigned char* smem_raw) {
   if (attn_use_mma(a.gi, a.hd)) attn_item_mma<NT, kCoherent, kEager>(a, s, vb, smem_raw);
