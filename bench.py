@@ -352,7 +352,7 @@ def run_gpu(args) -> None:
                 acc = d if acc is None else acc + d
                 # attention of head group 0, relative to the start of the attention phase
                 start = t[1:1 + 5 * nl:5]
-                s5 = (t[2 + 5 * nl:].reshape(nl, 8)[:, :7] - start[:, None]) / 1e3
+                s5 = (t[2 + 5 * nl:].reshape(nl, 8) - start[:, None]) / 1e3
                 sub = s5 if sub is None else sub + s5
             st.step_args.trace = None
             acc /= 8
@@ -363,7 +363,7 @@ def run_gpu(args) -> None:
             phase_us["lm_head"] = float(acc[5 * nl])
             phase_us["attention_group0_us"] = {k: float(sub[:, i].mean()) for i, k in enumerate(
                 ["split0_start", "split0_staged", "split0_scored", "split0_softmax", "split0_pv_done",
-                 "split0_counted", "merge_done"])}
+                 "split0_counted", "merge_done", "merge_start"])}
             phase_us["note"] = ("mean us per layer (lm_head: once per step) between grid barriers, each "
                                 "phase including its barrier; CTA 0 %globaltimer over 8 eager steps; "
                                 "attention_group0_us: head group 0 from the start of the attention phase")

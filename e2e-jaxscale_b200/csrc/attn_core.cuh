@@ -29,11 +29,12 @@ struct AttnArgs {
   float* part;     // [B*nkv*hg][splits][split_stride(gi)]: acc [gi][hd], then m [gi], l [gi] (padded)
   uint32_t* cnt;   // [B*nkv*hg], zero on entry, left zero
   uint64_t* trace; // null, or 8 %globaltimer stamps of group 0: item (0, 0) start, staged,
-                   // scores, softmax, P.V done, completion counted; the group's merge done
+                   // scores, softmax, P.V done, completion counted; the group's merge done,
+                   // the group's merge start (its last split counted)
 };
 
 __device__ __forceinline__ void attn_stamp(const AttnArgs& a, int vb, int s, int k) {
-  if (a.trace != nullptr && vb == 0 && (s == 0 || k == 6) && threadIdx.x == 0) a.trace[k] = globaltimer();
+  if (a.trace != nullptr && vb == 0 && (s == 0 || k >= 6) && threadIdx.x == 0) a.trace[k] = globaltimer();
 }
 
 // floats per split record: the accumulator tile, then (m, l) per head, padded so
@@ -103,15 +104,25 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t 
                : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ uint32_t dyn_smem_bytes() {
+  uint32_t r;
+  asm("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+  return r;
+}
 
 // Completion of one item: the item that completes the set of splits of group
 // vb merges them (flash-decoding combine).  Weights w_t[h] = exp(m_t - M) / L
 // are formed once in shared memory (`scratch`, free once the item's own work is
 // done), then every output element is a short dot product over the splits.
+// When the used split records fit in the dynamic shared memory past `scratch`
+// they arrive there in one cp.async round trip (m, l and the accumulators
+// together) and the merge runs from shared memory; otherwise m and l are read
+// first and the accumulators streamed from L2.
 template <int NT>
 __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int s, int b, int head0, int cur,
                                             float* scratch) {
   __shared__ bool is_last;
+  extern __shared__ __align__(16) unsigned char attn_dyn_smem[];
   const int gi = a.gi, hd = a.hd, tid = threadIdx.x;
   const int stride = split_stride(gi, hd);
   // the next kernel may launch once every item has reached this point (only
@@ -124,9 +135,53 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int s, in
   attn_stamp(a, vb, s, 5);
   if (!is_last) return;
   __threadfence();
+  attn_stamp(a, vb, s, 7);
 
   const int used = (cur + kChunk) / kChunk;
   const float* pb = a.part + (size_t)vb * a.splits * stride;
+  bf16* ob = a.out + ((size_t)b * a.nq + head0) * hd;
+  const uint32_t off = smem_addr(scratch) - smem_addr(attn_dyn_smem);
+  const size_t need = ((size_t)used * stride + (size_t)used * gi) * 4;
+  if ((off & 15u) == 0 && (hd & 1) == 0 && off + need <= dyn_smem_bytes()) {
+    constexpr int NW = NT / 32;
+    const int lane = tid & 31, warp = tid >> 5;
+    float* rec = scratch;                        // [used][stride]: the records as stored
+    float* w = rec + (size_t)used * stride;      // [used][gi] weights
+    const int n16 = (used * stride) >> 2;        // stride is a multiple of 4
+    for (int i = tid; i < n16; i += NT) cp_async16(rec + 4 * i, pb + 4 * i, 16u);
+    cp_async_wait_all();
+    __syncthreads();
+    for (int h = warp; h < gi; h += NW) {
+      float M = -INFINITY;
+      for (int t = lane; t < used; t += 32) M = fmaxf(M, rec[(size_t)t * stride + gi * hd + h]);
+      M = warp_max(M);
+      float L = 0.f;
+      for (int t = lane; t < used; t += 32) {
+        const float e = expf(rec[(size_t)t * stride + gi * hd + h] - M);
+        w[t * gi + h] = e;
+        L = fmaf(rec[(size_t)t * stride + gi * hd + gi + h], e, L);
+      }
+      L = warp_sum(L);
+      for (int t = lane; t < used; t += 32) w[t * gi + h] = w[t * gi + h] / L;
+    }
+    __syncthreads();
+    const int nv = (gi * hd) >> 1, s2 = stride >> 1;
+    const float2* r2 = reinterpret_cast<const float2*>(rec);
+    for (int i = tid; i < nv; i += NT) {
+      const int h = (i << 1) / hd;
+      float2 o = make_float2(0.f, 0.f);
+      for (int t = 0; t < used; ++t) {
+        const float wt = w[t * gi + h];
+        const float2 v = r2[(size_t)t * s2 + i];
+        o.x = fmaf(v.x, wt, o.x);
+        o.y = fmaf(v.y, wt, o.y);
+      }
+      *reinterpret_cast<uint32_t*>(ob + (i << 1)) = pack2(o.x, o.y);
+    }
+    if (tid == 0) a.cnt[vb] = 0u;
+    attn_stamp(a, vb, 0, 6);
+    return;
+  }
   float* wm = scratch;                       // [used][gi] m, then weights
   float* wl = wm + a.splits * gi;            // [used][gi] l
   float* Mg = wl + a.splits * gi;            // [gi]
@@ -151,7 +206,6 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int s, in
     wm[i] = expf(wm[i] - Mg[h]) / Lg[h];
   }
   __syncthreads();
-  bf16* ob = a.out + ((size_t)b * a.nq + head0) * hd;
   const int nv = (gi * hd) >> 2;
   for (int i = tid; i < nv; i += NT) {
     const int e = i << 2, h = e / hd;
@@ -344,8 +398,39 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint3
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <int NT, bool kCoherent, bool kEager>
-__device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, unsigned char* smem_raw) {
+// Staging of an item's cache rows ahead of the grid barrier that publishes this
+// step's q and its new K/V row (whole-step kernel): the rows of split s that
+// earlier steps wrote (before the position cur) are copied into the item's
+// shared-memory rows, rows past cur are zero-filled, the row at cur is left for
+// attn_item_mma<..., kPre = true>, which copies it and q after the barrier.
+// Returns the clamped position.  The positions do not change during a step.
+template <int NT>
+__device__ __forceinline__ int attn_prefetch_mma(const AttnArgs& a, int s, int vb, unsigned char* smem_raw) {
+  bf16* ks = reinterpret_cast<bf16*>(smem_raw) + kMmaHeads * kRowPad;
+  bf16* vs = ks + kChunk * kRowPad;
+  const int b = vb / (a.nkv * a.hg), kvh = (vb / a.hg) % a.nkv;
+  const int p0 = s * kChunk;
+  int cur = a.pos[b];
+  if (cur > a.max_seq - 1) cur = a.max_seq - 1;
+  if (cur < 0) cur = 0;
+  const int rc = cur - p0;  // row of position cur in this split (may lie outside it)
+  const size_t row_stride = (size_t)a.nkv * kMmaHd;
+  const bf16* kb = a.kc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
+  const bf16* vbp = a.vc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
+  for (int i = threadIdx.x; i < kChunk * 16; i += NT) {
+    const int r = i >> 4, c = i & 15;
+    if (r == rc) continue;
+    const bool live = r < rc;
+    const size_t off = (size_t)(live ? r : 0) * row_stride + c * 8;
+    cp_async16(ks + r * kRowPad + c * 8, kb + off, live ? 16u : 0u);
+    cp_async16(vs + r * kRowPad + c * 8, vbp + off, live ? 16u : 0u);
+  }
+  return cur;
+}
+
+template <int NT, bool kCoherent, bool kEager, bool kPre = false>
+__device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, unsigned char* smem_raw,
+                                              int pre_cur = 0) {
   constexpr int NW = NT / 32;
   constexpr int RW = kChunk / NW;   // score rows per warp (16 or 8)
   constexpr int NS = RW / 8;        // n8 score tiles per warp
@@ -368,7 +453,7 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
   attn_stamp(a, vb, s, 0);
 
   const int p0 = s * kChunk;
-  int cur = a.pos[b];
+  int cur = kPre ? pre_cur : a.pos[b];
   const int rows = kEager ? min(kChunk, a.max_seq - p0) : max(0, min(kChunk, min(cur, a.max_seq - 1) + 1 - p0));
   if (cur > a.max_seq - 1) cur = a.max_seq - 1;
   if (cur < 0) cur = 0;
@@ -387,16 +472,26 @@ __device__ __forceinline__ void attn_item_mma(const AttnArgs& a, int s, int vb, 
   const size_t row_stride = (size_t)a.nkv * kMmaHd;
   const bf16* kb = a.kc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
   const bf16* vbp = a.vc + ((size_t)b * a.max_seq + p0) * row_stride + (size_t)kvh * kMmaHd;
-  const int live_rows = kEager ? rows : min(rows, n);
-  for (int i = tid; i < kChunk * 16; i += NT) {
-    const int r = i >> 4, c = i & 15;
-    const bool live = r < live_rows;
-    const size_t off = (size_t)(live ? r : 0) * row_stride + c * 8;
-    cp_async16(ks + r * kRowPad + c * 8, kb + off, live ? 16u : 0u);
-    cp_async16(vs + r * kRowPad + c * 8, vbp + off, live ? 16u : 0u);
+  if (kPre) {
+    // every other row is in flight since attn_prefetch_mma
+    const int rc = cur - p0;
+    if (rc >= 0 && rc < kChunk && tid < 16) {
+      const size_t off = (size_t)rc * row_stride + tid * 8;
+      cp_async16(ks + rc * kRowPad + tid * 8, kb + off, 16u);
+      cp_async16(vs + rc * kRowPad + tid * 8, vbp + off, 16u);
+    }
+  } else {
+    const int live_rows = kEager ? rows : min(rows, n);
+    for (int i = tid; i < kChunk * 16; i += NT) {
+      const int r = i >> 4, c = i & 15;
+      const bool live = r < live_rows;
+      const size_t off = (size_t)(live ? r : 0) * row_stride + c * 8;
+      cp_async16(ks + r * kRowPad + c * 8, kb + off, live ? 16u : 0u);
+      cp_async16(vs + r * kRowPad + c * 8, vbp + off, live ? 16u : 0u);
+    }
   }
   cp_async_wait_all();
-  if (kEager) {
+  if (kEager && !kPre) {
     for (int i = tid; i < kChunk * 16; i += NT) {
       const int r = i >> 4, c = i & 15;
       if (r >= n && r < rows) {

@@ -49,6 +49,7 @@ constexpr long long kBarrierLimitCycles = 4000000000ll;  // ~2 s at the 1965 MHz
 constexpr size_t kWsBarrier = 0;
 constexpr size_t kWsLm = 256;
 constexpr size_t kWsAttn = 512;
+constexpr size_t kStepMergeSmemMax = 100 * 1024;  // two 256-thread CTAs per SM
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   uint32_t v;
@@ -257,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   at.cnt = reinterpret_cast<uint32_t*>(ws + kWsAttn + 256);
   at.part = reinterpret_cast<float*>(ws + kWsAttn + lay.counter_bytes);
   const int attn_items = M * a.n_kv_heads * lay.hg * lay.splits;
+  const bool attn_pre = attn_use_mma(lay.gi, a.head_dim) && (int)blockIdx.x < attn_items;
 
   for (int l = 0; l < a.n_layers; ++l) {
     const jsx_layer_weights L = layers[l];
@@ -277,14 +279,23 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       stage_x<M, false, true>(ga, xs);
       gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best);
     }
-    grid_sync(bar, gen);
-  trace_mark(a.trace, tn);
-    // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
     at.trace = a.trace ? a.trace + (2 + 5 * a.n_layers) + 8 * l : nullptr;
     at.kc = reinterpret_cast<const bf16*>(L.k_cache);
     at.vc = reinterpret_cast<const bf16*>(L.v_cache);
-    for (int it = blockIdx.x; it < attn_items; it += gridDim.x)
-      attn_item_any<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
+    grid_arrive(bar, gen);
+    // the cache rows of this CTA's first attention item that earlier steps
+    // wrote are staged while the barrier completes
+    int pre_cur = 0;
+    if (attn_pre) pre_cur = attn_prefetch_mma<kThreads>(at, blockIdx.x % at.splits, blockIdx.x / at.splits, smem_raw);
+    grid_wait(bar, gen);
+  trace_mark(a.trace, tn);
+    // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
+    for (int it = blockIdx.x; it < attn_items; it += gridDim.x) {
+      if (attn_pre && it == (int)blockIdx.x)
+        attn_item_mma<kThreads, true, true, true>(at, it % at.splits, it / at.splits, smem_raw, pre_cur);
+      else
+        attn_item_any<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
+    }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden);
     grid_wait(bar, gen);
@@ -425,7 +436,13 @@ static size_t step_smem(const jsx_decode_step_args& a) {
   if (a.n_heads * a.head_dim > kmax) kmax = a.n_heads * a.head_dim;
   const size_t x = (size_t)M * kmax * sizeof(bf16);
   const AttnLayout lay = attn_layout(M, a.n_heads, a.n_kv_heads, a.head_dim, a.max_seq);
-  const size_t at = attn_smem(lay.gi, a.head_dim, lay.splits);
+  size_t at = attn_smem(lay.gi, a.head_dim, lay.splits);
+  if (attn_use_mma(lay.gi, a.head_dim)) {
+    // room for the split merge to take every record into shared memory at once
+    // (attn_finish), while two CTAs still fit on an SM
+    const size_t merge = (size_t)kMmaHeads * kRowPad * 2 + (size_t)lay.splits * (lay.stride + lay.gi) * 4;
+    if (merge > at && merge <= kStepMergeSmemMax) at = merge;
+  }
   return x > at ? x : at;
 }
 
