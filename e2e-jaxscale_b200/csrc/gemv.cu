@@ -781,6 +781,7 @@ extern "C" int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm
 namespace jsx {
 int read_clear_step_error(uint32_t* out);  // decode_step.cu
 int read_clear_tc_error(uint32_t* out);    // tc_gemm.cu
+int read_clear_wide_error(uint32_t* out);  // tc_wide.cu
 }
 
 extern "C" int jsx_device_error(int* status) {
@@ -797,6 +798,9 @@ extern "C" int jsx_device_error(int* status) {
   uint32_t t = 0;
   st = jsx::read_clear_tc_error(&t);
   if (st != JSX_OK) return st;
-  *status = (v | w | t) ? JSX_ETIMEDOUT : JSX_OK;
+  uint32_t u = 0;
+  st = jsx::read_clear_wide_error(&u);
+  if (st != JSX_OK) return st;
+  *status = (v | w | t | u) ? JSX_ETIMEDOUT : JSX_OK;
   return JSX_OK;
 }

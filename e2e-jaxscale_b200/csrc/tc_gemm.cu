@@ -48,12 +48,12 @@
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "launch.cuh"
+#include "tc_core.cuh"
 
 namespace jsx {
 
 constexpr int kTcBM = 128;  // weight rows per tile (MMA M)
 constexpr int kTcBN = 32;   // tokens per tile (MMA N)
-constexpr int kTcBK = 64;   // K per stage: one 128-byte swizzle row of bf16
 constexpr int kTcStages = 8;
 constexpr int kTcThreads = 192;
 constexpr int kTcMaxM = 32;
@@ -65,7 +65,6 @@ constexpr uint32_t kTcRingBytes = kTcStages * kTcStageBytes;
 constexpr uint32_t kTcXBytes = kTcMaxM * kTcBM * 4;  // one exchange buffer: [32 tokens][128 rows] fp32
 constexpr uint32_t kTcTmemCols = 64;                  // two 32-column fp32 accumulators
 constexpr size_t kTcSmem = (size_t)kTcRingBytes + 2 * kTcXBytes + 1024 /* align */ + 1024 /* barriers */;
-constexpr long long kTcWaitCycles = 4000000000ll;  // ~2 s at the 1965 MHz max clock
 
 // workspace layout (bytes): kernel-done counter and argmax keys (zero between
 // calls), normalised activations [32][K] bf16, rank-local rows [M][N] fp32
@@ -102,169 +101,13 @@ __device__ __forceinline__ void tc_stamp(const TcArgs& t, int k) {
   if (t.trace) t.trace[(size_t)blockIdx.x * 8 + k] = globaltimer();
 }
 
-__device__ __forceinline__ uint32_t s_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void tc_mbar_init(uint64_t* b, uint32_t n) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(s_u32(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void tc_expect_tx(uint64_t* b, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(s_u32(b)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void tc_arrive(uint64_t* b) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(s_u32(b)) : "memory");
-}
-template <bool kCluster>
-__device__ __forceinline__ bool tc_try_wait(uint64_t* b, uint32_t parity) {
-  uint32_t ok;
-  if constexpr (kCluster) {
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(s_u32(b)), "r"(parity)
-        : "memory");
-  } else {
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(s_u32(b)), "r"(parity)
-        : "memory");
-  }
-  return ok != 0;
-}
-// Bounded wait.  false when the CTA's abort flag is up (another role gave up)
-// or after ~2 s (then the error word and the abort flag are set).  abort may
-// be null: drains that must finish regardless (still time-bounded).
-// kCluster: acquire at cluster scope (barriers that peers arrive on).
+// mbarrier wait bounded in time; a timeout raises this file's error word
 template <bool kCluster = false>
 __device__ __forceinline__ bool tc_wait(uint64_t* b, uint32_t parity, volatile uint32_t* abort) {
-  if (tc_try_wait<kCluster>(b, parity)) return true;
-  const long long t0 = clock64();
-  for (uint32_t it = 1;; ++it) {
-    if (tc_try_wait<kCluster>(b, parity)) return true;
-    if ((it & 63u) == 0) {
-      if (abort && *abort) return false;
-      if (clock64() - t0 > kTcWaitCycles) {
-        atomicOr(&g_tc_error, 1u);
-        if (abort) *abort = 1u;
-        return false;
-      }
-    }
-  }
+  return tc_wait_err<kCluster>(b, parity, abort, &g_tc_error);
 }
 
-// ---- cluster primitives ------------------------------------------------------
-__device__ __forceinline__ uint32_t cl_rank() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cl_id() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ uint32_t cl_count() {
-  uint32_t r;
-  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
-  return r;
-}
-// this CTA's shared address -> the same offset in cluster CTA `rank`
-__device__ __forceinline__ uint32_t cl_map(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ void cl_arrive_remote(uint32_t caddr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(caddr) : "memory");
-}
-__device__ __forceinline__ float2 cl_ld2(uint32_t caddr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(caddr) : "memory");
-  return v;
-}
-__device__ __forceinline__ void cl_fence() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
-__device__ __forceinline__ void cl_sync_all() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(s_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(s_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_map(const CUtensorMap* map) {
-  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
-}
-
-// Shared-memory matrix descriptor of a K-major, 128-byte-swizzled operand tile
-// (8-row swizzle atoms of 1024 bytes stacked along the M/N dimension):
-// start address, leading byte offset 16 B (unused with this swizzle), stride
-// byte offset 1024 B, descriptor version 1, layout type 2 (128-byte swizzle).
-// Advancing K by 16 elements inside the 128-byte row adds 32 bytes to the start.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)(16u >> 4) << 16;
-  d |= (uint64_t)(1024u >> 4) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-// Instruction descriptor of kind::f16: fp32 accumulate, bf16 A and B, both
-// K-major, N >> 3 at bit 17, M >> 4 at bit 24.
-constexpr uint32_t kTcIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcBN >> 3) << 17) |
-                              ((uint32_t)(kTcBM >> 4) << 24);
-
-__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(kTcIdesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(s_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-// Barriers over the 4 epilogue warps (named barrier 1, 128 threads; the warps
-// are converged first).  epi_all also ANDs a predicate across them, so a wait
-// that gave up in one thread makes every epilogue thread leave together.
-__device__ __forceinline__ void epi_sync() {
-  __syncwarp();
-  asm volatile("bar.sync 1, 128;" ::: "memory");
-}
-__device__ __forceinline__ bool epi_all(bool ok) {
-  __syncwarp();
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
-      : "=r"(r)
-      : "r"((uint32_t)ok)
-      : "memory");
-  return r != 0;
-}
-
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
+constexpr uint32_t kTcIdesc = tc_idesc(kTcBM, kTcBN);
 
 template <int EPI>
 __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant__ CUtensorMap tw,
@@ -385,7 +228,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
           const uint32_t sb = sa + kTcABytes;
 #pragma unroll
           for (int kk = 0; kk < kTcBK / 16; ++kk)
-            tc_mma(d, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32),
+            tc_mma(d, umma_desc_sw128(sa + kk * 32), umma_desc_sw128(sb + kk * 32), kTcIdesc,
                    (kb != kb0 || kk != 0) ? 1u : 0u);
           tc_commit(empty + s);
         }
@@ -546,41 +389,6 @@ __global__ void __launch_bounds__(256) k_tc_rows_allreduce(GemvArgs a, const flo
 }
 
 // ---- host ------------------------------------------------------------------------
-typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static int get_encoder(PFN_encodeTiled* out) {
-  static PFN_encodeTiled fn = nullptr;
-  static std::mutex mu;
-  std::lock_guard<std::mutex> lock(mu);
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    JSX_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
-    JSX_REQUIRE(p != nullptr && q == cudaDriverEntryPointSuccess, "cuTensorMapEncodeTiled unavailable");
-    fn = (PFN_encodeTiled)p;
-  }
-  *out = fn;
-  return JSX_OK;
-}
-
-// 2-D bf16 tensor map over a row-major [rows][K] matrix, box [box_rows][64],
-// 128-byte swizzle, out-of-range elements read as zero.
-static int make_map(CUtensorMap* map, const void* base, int rows, int K, int box_rows) {
-  PFN_encodeTiled enc;
-  int st = get_encoder(&enc);
-  if (st) return st;
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {(cuuint32_t)kTcBK, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  JSX_REQUIRE(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return JSX_OK;
-}
 
 // Cluster launch of k_tc_gemm; programmatic dependent launch when the
 // library's launch flags ask for it (attr holds 2 entries).

@@ -267,6 +267,72 @@ def tc_row_linear_allreduce(comm, x, w_nk, h, workspace):
          workspace.numel(), _stream())
 
 
+# ---- wide tensor-core projections (prefill / many tokens) ----------------------------
+def wide_workspace(M, shapes, device, norm=True) -> torch.Tensor:
+    """Workspace for every (K, N) in shapes at M tokens (with room for the
+    normalised activations when norm)."""
+    best = 0
+    for K_, N_ in shapes:
+        n = ctypes.c_size_t(0)
+        call("jsx_wide_workspace_size", M, K_, N_, int(norm), ctypes.byref(n))
+        best = max(best, n.value)
+    return torch.empty(best, dtype=torch.uint8, device=device)
+
+
+def wide_linear(x, w_nk, workspace, bias=None, gamma=None, eps=0.0, out=None):
+    _need(x, "x")
+    _need(w_nk, "w_nk")
+    _opt(bias, "bias")
+    _opt(gamma, "gamma")
+    _need(workspace, "workspace", torch.uint8)
+    N, K_ = w_nk.shape
+    x2 = x.reshape(-1, K_)
+    M = x2.shape[0]
+    out = torch.empty((M, N), dtype=BF16, device=x.device) if out is None else _need(out, "out")
+    call("jsx_wide_linear", _p(x2), _p(gamma), ctypes.c_float(eps), _p(w_nk), _p(bias), _p(out), M, K_, N,
+         _p(workspace), workspace.numel(), _stream())
+    return out.reshape(*x.shape[:-1], N)
+
+
+def wide_qkv_rope_cache(h, ln_gamma, eps, w_qkv, b_qkv, inv_freq, positions, q_out, k_cache, v_cache,
+                        nq, nkv, head_dim, rotary_dim, workspace, tokens_per_seq=1):
+    for t, n in ((h, "h"), (w_qkv, "w_qkv"), (q_out, "q_out"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(t, n)
+    _opt(ln_gamma, "ln_gamma")
+    _opt(b_qkv, "b_qkv")
+    _need(inv_freq, "inv_freq", torch.float32)
+    _need(positions, "positions", torch.int32)
+    _need(workspace, "workspace", torch.uint8)
+    M, K_ = h.shape
+    max_seq = k_cache.shape[1]
+    call("jsx_wide_qkv_rope_cache", _p(h), _p(ln_gamma), ctypes.c_float(eps), _p(w_qkv), _p(b_qkv),
+         _p(inv_freq), _p(positions), _p(q_out), _p(k_cache), _p(v_cache), M, tokens_per_seq, K_,
+         nq, nkv, head_dim, rotary_dim, max_seq, _p(workspace), workspace.numel(), _stream())
+
+
+def wide_gate_up_swiglu(h, ln_gamma, eps, w_gu, act, workspace):
+    _need(h, "h")
+    _opt(ln_gamma, "ln_gamma")
+    _need(w_gu, "w_gu")
+    _need(act, "act")
+    _need(workspace, "workspace", torch.uint8)
+    M, K_ = h.shape
+    I = w_gu.shape[0] // 2
+    call("jsx_wide_gate_up_swiglu", _p(h), _p(ln_gamma), ctypes.c_float(eps), _p(w_gu), _p(act), M, K_, I,
+         _p(workspace), workspace.numel(), _stream())
+
+
+def wide_row_linear_residual(x, w_nk, h, workspace):
+    _need(x, "x")
+    _need(w_nk, "w_nk")
+    _need(h, "h")
+    _need(workspace, "workspace", torch.uint8)
+    N, K_ = w_nk.shape
+    M = x.numel() // K_
+    call("jsx_wide_row_linear_residual", _p(x), _p(w_nk), _p(h), M, K_, N, _p(workspace), workspace.numel(),
+         _stream())
+
+
 def tc_lmhead_argmax(comm, h, norm_gamma, eps, w_vocab, vocab_offset, ids_out, workspace, logits_out=None):
     _need(h, "h")
     _opt(norm_gamma, "norm_gamma")

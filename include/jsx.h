@@ -206,6 +206,36 @@ int jsx_tc_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, 
                          int hidden, void* logits_out, int32_t* ids_out, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* ---- wide tensor-core projections (prefill, many tokens) ---------------------
+ * The column-parallel and single-rank row-parallel projections of
+ * LinearBase.__call__ (layers/linear.py:57-82) over a whole [B, S] token block
+ * (models/glm4.py:97-132 at prefill, runner.py:285-294), for any M >= 1 (tiles
+ * of 128 weight rows x 256 tokens on tcgen05 tensor cores, TMA-fed, fp32
+ * accumulation in TMEM).  Same packed weights, arguments and results as the
+ * jsx_tc_* / GEMV entry points (fp32 accumulation order differs).  gamma /
+ * ln_gamma: optional RMSNorm gain applied to the activations first
+ * (layers/normalization.py:31-37).
+ * workspace: jsx_wide_workspace_size(M, K, N, gamma != NULL) bytes, 16-byte
+ * aligned (the normalised activations live there).  Outputs and residuals
+ * must be 16-byte aligned. */
+int jsx_wide_workspace_size(int M, int K, int N, int has_gamma, size_t* bytes);
+int jsx_wide_linear(const void* x, const void* gamma, float eps, const void* w_nk, const void* bias,
+                    void* y, int M, int K, int N, void* workspace, size_t workspace_bytes,
+                    void* stream);
+int jsx_wide_qkv_rope_cache(const void* h, const void* ln_gamma, float eps, const void* w_qkv,
+                            const void* b_qkv, const float* inv_freq, const int32_t* positions,
+                            void* q_out, void* k_cache, void* v_cache, int M, int tokens_per_seq,
+                            int K, int nq, int nkv, int head_dim, int rotary_dim, int max_seq,
+                            void* workspace, size_t workspace_bytes, void* stream);
+int jsx_wide_gate_up_swiglu(const void* h, const void* ln_gamma, float eps, const void* w_gu,
+                            void* act, int M, int K, int I, void* workspace,
+                            size_t workspace_bytes, void* stream);
+/* h[M][N] += bf16(x[M][K] W^T): the row-parallel projection of one rank with
+ * the residual add (o_proj / down_proj at TP=1, layers/attention.py:159,
+ * models/glm4.py:49, :124, :130). */
+int jsx_wide_row_linear_residual(const void* x, const void* w_nk, void* h, int M, int K, int N,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- whole decode step ------------------------------------------------------
  * One cooperative kernel runs a full GLM-4 decode step for batch <= 8 on this
  * rank: embedding, every decoder layer (the work of jsx_qkv_rope_cache,

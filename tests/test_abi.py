@@ -82,6 +82,24 @@ def test_tc_workspace_size(jsx):
         lib.call("jsx_tc_workspace_size", 0, 64, 64, ctypes.byref(n))
 
 
+def test_wide_workspace_size(jsx):
+    """1 KB header, then (with a gain) the normalised activations [M][K] bf16
+    rounded to 1 KB."""
+    lib = jsx._lib
+    n = ctypes.c_size_t(0)
+    lib.call("jsx_wide_workspace_size", 4096, 4096, 4608, 1, ctypes.byref(n))
+    assert n.value == 1024 + 4096 * 4096 * 2
+    lib.call("jsx_wide_workspace_size", 300, 100, 8, 1, ctypes.byref(n))
+    assert n.value == 1024 + 60416                 # 300 x 100 x 2 = 60000 -> 60416
+    lib.call("jsx_wide_workspace_size", 300, 100, 8, 0, ctypes.byref(n))
+    assert n.value == 1024
+    with pytest.raises(lib.JsxError):
+        lib.call("jsx_wide_workspace_size", 0, 64, 64, 1, ctypes.byref(n))
+    with pytest.raises(lib.JsxError) as e:         # K not a multiple of 8, checked before any launch
+        lib.call("jsx_wide_linear", 1, None, 0.0, 1, None, 1, 256, 100, 64, 1, 1 << 20, None)
+    assert e.value.status == lib.JSX_EINVAL
+
+
 def test_moe_experts_workspace_and_limits(jsx):
     lib = jsx._lib
     n = ctypes.c_size_t(0)
