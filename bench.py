@@ -456,7 +456,7 @@ def run_rowpar(args) -> None:
     """Isolated row-parallel projection (o_proj W[4096 x 4096], down_proj W[13696 x 4096], bf16
     N(0, 0.02); activations N(0, 1)): the fused product + NVLink all-reduce + residual of
     this library against cuBLAS (torch.matmul) followed by NCCL all_reduce and the residual
-    add, M = 1, 8, 32 tokens, K split over the N ranks.  Time per call = CUDA events over
+    add, M = 1, 8, 32, 256, 4096 tokens, K split over the N ranks.  Time per call = CUDA events over
     `--steps` back-to-back calls after `--warmup`, max over ranks; rel_err compares the two
     results."""
     import torch
@@ -473,6 +473,7 @@ def run_rowpar(args) -> None:
     K = jsx.kernels
     mesh = jsx.create_mesh(tp=world)
     comm = mesh.comm(K.TC_MAX_TOKENS, 4096)
+    comm_t = mesh.comm_tiles(4096, 4096)
     stream = torch.cuda.current_stream()
 
     def max_over_ranks(x: float) -> float:
@@ -504,7 +505,7 @@ def run_rowpar(args) -> None:
         w_full = (torch.randn(N, Kfull, generator=g, device=dev) * 0.02).to(torch.bfloat16)
         w = w_full[:, rank * kl:(rank + 1) * kl].contiguous()          # this rank's [N, K/t]
         del w_full
-        for M in (1, 8, 32):
+        for M in (1, 8, 32, 256, 4096):
             x_full = torch.randn(M, Kfull, generator=g, device=dev).to(torch.bfloat16)
             x = x_full[:, rank * kl:(rank + 1) * kl].contiguous()
             h0 = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
@@ -512,10 +513,14 @@ def run_rowpar(args) -> None:
             if M <= K.MAX_DECODE_TOKENS:
                 fused = lambda: K.row_linear_allreduce(comm, x, w, h_f)
                 path = "GEMV (k_gemv<M,EPI_ROWAR>) + LL all-reduce"
-            else:
+            elif M <= K.TC_MAX_TOKENS:
                 ws = K.tc_workspace(M, [(kl, N)], dev)
                 fused = lambda: K.tc_row_linear_allreduce(comm, x, w, h_f, ws)
                 path = "tcgen05 (k_tc_gemm<EPI_ROWAR>) + LL all-reduce"
+            else:
+                ws = K.wide_workspace(M, [(kl, N)], dev, norm=False)
+                fused = lambda: K.wide_row_linear_allreduce(comm_t, x, w, h_f, ws)
+                path = "tcgen05 128x256 tiles (k_wide_gemm<EPI_ROWAR>) + in-epilogue tile exchange"
             h_b = h0.clone()
 
             def unfused():
@@ -536,8 +541,9 @@ def run_rowpar(args) -> None:
             t_u = timed(unfused)
             results.append({"op": name, "K": Kfull, "N": N, "M": M, "fused_us": t_f, "gemm_nccl_us": t_u,
                             "speedup": t_u / t_f, "rel_err": err, "fused_path": path})
-    if comm is not None:
-        comm.check()
+    for c_ in (comm, comm_t):
+        if c_ is not None:
+            c_.check()
     if rank == 0:
         print(json.dumps({"mode": "rowpar", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                           "dtype": "bf16", "data": "synthetic N(0,0.02) weights, N(0,1) activations (seed 1234)",

@@ -66,7 +66,7 @@ SIGNATURES = {
     "jsx_wide_linear": [P, P, F, P, P, P, I, I, I, P, SZ, P],
     "jsx_wide_qkv_rope_cache": [P, P, F, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P, SZ, P],
     "jsx_wide_gate_up_swiglu": [P, P, F, P, P, I, I, I, P, SZ, P],
-    "jsx_wide_row_linear_residual": [P, P, P, I, I, I, P, SZ, P],
+    "jsx_wide_row_linear_allreduce": [P, P, P, P, I, I, I, P, SZ, P],
     "jsx_moe_gate": [P, P, P, P, P, I, I, I, I, F, I, P],
     "jsx_mla_rope_cache": [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, P],
     "jsx_moe_experts_workspace_size": [I, I, I, I, I, P],
@@ -75,6 +75,7 @@ SIGNATURES = {
     "jsx_decode_step_workspace_size": [P, P],
     "jsx_decode_step": [P, P, P],
     "jsx_comm_create": [I, I, I, I, U64, P],
+    "jsx_comm_create_tiles": [I, I, I, I, U64, P],
     "jsx_comm_ipc_handle": [P, P],
     "jsx_comm_open_peers": [P, P],
     "jsx_comm_check": [P, P],

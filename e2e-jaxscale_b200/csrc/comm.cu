@@ -24,31 +24,12 @@ static size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 using namespace jsx;
 
-extern "C" int jsx_comm_create(int rank, int world, int max_tokens, int hidden, uint64_t timeout_ns,
-                               jsx_comm** out) {
-  JSX_REQUIRE(out != nullptr, "null out");
-  JSX_REQUIRE(world >= 1 && world <= kMaxRanks, "world=%d outside 1..%d", world, kMaxRanks);
-  JSX_REQUIRE(rank >= 0 && rank < world, "rank=%d outside [0, %d)", rank, world);
-  JSX_REQUIRE(max_tokens >= 1 && max_tokens <= 4096, "max_tokens=%d", max_tokens);
-  JSX_REQUIRE(hidden >= 1 && hidden <= (1 << 20), "hidden=%d", hidden);
-  *out = nullptr;
-  jsx_comm* c = (jsx_comm*)calloc(1, sizeof(jsx_comm));
-  if (!c) {
-    set_error("host allocation failed");
-    return JSX_ENOMEM;
-  }
+namespace jsx {
+
+// Allocates and zeroes the symmetric buffer (c->bytes, layout already set in
+// c->dev) and the local state words.
+static int comm_alloc(jsx_comm* c, jsx_comm** out) {
   JSX_CUDA(cudaGetDevice(&c->device));
-  const size_t flags = round256((size_t)(kMaxCtas + 1) * world * sizeof(uint32_t));
-  const size_t data = round256((size_t)2 * world * max_tokens * hidden * sizeof(unsigned long long));
-  const size_t keys = round256((size_t)2 * world * max_tokens * sizeof(unsigned long long));
-  c->bytes = flags + data + keys;
-  c->dev.off_data = flags;
-  c->dev.off_keys = flags + data;
-  c->dev.rank = rank;
-  c->dev.world = world;
-  c->dev.max_tokens = max_tokens;
-  c->dev.hidden = hidden;
-  c->dev.timeout_ns = timeout_ns ? timeout_ns : 5000000000ull;
   cudaError_t e = cudaMalloc((void**)&c->local, c->bytes);
   if (e != cudaSuccess) {
     free(c);
@@ -63,10 +44,75 @@ extern "C" int jsx_comm_create(int rank, int world, int max_tokens, int hidden, 
   JSX_CUDA(cudaMemset(c->local, 0, c->bytes));
   JSX_CUDA(cudaMemset(c->dev.state, 0, kStateWords * sizeof(uint32_t)));
   JSX_CUDA(cudaDeviceSynchronize());
-  c->dev.base[rank] = c->local;
-  c->opened = (world == 1);
+  c->dev.base[c->dev.rank] = c->local;
+  c->opened = (c->dev.world == 1);
   *out = c;
   return JSX_OK;
+}
+
+static jsx_comm* comm_new(int rank, int world, int max_tokens, int hidden, uint64_t timeout_ns) {
+  jsx_comm* c = (jsx_comm*)calloc(1, sizeof(jsx_comm));
+  if (!c) return nullptr;
+  c->dev.rank = rank;
+  c->dev.world = world;
+  c->dev.max_tokens = max_tokens;
+  c->dev.hidden = hidden;
+  c->dev.timeout_ns = timeout_ns ? timeout_ns : 5000000000ull;
+  return c;
+}
+
+}  // namespace jsx
+
+extern "C" int jsx_comm_create(int rank, int world, int max_tokens, int hidden, uint64_t timeout_ns,
+                               jsx_comm** out) {
+  JSX_REQUIRE(out != nullptr, "null out");
+  JSX_REQUIRE(world >= 1 && world <= kMaxRanks, "world=%d outside 1..%d", world, kMaxRanks);
+  JSX_REQUIRE(rank >= 0 && rank < world, "rank=%d outside [0, %d)", rank, world);
+  JSX_REQUIRE(max_tokens >= 1 && max_tokens <= 4096, "max_tokens=%d", max_tokens);
+  JSX_REQUIRE(hidden >= 1 && hidden <= (1 << 20), "hidden=%d", hidden);
+  *out = nullptr;
+  jsx_comm* c = comm_new(rank, world, max_tokens, hidden, timeout_ns);
+  if (!c) {
+    set_error("host allocation failed");
+    return JSX_ENOMEM;
+  }
+  const size_t flags = round256((size_t)(kMaxCtas + 1) * world * sizeof(uint32_t));
+  const size_t data = round256((size_t)2 * world * max_tokens * hidden * sizeof(unsigned long long));
+  const size_t keys = round256((size_t)2 * world * max_tokens * sizeof(unsigned long long));
+  c->bytes = flags + data + keys;
+  c->dev.off_data = flags;
+  c->dev.off_keys = flags + data;
+  return comm_alloc(c, out);
+}
+
+extern "C" int jsx_comm_create_tiles(int rank, int world, int max_tokens, int hidden, uint64_t timeout_ns,
+                                     jsx_comm** out) {
+  JSX_REQUIRE(out != nullptr, "null out");
+  JSX_REQUIRE(world >= 1 && world <= kMaxRanks, "world=%d outside 1..%d", world, kMaxRanks);
+  JSX_REQUIRE(rank >= 0 && rank < world, "rank=%d outside [0, %d)", rank, world);
+  JSX_REQUIRE(max_tokens >= 1 && max_tokens <= (1 << 20), "max_tokens=%d", max_tokens);
+  JSX_REQUIRE(hidden >= 2 && hidden % 2 == 0 && hidden <= (1 << 20), "hidden=%d", hidden);
+  *out = nullptr;
+  jsx_comm* c = comm_new(rank, world, max_tokens, hidden, timeout_ns);
+  if (!c) {
+    set_error("host allocation failed");
+    return JSX_ENOMEM;
+  }
+  const size_t tiles = (size_t)((max_tokens + kXTileTokens - 1) / kXTileTokens) *
+                       ((hidden + kXTileRows - 1) / kXTileRows);
+  const size_t owned = (tiles + world - 1) / world;
+  const size_t pflags = round256(owned * world * kXQuarters * sizeof(uint32_t));
+  const size_t rflags = round256(tiles * kXQuarters * sizeof(uint32_t));
+  const size_t slots = round256(owned * world * kXTileTokens * kXTileRows * 2);
+  const size_t result = round256((size_t)max_tokens * hidden * 2);
+  c->dev.max_tiles = (int)tiles;
+  c->dev.max_owned = (int)owned;
+  c->dev.off_pflags = 0;
+  c->dev.off_rflags = pflags;
+  c->dev.off_slots = pflags + rflags;
+  c->dev.off_result = pflags + rflags + slots;
+  c->bytes = pflags + rflags + slots + result;
+  return comm_alloc(c, out);
 }
 
 extern "C" int jsx_comm_ipc_handle(jsx_comm* comm, void* out64) {

@@ -29,6 +29,15 @@ constexpr int kMaxCtas = 1024;  // flag rows for per-CTA publication; row kMaxCt
 
 enum { kCalls = 0, kDone = 1, kError = 2, kStateWords = 8 };
 
+// Tile exchange of the wide row-parallel product (jsx_comm_create_tiles): an
+// output tile of kXTileRows weight rows x kXTileTokens tokens is owned by rank
+// (tile % world); the other ranks push their bf16 partial tiles into the
+// owner's receive slots, the owner sums them in rank order, adds the residual
+// and pushes the finished tile into every peer's result array.
+constexpr int kXTileRows = 128;
+constexpr int kXTileTokens = 256;
+constexpr int kXQuarters = 4;  // flags per tile: one per epilogue warp (32 rows each)
+
 struct CommDev {
   char* base[kMaxRanks];  // symmetric buffer of every rank, as mapped in this process
   uint32_t* state;        // local, not shared: calls, done, error
@@ -39,7 +48,45 @@ struct CommDev {
   size_t off_data;        // u64 LL words [2][world][max_tokens][hidden]
   size_t off_keys;        // u64   [2][world][max_tokens]
   unsigned long long timeout_ns;
+  // tile exchange (zero sizes unless created by jsx_comm_create_tiles)
+  int max_tiles, max_owned;
+  size_t off_pflags;      // u32 [max_owned][world][4]: partial (tile j, source, quarter) arrived
+  size_t off_rflags;      // u32 [max_tiles][4]: finished tile quarter arrived
+  size_t off_slots;       // bf16 [max_owned][world][256 tokens][128 rows]: partials
+  size_t off_result;      // bf16 [max_tokens][hidden]: finished tiles of other owners
 };
+
+__device__ __forceinline__ uint32_t* pflag_ptr(const CommDev& c, int r, int j, int src, int q) {
+  return reinterpret_cast<uint32_t*>(c.base[r] + c.off_pflags) + ((size_t)j * c.world + src) * kXQuarters + q;
+}
+__device__ __forceinline__ uint32_t* rflag_ptr(const CommDev& c, int r, int tile, int q) {
+  return reinterpret_cast<uint32_t*>(c.base[r] + c.off_rflags) + (size_t)tile * kXQuarters + q;
+}
+__device__ __forceinline__ bf16* slot_ptr(const CommDev& c, int r, int j, int src) {
+  return reinterpret_cast<bf16*>(c.base[r] + c.off_slots) +
+         ((size_t)j * c.world + src) * (kXTileTokens * kXTileRows);
+}
+__device__ __forceinline__ bf16* result_ptr(const CommDev& c, int r) {
+  return reinterpret_cast<bf16*>(c.base[r] + c.off_result);
+}
+
+// Bounded wait (every calling thread) until *f reaches `epoch`, with acquire
+// at system scope; on timeout the comm's error word is set and false returned.
+__device__ __forceinline__ bool wait_epoch_sys(const CommDev& c, const uint32_t* f, uint32_t epoch) {
+  if ((int)(ld_acquire_sys(f) - epoch) >= 0) return true;
+  if (*reinterpret_cast<volatile uint32_t*>(c.state + kError)) return false;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if ((int)(ld_acquire_sys(f) - epoch) >= 0) return true;
+    if ((it & 63u) == 0) {
+      if (globaltimer() - t0 > c.timeout_ns || it > (1u << 28)) {
+        atomicOr(c.state + kError, 1u);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t* flag_ptr(const CommDev& c, int r, int row, int src) {
   return reinterpret_cast<uint32_t*>(c.base[r]) + (size_t)row * c.world + src;

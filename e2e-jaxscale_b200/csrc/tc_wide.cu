@@ -28,6 +28,7 @@
 // wait, copies and MMAs in flight are drained (bounded) and TMEM is freed.
 #include <stdio.h>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "launch.cuh"
@@ -118,7 +119,7 @@ __device__ __forceinline__ void wide_pair(const GemvArgs& a, int g, int m, float
 template <int EPI>
 __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constant__ CUtensorMap tw,
                                                             const __grid_constant__ CUtensorMap tx, const WideArgs t,
-                                                            const GemvArgs a) {
+                                                            const GemvArgs a, const CommDev c) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWRingBytes);
@@ -219,6 +220,8 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int odd = lane & 1;
     pdl_wait();  // the epilogue reads and writes what earlier kernels use
+    const bool xchg = EPI == EPI_ROWAR && c.world > 1;
+    const uint32_t epoch = xchg ? read_epoch(c) : 0u;
     uint32_t ai = 0;
     for (int tile = blockIdx.x; tile < t.tiles; tile += gridDim.x, ++ai) {
       const uint32_t b = ai & 1;
@@ -235,23 +238,97 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         b0 = ldbf(a.bias + row0);
         b1 = ldbf(a.bias + row0 + 1);
       }
+      // across ranks: the tile's owner sums, the others push their partial
+      const int owner = xchg ? tile % c.world : 0, jo = xchg ? tile / c.world : 0;
+      const bool mine = !xchg || owner == c.rank;
+      const int rl0 = 32 * q + (lane & ~1);  // row pair inside the tile
+      if (xchg && mine)
+        for (int src = 0; src < c.world; ++src)
+          if (src != c.rank) wait_epoch_sys(c, pflag_ptr(c, c.rank, jo, src, q), epoch);
+      bf16* push = (xchg && !mine) ? slot_ptr(c, owner, jo, c.rank) : nullptr;
 #pragma unroll 1
-      for (int c = 0; c < kWBN / 32; ++c) {
+      for (int ch = 0; ch < kWBN / 32; ++ch) {
         float v[32];
-        tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + b * kWBN + 32 * c, v);
-        if (c == kWBN / 32 - 1) {
+        tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + b * kWBN + 32 * ch, v);
+        if (ch == kWBN / 32 - 1) {
           tc_fence_before();
           __syncwarp();
           if (lane == 0) tc_arrive(acce + b);
         }
-        const int m0 = tt * kWBN + 32 * c + 16 * odd;
+        const int ml0 = 32 * ch + 16 * odd;  // token inside the tile
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           // even lane: rows (own, partner) of token j; odd lane: (partner, own) of token 16 + j
           const float own = odd ? v[16 + j] : v[j];
           const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[16 + j], 1);
-          const int m = m0 + j;
-          if (live && m < t.M) wide_pair<EPI>(a, g, m, odd ? other : own, odd ? own : other, b0, b1);
+          const float v0 = odd ? other : own, v1 = odd ? own : other;
+          const int ml = ml0 + j, m = tt * kWBN + ml;
+          if (!live || m >= t.M) continue;
+          if (!xchg) {
+            wide_pair<EPI>(a, g, m, v0, v1, b0, b1);
+          } else if (!mine) {
+            // this rank's partial, rounded to bf16 (the reference's per-rank result)
+            *reinterpret_cast<uint32_t*>(push + (size_t)ml * kWBM + rl0) = pack2(v0, v1);
+          } else {
+            // rank-ordered sum of the ranks' bf16 partials, + residual, to every rank
+            float s0 = 0.f, s1 = 0.f;
+            for (int src = 0; src < c.world; ++src) {
+              if (src == c.rank) {
+                s0 += rbf(v0);
+                s1 += rbf(v1);
+              } else {
+                const uint32_t u =
+                    __ldcg(reinterpret_cast<const unsigned int*>(slot_ptr(c, c.rank, jo, src) + (size_t)ml * kWBM + rl0));
+                s0 += bf_lo(u);
+                s1 += bf_hi(u);
+              }
+            }
+            const size_t off = (size_t)m * t.N + row0;
+            const uint32_t hv = *reinterpret_cast<const uint32_t*>(a.h + off);
+            const uint32_t out = pack2(bf_lo(hv) + rbf(s0), bf_hi(hv) + rbf(s1));
+            *reinterpret_cast<uint32_t*>(a.h + off) = out;
+            for (int d = 0; d < c.world; ++d)
+              if (d != c.rank) *reinterpret_cast<uint32_t*>(result_ptr(c, d) + off) = out;
+          }
+        }
+      }
+      if (xchg) {
+        // publish this warp's quarter: every lane fences its own stores first
+        __threadfence_system();
+        __syncwarp();
+        if (lane == 0) {
+          if (!mine) {
+            st_release_sys(pflag_ptr(c, owner, jo, c.rank, q), epoch);
+          } else {
+            for (int d = 0; d < c.world; ++d)
+              if (d != c.rank) st_release_sys(rflag_ptr(c, d, tile, q), epoch);
+          }
+        }
+      }
+    }
+    if (xchg) {
+      // the tiles this CTA computed for other owners: their finished rows -> h
+      for (int tile = blockIdx.x; tile < t.tiles; tile += gridDim.x) {
+        if (tile % c.world == c.rank) continue;
+        int ft, tt;
+        wide_tile(t, tile, ft, tt);
+        wait_epoch_sys(c, rflag_ptr(c, c.rank, tile, q), epoch);
+        const int r0 = ft * kWBM + 32 * q;
+        const int nr = min(32, t.N - r0), nm = min(kWBN, t.M - tt * kWBN);
+        if (nr <= 0) continue;
+        const bf16* res = result_ptr(c, c.rank);
+        if (nr == 32 && (t.N & 7) == 0) {
+          // 32 rows = 4 x 16 bytes per token: 8 tokens per warp instruction
+          for (int e = lane; e < nm * 4; e += 32) {
+            const size_t off = (size_t)(tt * kWBN + (e >> 2)) * t.N + r0 + 8 * (e & 3);
+            *reinterpret_cast<uint4*>(a.h + off) = __ldcg(reinterpret_cast<const uint4*>(res + off));
+          }
+        } else {
+          const int np = nr >> 1;
+          for (int e = lane; e < nm * np; e += 32) {
+            const size_t off = (size_t)(tt * kWBN + e / np) * t.N + r0 + 2 * (e % np);
+            *reinterpret_cast<uint32_t*>(a.h + off) = __ldcg(reinterpret_cast<const unsigned int*>(res + off));
+          }
         }
       }
     }
@@ -266,6 +343,15 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWTmemCols)
                  : "memory");
+  }
+  if (EPI == EPI_ROWAR && c.world > 1 && threadIdx.x == 0) {
+    // the last CTA advances the comm's call counter (the epoch of the next call)
+    const uint32_t epoch = read_epoch(c);
+    if (atomicAdd(c.state + kDone, 1u) == gridDim.x - 1) {
+      c.state[kDone] = 0u;
+      __threadfence();
+      c.state[kCalls] = epoch;
+    }
   }
 }
 
@@ -291,8 +377,10 @@ static WidePlan wide_plan(int M, int K, int N, bool norm) {
   return p;
 }
 
+CommDev comm_view(jsx_comm* comm);
+
 template <int EPI>
-static int wide_run(GemvArgs ga, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+static int wide_run(jsx_comm* comm, GemvArgs ga, void* workspace, size_t workspace_bytes, cudaStream_t s) {
   JSX_REQUIRE(ga.M >= 1, "M=%d", ga.M);
   JSX_REQUIRE(ga.K >= 8 && ga.K % 8 == 0, "K=%d must be a positive multiple of 8", ga.K);
   JSX_REQUIRE(ga.N >= 2 && ga.N % 2 == 0, "N=%d must be even", ga.N);
@@ -302,6 +390,14 @@ static int wide_run(GemvArgs ga, void* workspace, size_t workspace_bytes, cudaSt
   const WidePlan p = wide_plan(ga.M, ga.K, ga.N, ga.gamma != nullptr);
   JSX_REQUIRE(workspace && aligned16(workspace) && workspace_bytes >= p.bytes,
               "workspace of %zu bytes (16-byte aligned) required", p.bytes);
+  CommDev c = {};
+  c.world = 1;
+  if (EPI == EPI_ROWAR && comm) {
+    c = comm_view(comm);
+    JSX_REQUIRE(c.world == 1 || c.max_tiles > 0, "the comm has no tile exchange (jsx_comm_create_tiles)");
+    JSX_REQUIRE(c.world == 1 || (ga.M <= c.max_tokens && ga.N <= c.hidden), "M=%d N=%d exceed the comm (%d, %d)",
+                ga.M, ga.N, c.max_tokens, c.hidden);
+  }
   const void* x = ga.x;
   if (ga.gamma) {
     // RMS-normalised copy of the activations (layers/normalization.py:31-37)
@@ -327,7 +423,7 @@ static int wide_run(GemvArgs ga, void* workspace, size_t workspace_bytes, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (launch_flags() & JSX_LAUNCH_PDL) ? 1 : 0;
-  JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, tw, tx, p.t, ga));
+  JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, tw, tx, p.t, ga, c));
   return JSX_OK;
 }
 
@@ -347,7 +443,7 @@ extern "C" int jsx_wide_linear(const void* x, const void* gamma, float eps, cons
   GemvArgs a = {};
   a.x = (const bf16*)x; a.gamma = (const bf16*)gamma; a.eps = eps; a.w = (const bf16*)w_nk;
   a.M = M; a.K = K; a.N = N; a.bias = (const bf16*)bias; a.y = (bf16*)y;
-  return wide_run<EPI_LINEAR>(a, workspace, workspace_bytes, (cudaStream_t)stream);
+  return wide_run<EPI_LINEAR>(nullptr, a, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int jsx_wide_qkv_rope_cache(const void* h, const void* ln_gamma, float eps, const void* w_qkv,
@@ -365,7 +461,7 @@ extern "C" int jsx_wide_qkv_rope_cache(const void* h, const void* ln_gamma, floa
   a.M = M; a.K = K; a.N = (nq + 2 * nkv) * head_dim; a.bias = (const bf16*)b_qkv; a.y = (bf16*)q_out;
   a.inv_freq = inv_freq; a.pos = positions; a.kc = (bf16*)k_cache; a.vc = (bf16*)v_cache;
   a.nq = nq; a.nkv = nkv; a.hd = head_dim; a.rot = rotary_dim; a.max_seq = max_seq; a.tps = tokens_per_seq;
-  return wide_run<EPI_QKV>(a, workspace, workspace_bytes, (cudaStream_t)stream);
+  return wide_run<EPI_QKV>(nullptr, a, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int jsx_wide_gate_up_swiglu(const void* h, const void* ln_gamma, float eps, const void* w_gu, void* act,
@@ -374,13 +470,14 @@ extern "C" int jsx_wide_gate_up_swiglu(const void* h, const void* ln_gamma, floa
   GemvArgs a = {};
   a.x = (const bf16*)h; a.gamma = (const bf16*)ln_gamma; a.eps = eps; a.w = (const bf16*)w_gu;
   a.M = M; a.K = K; a.N = 2 * I; a.y = (bf16*)act;
-  return wide_run<EPI_SWIGLU>(a, workspace, workspace_bytes, (cudaStream_t)stream);
+  return wide_run<EPI_SWIGLU>(nullptr, a, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
-extern "C" int jsx_wide_row_linear_residual(const void* x, const void* w_nk, void* h, int M, int K, int N,
-                                            void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" int jsx_wide_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h, int M,
+                                             int K_local, int N, void* workspace, size_t workspace_bytes,
+                                             void* stream) {
   JSX_REQUIRE(x && w_nk && h, "null pointer argument");
   GemvArgs a = {};
-  a.x = (const bf16*)x; a.w = (const bf16*)w_nk; a.M = M; a.K = K; a.N = N; a.h = (bf16*)h;
-  return wide_run<EPI_ROWAR>(a, workspace, workspace_bytes, (cudaStream_t)stream);
+  a.x = (const bf16*)x; a.w = (const bf16*)w_nk; a.M = M; a.K = K_local; a.N = N; a.h = (bf16*)h;
+  return wide_run<EPI_ROWAR>(comm, a, workspace, workspace_bytes, (cudaStream_t)stream);
 }

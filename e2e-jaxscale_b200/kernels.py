@@ -322,15 +322,18 @@ def wide_gate_up_swiglu(h, ln_gamma, eps, w_gu, act, workspace):
          _p(workspace), workspace.numel(), _stream())
 
 
-def wide_row_linear_residual(x, w_nk, h, workspace):
+def wide_row_linear_allreduce(comm, x, w_nk, h, workspace):
+    """h += all-reduce over the comm's ranks of x @ w_nk^T (comm None: one rank);
+    comm: a tile-exchange Comm (mesh.Comm(..., tiles=True))."""
     _need(x, "x")
     _need(w_nk, "w_nk")
     _need(h, "h")
     _need(workspace, "workspace", torch.uint8)
     N, K_ = w_nk.shape
     M = x.numel() // K_
-    call("jsx_wide_row_linear_residual", _p(x), _p(w_nk), _p(h), M, K_, N, _p(workspace), workspace.numel(),
-         _stream())
+    handle = None if comm is None else comm.handle
+    call("jsx_wide_row_linear_allreduce", handle, _p(x), _p(w_nk), _p(h), M, K_, N, _p(workspace),
+         workspace.numel(), _stream())
 
 
 def tc_lmhead_argmax(comm, h, norm_gamma, eps, w_vocab, vocab_offset, ids_out, workspace, logits_out=None):

@@ -22,15 +22,16 @@ from ._lib import JSX_ETIMEDOUT, JsxError, call
 
 
 class Comm:
-    """One rank's jsx_comm (include/jsx.h, jsx_comm_*)."""
+    """One rank's jsx_comm (include/jsx.h, jsx_comm_*).  tiles=True: the tile
+    exchange of the wide row-parallel product (jsx_comm_create_tiles)."""
 
     def __init__(self, rank: int, world: int, max_tokens: int, hidden: int,
-                 group=None, timeout_s: float = 5.0):
+                 group=None, timeout_s: float = 5.0, tiles: bool = False):
         self.rank, self.world = rank, world
         self.max_tokens, self.hidden = max_tokens, hidden
         self.handle = ctypes.c_void_p()
-        call("jsx_comm_create", rank, world, max_tokens, hidden, int(timeout_s * 1e9),
-             ctypes.byref(self.handle))
+        call("jsx_comm_create_tiles" if tiles else "jsx_comm_create", rank, world, max_tokens, hidden,
+             int(timeout_s * 1e9), ctypes.byref(self.handle))
         if world > 1:
             buf = (ctypes.c_char * 64)()
             call("jsx_comm_ipc_handle", self.handle, buf)
@@ -129,6 +130,17 @@ class Mesh:
         if key not in self._comms:
             self._comms[key] = Comm(self.tp_rank, self.tp, max_tokens, hidden,
                                     group=self.group("tensor"), timeout_s=timeout_s)
+        return self._comms[key]
+
+    def comm_tiles(self, max_tokens: int, hidden: int, timeout_s: float = 5.0) -> Comm | None:
+        """The tensor-axis tile-exchange Comm of the wide row-parallel product
+        (prefill, many tokens); None when tp == 1."""
+        if self.tp == 1:
+            return None
+        key = ("tiles", max_tokens, hidden)
+        if key not in self._comms:
+            self._comms[key] = Comm(self.tp_rank, self.tp, max_tokens, hidden,
+                                    group=self.group("tensor"), timeout_s=timeout_s, tiles=True)
         return self._comms[key]
 
     @property

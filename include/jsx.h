@@ -230,11 +230,22 @@ int jsx_wide_qkv_rope_cache(const void* h, const void* ln_gamma, float eps, cons
 int jsx_wide_gate_up_swiglu(const void* h, const void* ln_gamma, float eps, const void* w_gu,
                             void* act, int M, int K, int I, void* workspace,
                             size_t workspace_bytes, void* stream);
-/* h[M][N] += bf16(x[M][K] W^T): the row-parallel projection of one rank with
- * the residual add (o_proj / down_proj at TP=1, layers/attention.py:159,
- * models/glm4.py:49, :124, :130). */
-int jsx_wide_row_linear_residual(const void* x, const void* w_nk, void* h, int M, int K, int N,
-                                 void* workspace, size_t workspace_bytes, void* stream);
+/* Row-parallel projection + TP all-reduce + residual for many tokens
+ * (o_proj / down_proj, layers/attention.py:62-66, :159, models/glm4.py:40-44,
+ * :49, :124, :130; the psum that layers/linear.py:72-78 leaves to XLA):
+ * h[M][N] += bf16(sum over ranks of bf16(x_r[M][K_local] W_r^T)), the ranks'
+ * bf16 partials summed in fp32 in rank order (identical h on every rank).
+ * comm: NULL or a 1-rank comm (residual add only), or a tile-exchange comm of
+ * jsx_comm_create_tiles with max_tokens >= M and hidden >= N: each output tile
+ * of 128 rows x 256 tokens is owned by one rank; the others write their
+ * partial tile into the owner's buffer over NVLink as soon as it leaves the
+ * tensor cores, the owner sums, adds the residual and writes the finished
+ * tile to every rank, so the exchange overlaps the GEMM tile by tile.  Every
+ * rank calls with the same M, K_local, N; a peer that does not arrive within
+ * the comm timeout makes jsx_comm_check report JSX_ETIMEDOUT. */
+int jsx_wide_row_linear_allreduce(jsx_comm* comm, const void* x, const void* w_nk, void* h, int M,
+                                  int K_local, int N, void* workspace, size_t workspace_bytes,
+                                  void* stream);
 
 /* ---- whole decode step ------------------------------------------------------
  * One cooperative kernel runs a full GLM-4 decode step for batch <= 8 on this
@@ -328,6 +339,13 @@ int jsx_moe_gate(const void* x, const void* w_nk, const float* correction_bias, 
  * every wait on a peer (0 = 2 s default). */
 int jsx_comm_create(int rank, int world, int max_tokens, int hidden, uint64_t timeout_ns,
                     jsx_comm** out);
+/* A comm whose symmetric buffer holds the tile exchange of
+ * jsx_wide_row_linear_allreduce for up to max_tokens tokens and hidden output
+ * rows (partial slots, finished-tile array and flags: about
+ * 2 x max_tokens x hidden x 2 bytes per rank).  Peers are opened with
+ * jsx_comm_ipc_handle / jsx_comm_open_peers like any comm. */
+int jsx_comm_create_tiles(int rank, int world, int max_tokens, int hidden, uint64_t timeout_ns,
+                          jsx_comm** out);
 /* CUDA IPC handle of the symmetric buffer (64 bytes). */
 int jsx_comm_ipc_handle(jsx_comm* comm, void* out64);
 /* Opens every peer's handle (handles = world x 64 bytes, in rank order). */

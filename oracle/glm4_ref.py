@@ -326,7 +326,7 @@ def row_parallel_reference(x_shards, w_shards):
     bf16 per-rank partials summed (as fp32 here) and rounded once."""
     acc = np.zeros((x_shards[0].shape[0], w_shards[0].shape[1]), np.float32)
     for xr, wr in zip(x_shards, w_shards):
-        acc += np.matmul(np.asarray(xr, np.float32), np.asarray(wr, np.float32))
+        acc += bf16(np.matmul(np.asarray(xr, np.float32), np.asarray(wr, np.float32)))
     return bf16(acc)
 
 

@@ -3,7 +3,8 @@ GPU, jsx_comm over CUDA IPC, the fused row-parallel all-reduce and the
 vocab-sharded LM-head argmax checked against the oracle (GEMV and tensor-core
 forms), TP=2 models at batch 2 (whole-step kernel) and batch 6 (tensor-core
 projections) against the oracle's teacher-forced logits, an expert-parallel MoE
-layer (EP=2) against the oracle's MoELayer, and a peer that never arrives: the waiting
+layer (EP=2) against the oracle's MoELayer, the wide row-parallel product with
+its tile-exchange all-reduce at 300-1024 tokens, and a peer that never arrives: the waiting
 rank's kernel gives up after the comm timeout, jsx_comm_check reports
 JSX_ETIMEDOUT and the context stays usable.  NVLS is off (NCCL_NVLS_ENABLE=0);
 the kernels use plain peer stores."""
@@ -202,6 +203,29 @@ def _worker(rank, world, port, q):
         out["moe_identical"] = all(torch.equal(allm[0], t) for t in allm)
         mesh_ep.close()
 
+        # (f) wide row-parallel product + tile-exchange all-reduce (prefill / many tokens), two
+        #     shapes back to back on one comm (ragged tiles, ownership alternating over the ranks)
+        ctile = mesh.comm_tiles(1024, 1024, timeout_s=2.0)
+        out["wide_errs"], out["wide_identical"] = [], []
+        for Mw, Kw, Nw in ((600, 2048, 640), (300, 1024, 256), (1024, 4096, 1024)):
+            xw = ref.bf16(rng.standard_normal((Mw, Kw)))
+            ww = ref.bf16(rng.standard_normal((Kw, Nw)) * 0.02)
+            hw = ref.bf16(rng.standard_normal((Mw, Nw)))
+            hdw = _bf(hw, dev)
+            wws = K.wide_workspace(Mw, [(Kw // world, Nw)], dev, norm=False)
+            K.wide_row_linear_allreduce(ctile, _bf(ref.shard_columns(xw, world, rank), dev),
+                                        K.pack_transpose(_bf(ref.shard_rows(ww, world, rank), dev)), hdw, wws)
+            torch.cuda.synchronize()
+            ctile.check()
+            wantw = ref.bf16(hw + ref.row_parallel_reference(
+                [ref.shard_columns(xw, world, r) for r in range(world)],
+                [ref.shard_rows(ww, world, r) for r in range(world)]))
+            gotw = hdw.float().cpu().numpy()
+            out["wide_errs"].append(float(np.max(np.abs(gotw - wantw)) / np.max(np.abs(wantw))))
+            allw = [torch.empty_like(hdw.cpu()) for _ in range(world)]
+            dist.all_gather(allw, hdw.cpu())
+            out["wide_identical"].append(all(torch.equal(allw[0], t) for t in allw))
+
         # (d) a peer that never arrives: rank 1 skips the call
         dist.barrier()
         c3 = jsx.mesh.Comm(rank, world, 8, 64, group=None, timeout_s=0.5)
@@ -254,5 +278,7 @@ def test_tensor_parallel_two_gpus():
         assert max(res[r]["tc_model_errs"]) <= 2e-2, res[r]["tc_model_errs"]
         assert res[r]["moe_err"] <= 2e-2 and res[r]["moe_cos"] >= 0.999, (res[r]["moe_err"], res[r]["moe_cos"])
         assert res[r]["moe_identical"]
+        assert max(res[r]["wide_errs"]) <= 1e-2, res[r]["wide_errs"]
+        assert all(res[r]["wide_identical"])
     assert res[0]["timeout_status"] == 3  # JSX_ETIMEDOUT
     assert res[0]["after_timeout"] == 8 * 64.0

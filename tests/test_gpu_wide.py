@@ -122,8 +122,8 @@ def test_wide_row_linear_residual(jsx, ref, cuda, rng, M, K, N):
     h0 = rand_bf16(ref, rng, (M, N))
     h = bf(h0, cuda)
     Kx = jsx.kernels
-    Kx.wide_row_linear_residual(bf(x, cuda), Kx.pack_transpose(bf(w, cuda)), h,
-                                Kx.wide_workspace(M, [(K, N)], cuda, norm=False))
+    Kx.wide_row_linear_allreduce(None, bf(x, cuda), Kx.pack_transpose(bf(w, cuda)), h,
+                                 Kx.wide_workspace(M, [(K, N)], cuda, norm=False))
     close(npf(h), ref.bf16(h0 + ref.linear(x, w)), exact_min=0.98)
 
 
