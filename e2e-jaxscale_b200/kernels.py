@@ -267,6 +267,18 @@ def tc_row_linear_allreduce(comm, x, w_nk, h, workspace):
          workspace.numel(), _stream())
 
 
+def attn_prefill(q, k_cache, v_cache, nq, nkv, head_dim, S, start_pos=0, scale=None, out=None):
+    """Causal prefill attention: q [B*S, nq*hd] -> out [B*S, nq*hd] over cache rows [0, start_pos + i]."""
+    for t, n in ((q, "q"), (k_cache, "k_cache"), (v_cache, "v_cache")):
+        _need(t, n)
+    B, L = k_cache.shape[0], k_cache.shape[1]
+    scale = head_dim ** -0.5 if scale is None else scale
+    out = torch.empty((B * S, nq * head_dim), dtype=BF16, device=q.device) if out is None else _need(out, "out")
+    call("jsx_attn_prefill", _p(q), _p(k_cache), _p(v_cache), _p(out), B, S, start_pos, nq, nkv, head_dim, L,
+         ctypes.c_float(scale), _stream())
+    return out
+
+
 # ---- wide tensor-core projections (prefill / many tokens) ----------------------------
 def wide_workspace(M, shapes, device, norm=True) -> torch.Tensor:
     """Workspace for every (K, N) in shapes at M tokens (with room for the

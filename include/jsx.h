@@ -118,6 +118,16 @@ int jsx_gate_up_swiglu(const void* h, const void* ln_gamma, float eps, const voi
  * out[B][nq*hd].  Split over the context; partial results go to `workspace`. */
 int jsx_attn_decode_workspace_size(int B, int nq, int nkv, int head_dim, int max_seq,
                                    size_t* bytes);
+/* Causal prefill attention over the static KV cache (layers/attention.py:101-160
+ * with the prefill mask of runner.py:26-32, cache_position = start_pos for the
+ * whole batch): query token i of sequence b (position start_pos + i) attends to
+ * cache rows [0, start_pos + i].  q and out [B * S][nq * head_dim] (q already
+ * rotated, rows [start_pos, start_pos + S) of the caches already written),
+ * caches [B][max_seq][nkv][head_dim].  head_dim 128 (JSX_ENOTSUP otherwise);
+ * fp32 softmax, probabilities rounded to bf16 for the P.V product. */
+int jsx_attn_prefill(const void* q, const void* k_cache, const void* v_cache, void* out, int B,
+                     int S, int start_pos, int nq, int nkv, int head_dim, int max_seq,
+                     float scale, void* stream);
 int jsx_attn_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
                     const int32_t* positions, int B, int nq, int nkv, int head_dim,
                     int max_seq, float scale, void* workspace, size_t workspace_bytes,
