@@ -104,7 +104,7 @@ extern "C" int jsx_comm_create_tiles(int rank, int world, int max_tokens, int hi
   const size_t pflags = round256(owned * world * kXQuarters * sizeof(uint32_t));
   const size_t rflags = round256(tiles * kXQuarters * sizeof(uint32_t));
   const size_t slots = round256(owned * world * kXTileTokens * kXTileRows * 2);
-  const size_t result = round256((size_t)max_tokens * hidden * 2);
+  const size_t result = round256(tiles * kXTileTokens * kXTileRows * 2);
   c->dev.max_tiles = (int)tiles;
   c->dev.max_owned = (int)owned;
   c->dev.off_pflags = 0;

@@ -52,8 +52,8 @@ struct CommDev {
   int max_tiles, max_owned;
   size_t off_pflags;      // u32 [max_owned][world][4]: partial (tile j, source, quarter) arrived
   size_t off_rflags;      // u32 [max_tiles][4]: finished tile quarter arrived
-  size_t off_slots;       // bf16 [max_owned][world][256 tokens][128 rows]: partials
-  size_t off_result;      // bf16 [max_tokens][hidden]: finished tiles of other owners
+  size_t off_slots;       // bf16 [max_owned][world][4 quarters][256 tokens][32 rows]: partials
+  size_t off_result;      // bf16 [max_tiles][4 quarters][256 tokens][32 rows]: finished tiles
 };
 
 __device__ __forceinline__ uint32_t* pflag_ptr(const CommDev& c, int r, int j, int src, int q) {
@@ -62,12 +62,14 @@ __device__ __forceinline__ uint32_t* pflag_ptr(const CommDev& c, int r, int j, i
 __device__ __forceinline__ uint32_t* rflag_ptr(const CommDev& c, int r, int tile, int q) {
   return reinterpret_cast<uint32_t*>(c.base[r] + c.off_rflags) + (size_t)tile * kXQuarters + q;
 }
-__device__ __forceinline__ bf16* slot_ptr(const CommDev& c, int r, int j, int src) {
+// [256 tokens][32 rows] block of quarter q (16 KB, contiguous)
+__device__ __forceinline__ bf16* slot_ptr(const CommDev& c, int r, int j, int src, int q) {
   return reinterpret_cast<bf16*>(c.base[r] + c.off_slots) +
-         ((size_t)j * c.world + src) * (kXTileTokens * kXTileRows);
+         (((size_t)j * c.world + src) * kXQuarters + q) * (kXTileTokens * kXTileRows / kXQuarters);
 }
-__device__ __forceinline__ bf16* result_ptr(const CommDev& c, int r) {
-  return reinterpret_cast<bf16*>(c.base[r] + c.off_result);
+__device__ __forceinline__ bf16* result_ptr(const CommDev& c, int r, int tile, int q) {
+  return reinterpret_cast<bf16*>(c.base[r] + c.off_result) +
+         ((size_t)tile * kXQuarters + q) * (kXTileTokens * kXTileRows / kXQuarters);
 }
 
 // Bounded wait (every calling thread) until *f reaches `epoch`, with acquire

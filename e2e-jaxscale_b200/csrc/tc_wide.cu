@@ -46,7 +46,8 @@ constexpr uint32_t kWBBytes = kWBN * kTcBK * 2;
 constexpr uint32_t kWStageBytes = kWABytes + kWBBytes;
 constexpr uint32_t kWRingBytes = kWStages * kWStageBytes;
 constexpr uint32_t kWTmemCols = 2 * kWBN;
-constexpr size_t kWSmem = (size_t)kWRingBytes + 1024 /* align */ + 1024 /* barriers */;
+constexpr uint32_t kWStageOff = kWRingBytes + 1024;  // after the ring and the barriers
+constexpr size_t kWSmem = (size_t)kWStageOff + 4 * 32 * 32 * 2 /* exchange staging */ + 1024 /* align */;
 constexpr uint32_t kWIdesc = tc_idesc(kWBM, kWBN);
 constexpr size_t kWOffXn = 1024;  // workspace: header, then the RMS-normalised activations [M][K] bf16
 
@@ -116,6 +117,91 @@ __device__ __forceinline__ void wide_pair(const GemvArgs& a, int g, int m, float
   }
 }
 
+__device__ __forceinline__ void pack8(const float (&f)[8], uint4& u) {
+  u.x = pack2(f[0], f[1]);
+  u.y = pack2(f[2], f[3]);
+  u.z = pack2(f[4], f[5]);
+  u.w = pack2(f[6], f[7]);
+}
+
+// One epilogue warp's quarter (32 rows x 256 tokens) of a tile in the
+// row-parallel product across ranks.  Per 32-token chunk the accumulator is
+// rounded to bf16 (this rank's partial, the reference's per-rank result) and
+// transposed through shared memory into [token][32 rows], so that every
+// transfer is a 16-byte store and a quarter is 16 KB contiguous:
+//   not the owner: push the partial into the owner's slot, then flag it;
+//   owner: wait for the peers' partials, sum the ranks' bf16 partials in fp32
+//   in rank order, round, add the residual (identical h on every rank), store
+//   h here and the finished quarter into every peer's result array, flag them.
+__device__ __forceinline__ void wide_exchange_tile(const CommDev& c, const WideArgs& t, const GemvArgs& a, int tile,
+                                                   int ft, int tt, int q, int lane, uint32_t epoch, uint32_t tacc,
+                                                   uint64_t* acc_empty, bf16* stg) {
+  const int owner = tile % c.world, jo = tile / c.world;
+  const bool mine = owner == c.rank;
+  if (mine)
+    for (int src = 0; src < c.world; ++src)
+      if (src != c.rank) wait_epoch_sys(c, pflag_ptr(c, c.rank, jo, src, q), epoch);
+  bf16* push = mine ? nullptr : slot_ptr(c, owner, jo, c.rank, q);
+#pragma unroll 1
+  for (int ch = 0; ch < kWBN / 32; ++ch) {
+    float v[32];
+    tc_ld32(tacc + 32 * ch, v);
+    if (ch == kWBN / 32 - 1) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc_arrive(acc_empty);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = __float2bfloat16_rn(v[j]);
+    __syncwarp();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = lane + 32 * k;  // 16-byte vector: token e / 4 of the chunk, rows 8 (e % 4) ..
+      const int tl = e >> 2, rv = 8 * (e & 3);
+      const int ml = 32 * ch + tl;  // token inside the tile
+      const uint4 part = *reinterpret_cast<const uint4*>(stg + tl * 32 + rv);
+      if (!mine) {
+        *reinterpret_cast<uint4*>(push + ml * 32 + rv) = part;
+        continue;
+      }
+      float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int src = 0; src < c.world; ++src) {
+        const uint4 u = src == c.rank ? part
+                                      : __ldcg(reinterpret_cast<const uint4*>(slot_ptr(c, c.rank, jo, src, q) +
+                                                                              ml * 32 + rv));
+        float f[8];
+        unpack8(u, f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum[i] += f[i];
+      }
+      const int m = tt * kWBN + ml, row = ft * kWBM + 32 * q + rv;
+      if (m >= t.M || row >= t.N) continue;
+      bf16* hp = a.h + (size_t)m * t.N + row;
+      float hf[8];
+      unpack8(*reinterpret_cast<const uint4*>(hp), hf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hf[i] += rbf(sum[i]);
+      uint4 out;
+      pack8(hf, out);
+      *reinterpret_cast<uint4*>(hp) = out;
+      for (int d = 0; d < c.world; ++d)
+        if (d != c.rank) *reinterpret_cast<uint4*>(result_ptr(c, d, tile, q) + ml * 32 + rv) = out;
+    }
+    __syncwarp();  // the staging buffer is refilled by the next chunk
+  }
+  // publish the quarter: every lane fences its own stores first
+  __threadfence_system();
+  __syncwarp();
+  if (lane == 0) {
+    if (!mine) {
+      st_release_sys(pflag_ptr(c, owner, jo, c.rank, q), epoch);
+    } else {
+      for (int d = 0; d < c.world; ++d)
+        if (d != c.rank) st_release_sys(rflag_ptr(c, d, tile, q), epoch);
+    }
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constant__ CUtensorMap tw,
                                                             const __grid_constant__ CUtensorMap tx, const WideArgs t,
@@ -129,6 +215,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
   uint64_t* fin = acce + 2;           // every MMA of the CTA complete
   uint32_t* misc = reinterpret_cast<uint32_t*>(fin + 1);  // tmem base, abort
   volatile uint32_t* abort_flag = misc + 1;
+  bf16* stg = reinterpret_cast<bf16*>(smem + kWStageOff);  // [4 warps][32 tokens][32 rows] (exchange)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 1) {
@@ -238,14 +325,11 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         b0 = ldbf(a.bias + row0);
         b1 = ldbf(a.bias + row0 + 1);
       }
-      // across ranks: the tile's owner sums, the others push their partial
-      const int owner = xchg ? tile % c.world : 0, jo = xchg ? tile / c.world : 0;
-      const bool mine = !xchg || owner == c.rank;
-      const int rl0 = 32 * q + (lane & ~1);  // row pair inside the tile
-      if (xchg && mine)
-        for (int src = 0; src < c.world; ++src)
-          if (src != c.rank) wait_epoch_sys(c, pflag_ptr(c, c.rank, jo, src, q), epoch);
-      bf16* push = (xchg && !mine) ? slot_ptr(c, owner, jo, c.rank) : nullptr;
+      if (xchg) {
+        wide_exchange_tile(c, t, a, tile, ft, tt, q, lane, epoch, tmem + ((uint32_t)(32 * q) << 16) + b * kWBN,
+                           acce + b, stg + (warp - 2) * (32 * 32));
+        continue;
+      }
 #pragma unroll 1
       for (int ch = 0; ch < kWBN / 32; ++ch) {
         float v[32];
@@ -255,54 +339,14 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
           __syncwarp();
           if (lane == 0) tc_arrive(acce + b);
         }
-        const int ml0 = 32 * ch + 16 * odd;  // token inside the tile
+        const int m0 = tt * kWBN + 32 * ch + 16 * odd;
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           // even lane: rows (own, partner) of token j; odd lane: (partner, own) of token 16 + j
           const float own = odd ? v[16 + j] : v[j];
           const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[16 + j], 1);
-          const float v0 = odd ? other : own, v1 = odd ? own : other;
-          const int ml = ml0 + j, m = tt * kWBN + ml;
-          if (!live || m >= t.M) continue;
-          if (!xchg) {
-            wide_pair<EPI>(a, g, m, v0, v1, b0, b1);
-          } else if (!mine) {
-            // this rank's partial, rounded to bf16 (the reference's per-rank result)
-            *reinterpret_cast<uint32_t*>(push + (size_t)ml * kWBM + rl0) = pack2(v0, v1);
-          } else {
-            // rank-ordered sum of the ranks' bf16 partials, + residual, to every rank
-            float s0 = 0.f, s1 = 0.f;
-            for (int src = 0; src < c.world; ++src) {
-              if (src == c.rank) {
-                s0 += rbf(v0);
-                s1 += rbf(v1);
-              } else {
-                const uint32_t u =
-                    __ldcg(reinterpret_cast<const unsigned int*>(slot_ptr(c, c.rank, jo, src) + (size_t)ml * kWBM + rl0));
-                s0 += bf_lo(u);
-                s1 += bf_hi(u);
-              }
-            }
-            const size_t off = (size_t)m * t.N + row0;
-            const uint32_t hv = *reinterpret_cast<const uint32_t*>(a.h + off);
-            const uint32_t out = pack2(bf_lo(hv) + rbf(s0), bf_hi(hv) + rbf(s1));
-            *reinterpret_cast<uint32_t*>(a.h + off) = out;
-            for (int d = 0; d < c.world; ++d)
-              if (d != c.rank) *reinterpret_cast<uint32_t*>(result_ptr(c, d) + off) = out;
-          }
-        }
-      }
-      if (xchg) {
-        // publish this warp's quarter: every lane fences its own stores first
-        __threadfence_system();
-        __syncwarp();
-        if (lane == 0) {
-          if (!mine) {
-            st_release_sys(pflag_ptr(c, owner, jo, c.rank, q), epoch);
-          } else {
-            for (int d = 0; d < c.world; ++d)
-              if (d != c.rank) st_release_sys(rflag_ptr(c, d, tile, q), epoch);
-          }
+          const int m = m0 + j;
+          if (live && m < t.M) wide_pair<EPI>(a, g, m, odd ? other : own, odd ? own : other, b0, b1);
         }
       }
     }
@@ -313,22 +357,14 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         int ft, tt;
         wide_tile(t, tile, ft, tt);
         wait_epoch_sys(c, rflag_ptr(c, c.rank, tile, q), epoch);
+        const bf16* res = result_ptr(c, c.rank, tile, q);  // [256 tokens][32 rows]
         const int r0 = ft * kWBM + 32 * q;
-        const int nr = min(32, t.N - r0), nm = min(kWBN, t.M - tt * kWBN);
-        if (nr <= 0) continue;
-        const bf16* res = result_ptr(c, c.rank);
-        if (nr == 32 && (t.N & 7) == 0) {
-          // 32 rows = 4 x 16 bytes per token: 8 tokens per warp instruction
-          for (int e = lane; e < nm * 4; e += 32) {
-            const size_t off = (size_t)(tt * kWBN + (e >> 2)) * t.N + r0 + 8 * (e & 3);
-            *reinterpret_cast<uint4*>(a.h + off) = __ldcg(reinterpret_cast<const uint4*>(res + off));
-          }
-        } else {
-          const int np = nr >> 1;
-          for (int e = lane; e < nm * np; e += 32) {
-            const size_t off = (size_t)(tt * kWBN + e / np) * t.N + r0 + 2 * (e % np);
-            *reinterpret_cast<uint32_t*>(a.h + off) = __ldcg(reinterpret_cast<const unsigned int*>(res + off));
-          }
+        for (int e = lane; e < kWBN * 4; e += 32) {
+          const int ml = e >> 2, rv = 8 * (e & 3);
+          const int m = tt * kWBN + ml, row = r0 + rv;
+          if (m < t.M && row < t.N)
+            *reinterpret_cast<uint4*>(a.h + (size_t)m * t.N + row) =
+                __ldcg(reinterpret_cast<const uint4*>(res + ml * 32 + rv));
         }
       }
     }
@@ -397,6 +433,7 @@ static int wide_run(jsx_comm* comm, GemvArgs ga, void* workspace, size_t workspa
     JSX_REQUIRE(c.world == 1 || c.max_tiles > 0, "the comm has no tile exchange (jsx_comm_create_tiles)");
     JSX_REQUIRE(c.world == 1 || (ga.M <= c.max_tokens && ga.N <= c.hidden), "M=%d N=%d exceed the comm (%d, %d)",
                 ga.M, ga.N, c.max_tokens, c.hidden);
+    JSX_REQUIRE(c.world == 1 || ga.N % 8 == 0, "N=%d must be a multiple of 8 across ranks", ga.N);
   }
   const void* x = ga.x;
   if (ga.gamma) {
