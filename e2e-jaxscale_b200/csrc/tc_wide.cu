@@ -154,38 +154,74 @@ __device__ __forceinline__ void wide_exchange_tile(const CommDev& c, const WideA
 #pragma unroll
     for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = __float2bfloat16_rn(v[j]);
     __syncwarp();
+    // this lane's 4 vectors of the chunk: vector e = lane + 32 k is token e / 4,
+    // rows 8 (e % 4) .. + 7 of the quarter
+    uint4 part[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const int e = lane + 32 * k;  // 16-byte vector: token e / 4 of the chunk, rows 8 (e % 4) ..
-      const int tl = e >> 2, rv = 8 * (e & 3);
-      const int ml = 32 * ch + tl;  // token inside the tile
-      const uint4 part = *reinterpret_cast<const uint4*>(stg + tl * 32 + rv);
-      if (!mine) {
-        *reinterpret_cast<uint4*>(push + ml * 32 + rv) = part;
-        continue;
+      const int e = lane + 32 * k;
+      part[k] = *reinterpret_cast<const uint4*>(stg + (e >> 2) * 32 + 8 * (e & 3));
+    }
+    const int mlc = 32 * ch;  // first token of the chunk inside the tile
+    if (!mine) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = lane + 32 * k;
+        *reinterpret_cast<uint4*>(push + (mlc + (e >> 2)) * 32 + 8 * (e & 3)) = part[k];
       }
-      float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    } else {
+      // every load of the chunk is issued before any store (one round trip per source)
+      uint4 hv[4];
+      bool live[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = lane + 32 * k;
+        const int m = tt * kWBN + mlc + (e >> 2), row = ft * kWBM + 32 * q + 8 * (e & 3);
+        live[k] = m < t.M && row < t.N;
+        hv[k] = live[k] ? *reinterpret_cast<const uint4*>(a.h + (size_t)m * t.N + row) : make_uint4(0, 0, 0, 0);
+      }
+      float sum[4][8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum[k][i] = 0.f;
       for (int src = 0; src < c.world; ++src) {
-        const uint4 u = src == c.rank ? part
-                                      : __ldcg(reinterpret_cast<const uint4*>(slot_ptr(c, c.rank, jo, src, q) +
-                                                                              ml * 32 + rv));
-        float f[8];
-        unpack8(u, f);
+        uint4 u[4];
+        if (src == c.rank) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sum[i] += f[i];
+          for (int k = 0; k < 4; ++k) u[k] = part[k];
+        } else {
+          const bf16* sp = slot_ptr(c, c.rank, jo, src, q) + mlc * 32;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int e = lane + 32 * k;
+            u[k] = __ldcg(reinterpret_cast<const uint4*>(sp + (e >> 2) * 32 + 8 * (e & 3)));
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          float f[8];
+          unpack8(u[k], f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) sum[k][i] += f[i];
+        }
       }
-      const int m = tt * kWBN + ml, row = ft * kWBM + 32 * q + rv;
-      if (m >= t.M || row >= t.N) continue;
-      bf16* hp = a.h + (size_t)m * t.N + row;
-      float hf[8];
-      unpack8(*reinterpret_cast<const uint4*>(hp), hf);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) hf[i] += rbf(sum[i]);
-      uint4 out;
-      pack8(hf, out);
-      *reinterpret_cast<uint4*>(hp) = out;
-      for (int d = 0; d < c.world; ++d)
-        if (d != c.rank) *reinterpret_cast<uint4*>(result_ptr(c, d, tile, q) + ml * 32 + rv) = out;
+      for (int k = 0; k < 4; ++k) {
+        if (!live[k]) continue;
+        const int e = lane + 32 * k;
+        const int ml = mlc + (e >> 2), rv = 8 * (e & 3);
+        const int m = tt * kWBN + ml, row = ft * kWBM + 32 * q + rv;
+        float hf[8];
+        unpack8(hv[k], hf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) hf[i] += rbf(sum[k][i]);
+        uint4 out;
+        pack8(hf, out);
+        *reinterpret_cast<uint4*>(a.h + (size_t)m * t.N + row) = out;
+        for (int d = 0; d < c.world; ++d)
+          if (d != c.rank) *reinterpret_cast<uint4*>(result_ptr(c, d, tile, q) + ml * 32 + rv) = out;
+      }
     }
     __syncwarp();  // the staging buffer is refilled by the next chunk
   }
@@ -359,12 +395,17 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         wait_epoch_sys(c, rflag_ptr(c, c.rank, tile, q), epoch);
         const bf16* res = result_ptr(c, c.rank, tile, q);  // [256 tokens][32 rows]
         const int r0 = ft * kWBM + 32 * q;
-        for (int e = lane; e < kWBN * 4; e += 32) {
-          const int ml = e >> 2, rv = 8 * (e & 3);
-          const int m = tt * kWBN + ml, row = r0 + rv;
-          if (m < t.M && row < t.N)
-            *reinterpret_cast<uint4*>(a.h + (size_t)m * t.N + row) =
-                __ldcg(reinterpret_cast<const uint4*>(res + ml * 32 + rv));
+        // 32 vectors per lane, 8 loads in flight before their stores
+        for (int e0 = 0; e0 < kWBN * 4; e0 += 8 * 32) {
+          uint4 vv[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) vv[k] = __ldcg(reinterpret_cast<const uint4*>(res + 8 * (e0 + lane + 32 * k)));
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int e = e0 + lane + 32 * k;
+            const int m = tt * kWBN + (e >> 2), row = r0 + 8 * (e & 3);
+            if (m < t.M && row < t.N) *reinterpret_cast<uint4*>(a.h + (size_t)m * t.N + row) = vv[k];
+          }
         }
       }
     }
