@@ -62,6 +62,9 @@ def parse():
     ap.add_argument("--impl", choices=["jsx", "reference"], default="jsx")
     ap.add_argument("--rowpar", action="store_true",
                     help="isolated row-parallel projection: fused vs cuBLAS + NCCL (configuration 2)")
+    ap.add_argument("--prefill", action="store_true",
+                    help="prefill of --batch x --seq prompt tokens in one pass (configuration 3)")
+    ap.add_argument("--seq", type=int, default=1024, help="prompt length of --prefill")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch without programmatic dependent launch (on by default)")
     # profiling-only shape overrides (a smaller device footprint for ncu captures)
@@ -555,12 +558,101 @@ def run_rowpar(args) -> None:
         dist.destroy_process_group()
 
 
+def run_prefill(args) -> None:
+    """Configuration 3: GLM-4-9B-shaped prefill of --batch x --seq seeded uniform prompt ids
+    (random-init bf16 weights, causal, cache length --seq) in one pass per rank: wide tcgen05
+    projections, prefill attention, row-parallel products with the in-epilogue tile exchange
+    at TP > 1, and the greedy token of every sequence's last position.  Time per prefill =
+    CUDA events over --steps prefills after --warmup, max over ranks.  MFU counts the
+    matmul flops without the LM head of every position (this path computes last-position
+    logits only, the reference all of them) plus the causal attention flops."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    jsx = importlib.import_module("e2e-jaxscale_b200")
+    K = jsx.kernels
+    K.set_pdl(not args.no_pdl)
+    mesh = jsx.create_mesh(tp=world)
+    cfg = jsx.ModelConfig(num_hidden_layers=args.layers, vocab_size=args.vocab)
+    model = jsx.GLM4ForCausalLM(cfg, mesh)
+    model.init_random(seed=args.seed)
+    B = args.batch if args.batch > 1 else 32
+    S = args.seq
+    ps = jsx.PrefillState(model, B, S, S)
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g, dtype=torch.int32).to(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(max(args.warmup, 1)):
+        model.prefill(ps, ids)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler(local)
+    steps = max(args.steps, 1)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        model.prefill(ps, ids)
+    b.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if ps.comm is not None:
+        ps.comm.check()
+    H, I, nq, hd, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_attention_heads, cfg.head_dim, args.layers
+    qkv_rows = (nq + 2 * cfg.num_key_value_heads) * hd
+    mm_per_tok = 2.0 * L * H * (qkv_rows + H + 3 * I)
+    attn = 4.0 * nq * hd * (S + 1) / 2 * L
+    flops = B * S * (mm_per_tok + attn) + 2.0 * B * H * cfg.vocab_size
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        peak, peak_src = float(pk["bf16_tflops_sustained"]), "measured bf16_tflops_sustained (cuBLAS, long loop)"
+    except Exception:
+        peak, peak_src = 1400.0, "fallback sustained bf16"
+    tflops = flops / (ms * 1e-3) / 1e12
+    if rank == 0:
+        print(json.dumps({
+            "mode": "prefill", "metric": "GLM-4-9B prefill tok/s and MFU (configuration 3)",
+            "value": B * S / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_prefill": ms, "higher_is_better": True, "dtype": "bf16",
+            "data": "synthetic: random-init N(0,0.02) bf16 weights (device RNG), uniform prompt ids seed 1",
+            "config": {"workload": f"GLM-4-9B-shaped prefill, batch {B} x {S} tokens, causal, cache {S}, "
+                                   f"{args.layers} layers, TP={world}", "batch": B, "seq": S, "tp": world,
+                       "parallelism": f"tp{world}"},
+            "flops_per_prefill": flops, "achieved_tflops_per_gpu": tflops / world,
+            "mfu": tflops / world / peak, "peak_tflops": peak, "peak_source": peak_src,
+            "flops_note": "matmul flops of every position without the all-position LM head, causal attention "
+                          "flops, and the last-position LM head",
+            "clocks": clk}), flush=True)
+    mesh.close()
+    if world > 1:
+        barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
     elif args.rowpar:
         run_rowpar(args)
+    elif args.prefill:
+        run_prefill(args)
     else:
         run_gpu(args)
 

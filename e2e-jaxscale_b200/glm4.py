@@ -36,6 +36,9 @@ TC_CHUNK = K.TC_MAX_TOKENS
 # smallest batch whose projections run on the tensor cores (jsx_tc_*); smaller
 # batches stream the weights through the CUDA-core GEMV / whole-step kernel
 TC_MIN_BATCH = int(os.environ.get("JSX_TC_MIN_BATCH", "3"))
+# smallest prompt block (batch x prompt tokens) prefilled in one pass on the wide
+# tensor-core GEMM and the prefill attention; smaller prompts run token by token
+WIDE_MIN_TOKENS = int(os.environ.get("JSX_WIDE_MIN_TOKENS", "64"))
 
 
 class DecodeState:
@@ -92,9 +95,42 @@ class DecodeState:
         self.step_args = a
 
 
+class PrefillState:
+    """Device buffers of one prefill block: B sequences x S prompt tokens at
+    positions start .. start + S - 1, all processed in one pass (the reference's
+    prefill forward, models/glm4.py:162-195 with S > 1)."""
+
+    def __init__(self, model: "GLM4ForCausalLM", batch: int, seq: int, max_seq: int, caches=None,
+                 want_logits: bool = False):
+        dev, c = model.device, model.config
+        M = batch * seq
+        self.batch, self.seq, self.max_seq = batch, seq, max_seq
+        self.ids = torch.zeros(M, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(M, dtype=torch.int32, device=dev)
+        self.h = torch.zeros(M, c.hidden_size, dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros(M, model.nq_l * c.head_dim, dtype=torch.bfloat16, device=dev)
+        self.attn = torch.zeros_like(self.q)
+        self.act = torch.zeros(M, model.I_l, dtype=torch.bfloat16, device=dev)
+        self.caches = caches if caches is not None else init_kv_caches(
+            batch, max_seq, c.num_hidden_layers, c.num_key_value_heads, c.head_dim, mesh=model.mesh,
+            num_heads=c.num_attention_heads, device=dev)
+        H = c.hidden_size
+        lp = model.layers[0]
+        shapes = [tuple(reversed(lp.w_qkv.shape)), tuple(reversed(lp.w_o.shape)),
+                  tuple(reversed(lp.w_gu.shape)), tuple(reversed(lp.w_d.shape))]
+        self.ws = K.wide_workspace(M, shapes + [(H, model.V_l)], dev)
+        # the head: last prompt position of every sequence
+        self.last_h = torch.zeros(batch, H, dtype=torch.bfloat16, device=dev)
+        self.next_ids = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.logits = (torch.zeros(batch, model.V_l, dtype=torch.bfloat16, device=dev)
+                       if want_logits else None)
+        self.tc_ws = K.tc_workspace(min(batch, TC_CHUNK), [(H, model.V_l)], dev)
+        self.comm = model.mesh.comm_tiles(M, H) if model.tp > 1 else None
+
+
 class GLM4ForCausalLM:
     """models/glm4.py:198-260.  __call__ keeps the reference signature; the
-    decode fast path is step()/DecodeGraph."""
+    decode fast path is step()/DecodeGraph, the prompt fast path prefill()."""
 
     def __init__(self, config: ModelConfig, mesh, dtype=torch.bfloat16):
         c = config
@@ -230,6 +266,38 @@ class GLM4ForCausalLM:
             self.run_head(st)
         st.pos.add_(1)
 
+    # ---- prefill: the whole prompt block in one pass ----
+    def prefill_body(self, ps: PrefillState, input_ids, start: int = 0) -> None:
+        """Embedding + all decoder layers over B x S prompt tokens at positions
+        start .. start + S - 1 (models/glm4.py:162-195 at prefill; the caches
+        receive rows [start, start + S)).  input_ids: [B, S] on the device."""
+        c = self.config
+        B, S = ps.batch, ps.seq
+        eps, hd, rot, ws = c.rms_norm_eps, c.head_dim, self.rotary.rotary_dim, ps.ws
+        ps.ids.copy_(input_ids.reshape(-1))
+        ps.pos.copy_((torch.arange(S, dtype=torch.int32, device=self.device) + start).repeat(B))
+        K.embed(ps.ids, self.embed, out=ps.h)
+        for lp, cache in zip(self.layers, ps.caches):
+            K.wide_qkv_rope_cache(ps.h, lp.ln1, eps, lp.w_qkv, lp.b_qkv, self.inv_freq, ps.pos, ps.q,
+                                  cache.k, cache.v, self.nq_l, self.nkv_l, hd, rot, ws, tokens_per_seq=S)
+            K.attn_prefill(ps.q, cache.k, cache.v, self.nq_l, self.nkv_l, hd, S, start_pos=start,
+                           scale=self.scale, out=ps.attn)
+            K.wide_row_linear_allreduce(ps.comm, ps.attn, lp.w_o, ps.h, ws)
+            K.wide_gate_up_swiglu(ps.h, lp.ln2, eps, lp.w_gu, ps.act, ws)
+            K.wide_row_linear_allreduce(ps.comm, ps.act, lp.w_d, ps.h, ws)
+
+    def prefill(self, ps: PrefillState, input_ids, start: int = 0) -> torch.Tensor:
+        """prefill_body, then the final norm + LM head + greedy argmax at the last
+        prompt position of every sequence (runner.py:281); returns ps.next_ids."""
+        self.prefill_body(ps, input_ids, start)
+        ps.last_h.copy_(ps.h.view(ps.batch, ps.seq, -1)[:, -1])
+        for b0 in range(0, ps.batch, TC_CHUNK):
+            b1 = min(ps.batch, b0 + TC_CHUNK)
+            K.tc_lmhead_argmax(self.comm, ps.last_h[b0:b1], self.norm, self.config.rms_norm_eps, self.lm_head,
+                               self.vocab_offset, ps.next_ids[b0:b1], ps.tc_ws,
+                               None if ps.logits is None else ps.logits[b0:b1])
+        return ps.next_ids
+
     def kernels_per_step(self, batch: int, head: bool = True) -> int:
         tc = batch >= TC_MIN_BATCH or batch > CHUNK
         if self.fused_step and not tc:
@@ -259,6 +327,18 @@ class GLM4ForCausalLM:
             if not torch.equal(pos, cp.expand(B, S)):
                 raise ValueError("positions must equal cache_position for every sequence")
         L = kv_caches[0].k.shape[1] if kv_caches is not None else int(pos.max()) + 1
+        start = int(pos[0, 0])
+        if S > 1 and B * S >= WIDE_MIN_TOKENS and torch.equal(
+                pos, (torch.arange(S, dtype=torch.int32, device=dev) + start).expand(B, S)):
+            # one pass over the whole block; logits of every position (layers/embedding.py:88-92)
+            ps = PrefillState(self, B, S, L, caches=kv_caches)
+            self.prefill_body(ps, ids, start)
+            local = K.wide_linear(ps.h, self.lm_head, ps.ws, gamma=self.norm, eps=self.config.rms_norm_eps)
+            if self.tp > 1:
+                parts = [torch.empty_like(local) for _ in range(self.tp)]
+                dist.all_gather(parts, local, group=self.mesh.group("tensor"))
+                local = torch.cat(parts, dim=-1)
+            return local.reshape(B, S, -1), (ps.caches if kv_caches is not None else None)
         st = DecodeState(self, B, L, caches=kv_caches, want_logits=True)
         logits = torch.empty(B, S, self.config.vocab_size, dtype=torch.bfloat16, device=dev)
         for s in range(S):

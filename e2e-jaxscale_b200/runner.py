@@ -12,7 +12,7 @@ from __future__ import annotations
 
 import torch
 
-from .glm4 import DecodeGraph, DecodeState, GLM4ForCausalLM
+from .glm4 import WIDE_MIN_TOKENS, DecodeGraph, DecodeState, GLM4ForCausalLM, PrefillState
 
 NEG = -1e9
 
@@ -92,12 +92,18 @@ def greedy_generate(model, input_ids, max_new_tokens: int = 128, max_cache_len: 
         cache.v.zero_()
     st.pos.zero_()
     host_ids = ids.pin_memory() if torch.cuda.is_available() else ids
-    for s in range(S):
-        st.ids.copy_(host_ids[:, s].to(dev, non_blocking=True))
-        if s < S - 1:
-            g.prefill()
-        else:
-            g.decode()
+    if S > 1 and B * S >= WIDE_MIN_TOKENS:
+        # the whole prompt in one pass (wide tensor-core projections + prefill attention)
+        ps = PrefillState(jm.model, B, S, L, caches=st.caches)
+        st.ids.copy_(jm.model.prefill(ps, host_ids.to(dev, non_blocking=True)))
+        st.pos.fill_(S)
+    else:
+        for s in range(S):
+            st.ids.copy_(host_ids[:, s].to(dev, non_blocking=True))
+            if s < S - 1:
+                g.prefill()
+            else:
+                g.decode()
     out = [st.ids.to("cpu")]
     for _ in range(max_new_tokens - 1):
         g.decode()
