@@ -59,6 +59,9 @@ __global__ void __launch_bounds__(kPfThreads, 2) k_attn_prefill(PfArgs a) {
   const int nkb = (kend + kPfKeys - 1) / kPfKeys;
   const size_t qstride = (size_t)a.nq * kPfHd;
   const size_t rs = (size_t)a.nkv * kPfHd;
+  // q and the new cache rows come from the previous kernel (launched with
+  // programmatic dependent launch, it may still be running)
+  pdl_wait();
 
   const bf16* qg = a.q + (size_t)(b * a.S + i0) * qstride + h * kPfHd;
   for (int e = tid; e < kPfRows * 16; e += kPfThreads) {

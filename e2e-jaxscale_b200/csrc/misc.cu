@@ -44,6 +44,7 @@ __device__ __forceinline__ void pack_source(const PackArgs& a, int R, int& which
 
 __global__ void k_pack(PackArgs a) {
   __shared__ bf16 tile[32][33];
+  pdl_wait();  // the source may come from the previous kernel
   const int R0 = blockIdx.x * 32, k0 = blockIdx.y * 32;
   const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
   for (int i = ty; i < 32; i += 8) {
