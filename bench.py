@@ -65,6 +65,8 @@ def parse():
     ap.add_argument("--prefill", action="store_true",
                     help="prefill of --batch x --seq prompt tokens in one pass (configuration 3)")
     ap.add_argument("--seq", type=int, default=1024, help="prompt length of --prefill")
+    ap.add_argument("--flash", action="store_true",
+                    help="GLM-4.7-Flash-shaped MoE + MLA decode, 4-layer slice (configuration 4)")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch without programmatic dependent launch (on by default)")
     # profiling-only shape overrides (a smaller device footprint for ncu captures)
@@ -645,6 +647,89 @@ def run_prefill(args) -> None:
         dist.destroy_process_group()
 
 
+def run_flash(args) -> None:
+    """Configuration 4: GLM-4.7-Flash-shaped MoE decode on a 4-layer slice (hidden 2048, MLA with
+    q_lora 768 / kv_lora 512 / nope 192 / rope 64 / v 256 / 20 heads, 64 routed experts of 1536
+    with top-4 softmax routing and one shared expert of 1536, a dense SwiGLU MLP of 10240 in
+    layer 0), random-init bf16 weights N(0, 0.02), batch 1 and 32 at context 1024 (the cache
+    rows before the position hold seeded random values).  Each step is the reference-signature
+    forward of one token per sequence through GLM4FlashForCausalLM (eager layer calls, not a
+    captured graph); time per step = CUDA events over --steps steps after --warmup, max over
+    ranks.  Mesh: TP = min(2, N), EP = N / TP."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    jsx = importlib.import_module("e2e-jaxscale_b200")
+    K = jsx.kernels
+    K.set_pdl(not args.no_pdl)
+    tp = min(2, world)
+    mesh = jsx.create_mesh(tp=tp, ep=world // tp)
+    cfg = jsx.ModelConfig(hidden_size=2048, num_hidden_layers=4, num_attention_heads=20, num_key_value_heads=20,
+                          intermediate_size=10240, vocab_size=args.vocab, rms_norm_eps=1e-5,
+                          rope_theta=1000000.0, n_routed_experts=64, n_shared_experts=1, num_experts_per_tok=4,
+                          moe_intermediate_size=1536, routed_scaling_factor=1.8, norm_topk_prob=True,
+                          first_k_dense_replace=1, q_lora_rank=768, kv_lora_rank=512, qk_nope_head_dim=192,
+                          qk_rope_head_dim=64, v_head_dim=256, attention_bias=False, partial_rotary_factor=1.0)
+    model = jsx.GLM4FlashForCausalLM(cfg, mesh)
+    model.init_random(seed=args.seed)
+    ctx = args.ctx
+    out = {}
+    for B in (1, 32):
+        L = ctx + args.warmup + max(args.steps, 1) + 1
+        caches = model.init_kv_caches(B, L)
+        g = torch.Generator(device=dev).manual_seed(7)
+        for c_ in caches:
+            c_.k[:, :ctx].normal_(generator=g)
+            c_.v[:, :ctx].normal_(generator=g)
+        ids = np.random.default_rng(1).integers(0, cfg.vocab_size, (B, 1))
+        pos = ctx
+
+        def step():
+            nonlocal pos, ids
+            logits, _ = model(ids, np.full((B, 1), pos), None, kv_caches=caches, cache_position=[pos])
+            pos += 1
+            return logits
+
+        for _ in range(max(args.warmup, 1)):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(max(args.steps, 1)):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / max(args.steps, 1)
+        if world > 1:
+            t = torch.tensor([ms], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        out[f"batch_{B}"] = {"value": B / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms}
+        del caches
+    if rank == 0:
+        print(json.dumps({"mode": "flash", "metric": "GLM-4.7-Flash-shaped MoE decode tok/s (configuration 4)",
+                          "n_gpus": world, "mesh": {"tensor": tp, "expert": world // tp}, "steps": args.steps,
+                          "warmup": args.warmup, "dtype": "bf16", "context": ctx,
+                          "data": "synthetic: random-init N(0,0.02) bf16 weights, random cache rows, seeded ids",
+                          "config": {"workload": "GLM-4.7-Flash-shaped 4-layer slice, decode, context "
+                                                 f"{ctx}, TP={tp} x EP={world // tp}"},
+                          "note": "eager per-layer calls (host launch cost included), not a captured graph",
+                          **out}), flush=True)
+    mesh.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -653,6 +738,8 @@ def main():
         run_rowpar(args)
     elif args.prefill:
         run_prefill(args)
+    elif args.flash:
+        run_flash(args)
     else:
         run_gpu(args)
 

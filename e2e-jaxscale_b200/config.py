@@ -32,6 +32,10 @@ class ModelConfig:
     topk_method: str = "greedy"
     norm_topk_prob: bool = True
     first_k_dense_replace: int = 0
+    # width of the MoE layers' shared expert; None: moe_intermediate_size x n_shared_experts (the
+    # GLM-4.7-Flash checkpoint's shape, which replaces the reference's intermediate_size placeholder
+    # at load time, layers/linear.py:45-49)
+    shared_expert_intermediate_size: int | None = None
     q_lora_rank: int | None = None
     kv_lora_rank: int | None = None
     qk_nope_head_dim: int | None = None
@@ -47,6 +51,12 @@ class ModelConfig:
                 self.head_dim = self.qk_nope_head_dim + self.qk_rope_head_dim
             else:
                 self.head_dim = self.hidden_size // self.num_attention_heads
+
+    @property
+    def shared_intermediate_size(self) -> int:
+        if self.shared_expert_intermediate_size is not None:
+            return self.shared_expert_intermediate_size
+        return self.moe_intermediate_size * (self.n_shared_experts or 1)
 
     @property
     def is_moe(self) -> bool:

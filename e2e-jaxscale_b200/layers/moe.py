@@ -153,3 +153,34 @@ class MoELayer:
             K.gate_up_swiglu(x[n0:n1], None, 0.0, self.s_gu, act[n0:n1])
             K.row_linear_allreduce_add(comm, act[n0:n1], self.s_d, routed[n0:n1], out[n0:n1])
         return out.reshape(hidden_states.shape)
+
+
+class DenseMLP:
+    """layers/moe.py:270-300: down(silu(gate(x)) * up(x)) for the first_k_dense_replace
+    layers of GLM-4.7-Flash, gate/up column-parallel and down row-parallel over the
+    tensor axis like GLM-4-9B's MLP: jsx_gate_up_swiglu on this rank's gate/up slice,
+    then the down projection with its fused all-reduce."""
+
+    def __init__(self, hidden_size: int, intermediate_size: int, mesh, dtype=torch.bfloat16):
+        self.hidden_size = hidden_size
+        self.gate_proj = LinearBase(hidden_size, intermediate_size, mesh, params_dtype=dtype,
+                                    kernel_axes=(None, "tensor"))
+        self.up_proj = LinearBase(hidden_size, intermediate_size, mesh, params_dtype=dtype,
+                                  kernel_axes=(None, "tensor"))
+        self.down_proj = LinearBase(intermediate_size, hidden_size, mesh, params_dtype=dtype,
+                                    kernel_axes=("tensor", None))
+        self._key = None
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        dev = x.device
+        key = (id(self.gate_proj.weight.value), id(self.up_proj.weight.value), str(dev))
+        if self._key != key:
+            self.w_gu = K.pack_gate_up(self.gate_proj.local_weight(dev), self.up_proj.local_weight(dev))
+            self._key = key
+        H = self.hidden_size
+        x2 = x.reshape(-1, H).contiguous()
+        act = torch.empty(x2.shape[0], self.w_gu.shape[0] // 2, dtype=torch.bfloat16, device=dev)
+        for m0 in range(0, x2.shape[0], K.MAX_DECODE_TOKENS):
+            m1 = min(x2.shape[0], m0 + K.MAX_DECODE_TOKENS)
+            K.gate_up_swiglu(x2[m0:m1], None, 0.0, self.w_gu, act[m0:m1])
+        return self.down_proj(act).reshape(x.shape)

@@ -436,3 +436,60 @@ def mla_attention(p: MLAParams, x, positions, mask, kv, cache_position, nh, nope
     probs = bf16(e / e.sum(axis=-1, keepdims=True, dtype=np.float32))
     out = bf16(np.einsum("bhsl,blhd->bshd", probs, vc, dtype=np.float32)).reshape(B, S, nh * vdim)
     return linear(out, p.o)
+
+
+# ---------------------------------------------------------------------------
+# GLM-4.7-Flash decoder (models/glm4_flash.py:26-205): MLA attention in every
+# layer, a dense SwiGLU MLP in the first first_k_dense_replace layers
+# (layers/moe.py:270-300), the MoE layer after; pre-norm with bf16 residual adds
+# ---------------------------------------------------------------------------
+
+@dataclass
+class FlashLayerParams:
+    ln1: np.ndarray
+    mla: MLAParams
+    ln2: np.ndarray
+    dense: tuple | None = None   # (wg, wu, wd) [in, out]
+    moe: dict | None = None      # router, bias, eg, eu, ed, sg, su, sd
+
+
+@dataclass
+class FlashParams:
+    embed: np.ndarray
+    layers: list
+    norm: np.ndarray
+    lm_head: np.ndarray          # [V, H]
+    nh: int
+    nope: int
+    rope_d: int
+    vdim: int
+    eps: float
+    rope_theta: float
+    top_k: int
+    scale: float
+    norm_topk: bool = True
+
+
+def flash_forward(p: FlashParams, input_ids, positions, mask, kv_caches, cache_position):
+    """GLM4FlashForCausalLM.__call__ (models/glm4_flash.py:93-110, :140-205): logits
+    [B, S, V] (bf16 values); kv_caches [(k, v)] per layer updated in place."""
+    inv = rope_inv_freq(p.rope_d, theta=p.rope_theta, partial=1.0)
+    h = p.embed[np.asarray(input_ids)]
+    for lp, kv in zip(p.layers, kv_caches):
+        r = h
+        x = rmsnorm(h, lp.ln1, p.eps)
+        a = mla_attention(lp.mla, x, positions, mask, kv, cache_position, p.nh, p.nope, p.rope_d, p.vdim,
+                          p.eps, inv)
+        h = bf16(r + a)
+        r = h
+        x = rmsnorm(h, lp.ln2, p.eps)
+        if lp.dense is not None:
+            wg, wu, wd = lp.dense
+            y = linear(bf16(silu(linear(x, wg)) * linear(x, wu)), wd)
+        else:
+            m = lp.moe
+            y = moe_layer(x, m["router"], m["bias"], p.top_k, p.scale, p.norm_topk, m["eg"], m["eu"], m["ed"],
+                          m["sg"], m["su"], m["sd"])
+        h = bf16(r + y)
+    hn = rmsnorm(h, p.norm, p.eps)
+    return bf16(np.einsum("bsh,vh->bsv", hn, p.lm_head, dtype=np.float32))
