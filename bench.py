@@ -653,9 +653,10 @@ def run_flash(args) -> None:
     with top-4 softmax routing and one shared expert of 1536, a dense SwiGLU MLP of 10240 in
     layer 0), random-init bf16 weights N(0, 0.02), batch 1 and 32 at context 1024 (the cache
     rows before the position hold seeded random values).  Each step is the reference-signature
-    forward of one token per sequence through GLM4FlashForCausalLM (eager layer calls, not a
-    captured graph); time per step = CUDA events over --steps steps after --warmup, max over
-    ranks.  Mesh: TP = min(2, N), EP = N / TP."""
+    forward of one token per sequence through GLM4FlashForCausalLM on device-resident ids and
+    positions, captured once in a CUDA graph (the position advances inside the graph) and
+    replayed; time per step = CUDA events over --steps replays after --warmup, max over ranks.
+    Mesh: TP = min(2, N), EP = N / TP."""
     import torch
     import torch.distributed as dist
 
@@ -688,26 +689,30 @@ def run_flash(args) -> None:
         for c_ in caches:
             c_.k[:, :ctx].normal_(generator=g)
             c_.v[:, :ctx].normal_(generator=g)
-        ids = np.random.default_rng(1).integers(0, cfg.vocab_size, (B, 1))
-        pos = ctx
+        ids = torch.from_numpy(np.random.default_rng(1).integers(0, cfg.vocab_size, (B, 1)).astype(np.int32)).to(dev)
+        pos = torch.full((B, 1), ctx, dtype=torch.int32, device=dev)
 
         def step():
-            nonlocal pos, ids
-            logits, _ = model(ids, np.full((B, 1), pos), None, kv_caches=caches, cache_position=[pos])
-            pos += 1
-            return logits
+            model(ids, pos, None, kv_caches=caches, cache_position=None)
+            pos.add_(1)
 
-        for _ in range(max(args.warmup, 1)):
+        for _ in range(max(args.warmup, 1)):  # eager: creates every lazily built resource
             step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        pos.fill_(ctx + max(args.warmup, 1))
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(max(args.steps, 1)):
-            step()
+            graph.replay()
         b.record()
         torch.cuda.synchronize()
+        del graph
         ms = a.elapsed_time(b) / max(args.steps, 1)
         if world > 1:
             t = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -722,7 +727,7 @@ def run_flash(args) -> None:
                           "data": "synthetic: random-init N(0,0.02) bf16 weights, random cache rows, seeded ids",
                           "config": {"workload": "GLM-4.7-Flash-shaped 4-layer slice, decode, context "
                                                  f"{ctx}, TP={tp} x EP={world // tp}"},
-                          "note": "eager per-layer calls (host launch cost included), not a captured graph",
+                          "note": "one decode step captured in a CUDA graph and replayed",
                           **out}), flush=True)
     mesh.close()
     if world > 1:

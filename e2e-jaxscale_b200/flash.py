@@ -115,7 +115,9 @@ class GLM4FlashForCausalLM:
         return [KVCache(mk(qd), mk(c.v_head_dim)) for _ in self.layers]
 
     def __call__(self, input_ids, positions, attention_mask=None, kv_caches=None, cache_position=None):
-        ids = torch.as_tensor(np.asarray(input_ids), dtype=torch.int32)
+        """input_ids / positions: host arrays, or device tensors (then the call issues no
+        host<->device copy and can be captured in a CUDA graph; pass cache_position=None)."""
+        ids = input_ids if torch.is_tensor(input_ids) else torch.as_tensor(np.asarray(input_ids), dtype=torch.int32)
         h = self.embed_tokens(ids)
         new = []
         for i, lyr in enumerate(self.layers):

@@ -90,7 +90,10 @@ class MLAAttention:
         B, S, H = hidden_states.shape
         nh, nope, rope, vd = self.local_heads, self.qk_nope_head_dim, self.qk_rope_head_dim, self.v_head_dim
         qd = nope + rope
-        pos = torch.as_tensor(np.array(positions)).to(device=dev, dtype=torch.int32).reshape(B, S)
+        if torch.is_tensor(positions):  # device positions: no host round trip (graph capture)
+            pos = positions.to(device=dev, dtype=torch.int32).reshape(B, S)
+        else:
+            pos = torch.as_tensor(np.array(positions)).to(device=dev, dtype=torch.int32).reshape(B, S)
         if cache_position is not None:
             cp = torch.as_tensor(np.array(cache_position)).to(device=dev, dtype=torch.int32).reshape(1, S)
             if not torch.equal(pos, cp.expand(B, S)):

@@ -15,9 +15,16 @@ class RMSNorm:
         self.epsilon = epsilon
         self.param_dtype = param_dtype
         self.scale = Param(torch.ones(hidden_size, dtype=torch.float32))
+        self._gain = None
+        self._key = None
 
     def gain(self, device) -> torch.Tensor:
-        return to_device(self.scale.value, device)
+        """The gain on `device` (bf16), converted once per assigned value."""
+        key = (id(self.scale.value), str(device))
+        if self._key != key:
+            self._gain = to_device(self.scale.value, device)
+            self._key = key
+        return self._gain
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return K.rmsnorm(x.contiguous(), self.gain(x.device), self.epsilon)
