@@ -1,6 +1,6 @@
 """Generates tests/golden/reference_golden.npz by executing the REFERENCE's own
-source files (layers/*.py incl. the MoE layer, models/glm4.py, runner.py of
-sdh1014/e2e-JaxScale)
+source files (layers/*.py incl. the MoE and MLA layers, models/glm4.py,
+models/glm4_flash.py, runner.py of sdh1014/e2e-JaxScale)
 on the CPU through the numpy stand-in under tests/golden/jaxshim/ (JAX and Flax
 are not installable here).  The fixture pins the oracle (oracle/glm4_ref.py)
 to the reference's composition of operations: where it rounds to bf16, adds
@@ -201,6 +201,55 @@ def main():
     ym2, cm2 = mla(hm2, np.full((B, 1), S, np.int32), runner.make_decode_mask(S, L, dtype=BF), kv_cache=cm,
                    cache_position=np.array([S], np.int32))
     out.update(mla_h=hm, mla_y=ym, mla_h2=hm2, mla_y2=ym2, mla_k=cm2.k, mla_v=cm2.v)
+
+    # GLM-4.7-Flash model (models/glm4_flash.py): MLA in every layer, a dense MLP in layer 0,
+    # MoE (8 experts, top-4, shared expert of 64) in layers 1-2; a 4-token prefill and one
+    # decode step through the reference's own model class
+    from models.glm4_flash import GLM4FlashForCausalLM  # reference
+    fcfg = ModelConfig(hidden_size=256, num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=4,
+                       intermediate_size=192, vocab_size=1000, rms_norm_eps=1e-5, rope_theta=1000000.0,
+                       n_routed_experts=8, n_shared_experts=1, num_experts_per_tok=4, moe_intermediate_size=64,
+                       routed_scaling_factor=1.8, norm_topk_prob=True, first_k_dense_replace=1, q_lora_rank=96,
+                       kv_lora_rank=64, qk_nope_head_dim=48, qk_rope_head_dim=16, v_head_dim=64,
+                       attention_bias=False)
+    fm = GLM4FlashForCausalLM(fcfg, mesh1, dtype=BF)
+    fm.model.embed_tokens.embedding.value = rnd((1000, 256), 0.05)
+    out["flash_embed"] = fm.model.embed_tokens.embedding.value
+    for i, lay in enumerate(fm.model.layers):
+        at = lay.self_attn
+        for name, shp in {"q_a_proj": (256, 96), "q_b_proj": (96, 4 * 64), "kv_a_proj_with_mqa": (256, 64 + 16),
+                          "kv_b_proj": (64, 4 * (48 + 64)), "o_proj": (4 * 64, 256)}.items():
+            getattr(at, name).weight.value = rnd(shp, 0.05)
+            out[f"flash_{i}_{name}"] = getattr(at, name).weight.value
+        if i == 0:
+            for name, shp in {"gate_proj": (256, 192), "up_proj": (256, 192), "down_proj": (192, 256)}.items():
+                getattr(lay.mlp, name).weight.value = rnd(shp, 0.05)
+                out[f"flash_{i}_{name}"] = getattr(lay.mlp, name).weight.value
+        else:
+            mo = lay.mlp
+            mo.gate.weight.weight.value = rnd((256, 8), 0.05)
+            mo.expert_gate_weight.value = rnd((8, 256, 64), 0.05)
+            mo.expert_up_weight.value = rnd((8, 256, 64), 0.05)
+            mo.expert_down_weight.value = rnd((8, 64, 256), 0.05)
+            mo.shared_experts.gate_proj.weight.value = rnd((256, 64), 0.05)
+            mo.shared_experts.up_proj.weight.value = rnd((256, 64), 0.05)
+            mo.shared_experts.down_proj.weight.value = rnd((64, 256), 0.05)
+            out.update({f"flash_{i}_router": mo.gate.weight.weight.value, f"flash_{i}_eg": mo.expert_gate_weight.value,
+                        f"flash_{i}_eu": mo.expert_up_weight.value, f"flash_{i}_ed": mo.expert_down_weight.value,
+                        f"flash_{i}_sg": mo.shared_experts.gate_proj.weight.value,
+                        f"flash_{i}_su": mo.shared_experts.up_proj.weight.value,
+                        f"flash_{i}_sd": mo.shared_experts.down_proj.weight.value})
+    fm.lm_head.embedding.value = rnd((1000, 256), 0.05)
+    out["flash_lm_head"] = fm.lm_head.embedding.value
+    Bf, Sf, Lf = 2, 4, 8
+    fprompt = np.random.default_rng(3).integers(0, 1000, (Bf, Sf)).astype(np.int32)
+    fkv = [KVCache(k=np.zeros((Bf, Lf, 4, 64), BF), v=np.zeros((Bf, Lf, 4, 64), BF)) for _ in range(3)]
+    flg, fkv = fm(fprompt, runner.make_positions(Sf, Bf), runner.make_prefill_mask(Sf, Lf, dtype=BF),
+                  kv_caches=fkv, cache_position=np.arange(Sf, dtype=np.int32))
+    fnext = np.argmax(np.asarray(flg[:, -1], np.float32), axis=-1).astype(np.int32)[:, None]
+    flg2, fkv = fm(fnext, np.full((Bf, 1), Sf, np.int32), runner.make_decode_mask(Sf, Lf, dtype=BF),
+                   kv_caches=fkv, cache_position=np.array([Sf], np.int32))
+    out.update(flash_prompt=fprompt, flash_logits=flg, flash_next=fnext, flash_logits2=flg2)
 
     ser = {}
     for k_, v in out.items():

@@ -1,5 +1,6 @@
 """Pins the CPU oracle to the reference's own code: tests/golden/reference_golden.npz
-was produced by running the reference's layers/, models/glm4.py and runner.py
+was produced by running the reference's layers/, models/glm4.py, models/glm4_flash.py
+and runner.py
 (through the numpy stand-in for jax/flax, tests/golden/make_golden.py).  The
 oracle must reproduce every recorded output bit for bit on the same inputs."""
 
@@ -111,3 +112,36 @@ def test_mla_attention_prefill_then_decode(ref, g):
     same(y2, g["mla_y2"])
     same(kc, g["mla_k"])
     same(vc, g["mla_v"])
+
+
+def flash_params_from_golden(ref, g, layers=3, hidden=256):
+    """The reference GLM4FlashForCausalLM's weights as recorded by make_golden.py."""
+    out = []
+    for i in range(layers):
+        mla = ref.MLAParams(q_a=g[f"flash_{i}_q_a_proj"], q_a_ln=np.ones(96, np.float32), q_b=g[f"flash_{i}_q_b_proj"],
+                            kv_a=g[f"flash_{i}_kv_a_proj_with_mqa"], kv_a_ln=np.ones(64, np.float32),
+                            kv_b=g[f"flash_{i}_kv_b_proj"], o=g[f"flash_{i}_o_proj"])
+        ones = np.ones(hidden, np.float32)
+        if i == 0:
+            out.append(ref.FlashLayerParams(ln1=ones, mla=mla, ln2=ones,
+                                            dense=(g["flash_0_gate_proj"], g["flash_0_up_proj"],
+                                                   g["flash_0_down_proj"])))
+        else:
+            out.append(ref.FlashLayerParams(ln1=ones, mla=mla, ln2=ones, moe=dict(
+                router=g[f"flash_{i}_router"], bias=None, eg=g[f"flash_{i}_eg"], eu=g[f"flash_{i}_eu"],
+                ed=g[f"flash_{i}_ed"], sg=g[f"flash_{i}_sg"], su=g[f"flash_{i}_su"], sd=g[f"flash_{i}_sd"])))
+    return ref.FlashParams(embed=g["flash_embed"], layers=out, norm=np.ones(hidden, np.float32),
+                           lm_head=g["flash_lm_head"], nh=4, nope=48, rope_d=16, vdim=64, eps=1e-5,
+                           rope_theta=1000000.0, top_k=4, scale=1.8)
+
+
+def test_flash_model_prefill_then_decode(ref, g):
+    """models/glm4_flash.py (GLM4FlashForCausalLM: MLA, dense MLP in layer 0, MoE after)."""
+    p = flash_params_from_golden(ref, g)
+    B, S, L = 2, 4, 8
+    kv = [(np.zeros((B, L, 4, 64), np.float32), np.zeros((B, L, 4, 64), np.float32)) for _ in range(3)]
+    lg = ref.flash_forward(p, g["flash_prompt"], np.broadcast_to(np.arange(S), (B, S)), ref.make_prefill_mask(S, L),
+                           kv, np.arange(S))
+    same(lg, g["flash_logits"])
+    lg2 = ref.flash_forward(p, g["flash_next"], np.full((B, 1), S), ref.make_decode_mask(S, L), kv, [S])
+    same(lg2, g["flash_logits2"])
