@@ -172,6 +172,12 @@ class GLM4ForCausalLM:
         del lm
         torch.cuda.synchronize(dev)
 
+    def load_weights(self, model_config: ModelConfig | None = None) -> None:
+        """models/glm4.py:262-274: this rank's shards of the HF safetensors checkpoint in
+        (model_config or self.config).model_path (checkpoint.py holds the name mapping)."""
+        from .checkpoint import load_glm4
+        load_glm4(self, (model_config or self.config).model_path)
+
     def init_random(self, seed: int = 0) -> None:
         """Synthetic N(0, 0.02) bf16 weights generated on the device, gains = 1."""
         dev, c = self.device, self.config

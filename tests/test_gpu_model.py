@@ -296,3 +296,21 @@ def test_fused_step_batch8_full_width(jsx, ref, cuda, gemv_batches):
     model.fused_step = True
     for x, y in zip(out[False], out[True]):
         assert np.array_equal(x, y)
+
+
+def test_load_weights_from_safetensors(jsx, ref, cuda, tmp_path):
+    """GLM4ForCausalLM.load_weights on an HF-named safetensors checkpoint packs exactly
+    the weights that load_state packs from the same reference-layout parameters."""
+    from test_checkpoint import hf_checkpoint
+    rc = small_cfg(ref)
+    params = ref.init_params(rc, seed=14)
+    cfg = to_model_config(jsx, rc)
+    cfg.model_path = hf_checkpoint(ref, tmp_path, rc, params)
+    a = jsx.GLM4ForCausalLM(cfg, jsx.create_mesh(1))
+    a.load_state(params)
+    b = jsx.GLM4ForCausalLM(cfg, jsx.create_mesh(1))
+    b.load_weights()
+    for la, lb in zip(a.layers, b.layers):
+        for n in ("ln1", "w_qkv", "b_qkv", "w_o", "ln2", "w_gu", "w_d"):
+            assert torch.equal(getattr(la, n), getattr(lb, n)), n
+    assert torch.equal(a.embed, b.embed) and torch.equal(a.norm, b.norm) and torch.equal(a.lm_head, b.lm_head)
