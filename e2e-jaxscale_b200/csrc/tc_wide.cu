@@ -26,8 +26,6 @@
 // No multicast.  Every mbarrier wait is time-bounded; on a timeout the kernel
 // sets its error word (jsx_device_error), the other roles stop at their next
 // wait, copies and MMAs in flight are drained (bounded) and TMEM is freed.
-#include <stdio.h>
-
 #include "comm.cuh"
 #include "common.cuh"
 #include "gemv_core.cuh"
@@ -53,6 +51,8 @@ constexpr size_t kWOffXn = 1024;  // workspace: header, then the RMS-normalised 
 
 static_assert(kWBN % 32 == 0 && kWBN <= 256, "token tile: MMA N and TMA box limit");
 static_assert(kWTmemCols <= 512, "two accumulators in the SM's TMEM");
+static_assert(kWBM == kXTileRows && kWBN == kXTileTokens && kWBM == 32 * kXQuarters,
+              "the tile exchange's slots hold one output tile, one quarter per epilogue warp");
 
 static __device__ uint32_t g_wide_error;
 
