@@ -64,6 +64,7 @@ SIGNATURES = {
     "jsx_tc_lmhead_argmax": [P, P, P, F, P, I, I, I, I, P, P, P, SZ, P],
     "jsx_wide_workspace_size": [I, I, I, I, P],
     "jsx_attn_prefill": [P, P, P, P, I, I, I, I, I, I, I, F, P],
+    "jsx_sample": [P, P, P, P, I, I, F, F, I, F, P],
     "jsx_wide_linear": [P, P, F, P, P, P, I, I, I, P, SZ, P],
     "jsx_wide_qkv_rope_cache": [P, P, F, P, P, P, P, P, P, P, I, I, I, I, I, I, I, I, P, SZ, P],
     "jsx_wide_gate_up_swiglu": [P, P, F, P, P, I, I, I, P, SZ, P],

@@ -279,6 +279,25 @@ def attn_prefill(q, k_cache, v_cache, nq, nkv, head_dim, S, start_pos=0, scale=N
     return out
 
 
+def sample(logits, gumbel, presence=None, repetition_penalty=1.0, temperature=1.0, top_k=0, top_p=1.0,
+           out=None):
+    """runner.py:315-359: next tokens [B] int32 from logits [B, V] bf16; gumbel [B, k] bf16 is the
+    categorical draw's noise for the k = (top_k or 200) candidates; presence [B, V] bool/uint8."""
+    _need(logits, "logits")
+    _need(gumbel, "gumbel")
+    B, V = logits.shape
+    pres = None
+    if presence is not None:
+        pres = presence.to(torch.uint8).contiguous()
+        if pres.shape != logits.shape or pres.device != logits.device:
+            raise ValueError("presence must be [B, V] on the logits' device")
+    out = torch.empty(B, dtype=torch.int32, device=logits.device) if out is None else _need(out, "out", torch.int32)
+    call("jsx_sample", _p(logits), None if pres is None else ctypes.c_void_p(pres.data_ptr()), _p(gumbel),
+         _p(out), B, V, ctypes.c_float(repetition_penalty), ctypes.c_float(temperature), top_k,
+         ctypes.c_float(top_p), _stream())
+    return out
+
+
 # ---- wide tensor-core projections (prefill / many tokens) ----------------------------
 def wide_workspace(M, shapes, device, norm=True) -> torch.Tensor:
     """Workspace for every (K, N) in shapes at M tokens (with room for the

@@ -216,6 +216,20 @@ int jsx_tc_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, 
                          int hidden, void* logits_out, int32_t* ids_out, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* ---- sampling --------------------------------------------------------------
+ * The reference's _jit_sample (runner.py:315-359) for one token per sequence:
+ * repetition penalty on the tokens flagged in presence[B][V] (x / rp when x > 0,
+ * else x * rp; presence may be NULL), temperature (skipped at 1), the top-k
+ * candidates (top_k <= 0 means 200, like the reference; k <= 256), top-p on the
+ * k candidates (a candidate whose preceding probability mass reaches top_p is
+ * dropped), then the categorical draw argmax(value + gumbel): gumbel[B][k] is
+ * the caller's Gumbel noise, one value per candidate in top-k order (values
+ * descending, lower index first on ties).  bf16 arithmetic as the reference's,
+ * with rp and temperature rounded to bf16.  tokens_out[B] int32. */
+int jsx_sample(const void* logits, const uint8_t* presence, const void* gumbel, int32_t* tokens_out,
+               int B, int V, float repetition_penalty, float temperature, int top_k, float top_p,
+               void* stream);
+
 /* ---- wide tensor-core projections (prefill, many tokens) ---------------------
  * The column-parallel and single-rank row-parallel projections of
  * LinearBase.__call__ (layers/linear.py:57-82) over a whole [B, S] token block

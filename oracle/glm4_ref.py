@@ -493,3 +493,40 @@ def flash_forward(p: FlashParams, input_ids, positions, mask, kv_caches, cache_p
         h = bf16(r + y)
     hn = rmsnorm(h, p.norm, p.eps)
     return bf16(np.einsum("bsh,vh->bsv", hn, p.lm_head, dtype=np.float32))
+
+
+# ---------------------------------------------------------------------------
+# sampling (runner.py:315-359, _jit_sample) with the categorical draw's Gumbel
+# noise given (jax.random.categorical = argmax(logits + gumbel noise))
+# ---------------------------------------------------------------------------
+
+def sample_tokens(logits, presence, gumbel, repetition_penalty, temperature, top_k, top_p):
+    """logits [B, V] (bf16 values), presence [B, V] bool or None, gumbel [B, k] (bf16
+    values, one per top-k candidate in lax.top_k order).  bf16 arithmetic with the
+    Python scalars rounded to bf16 (weak typing).  Returns (tokens [B] int32, the
+    smallest |preceding mass - top_p| over the candidates of each row, for
+    near-tie reporting)."""
+    x = bf16(logits)
+    rp = np.float32(bf16(np.float32(repetition_penalty)))
+    pen = bf16(np.where(x > 0, x / rp, x * rp))
+    if presence is not None:
+        x = np.where(np.asarray(presence, bool), pen, x)
+    if temperature != 1.0:
+        x = bf16(x / np.float32(bf16(np.float32(temperature))))
+    k = top_k if top_k > 0 else 200
+    B = x.shape[0]
+    tokens = np.zeros(B, np.int32)
+    margins = np.full(B, np.inf, np.float32)
+    for b in range(B):
+        order = np.argsort(-x[b], kind="stable")[:k]   # lax.top_k: descending, lower index first on ties
+        vals = x[b, order].astype(np.float32)
+        if top_p < 1.0:
+            e = np.exp(vals - vals.max(), dtype=np.float32)
+            probs = (e / e.sum(dtype=np.float32)).astype(np.float32)
+            cum = np.cumsum(probs, dtype=np.float32)
+            before = cum - probs
+            margins[b] = np.min(np.abs(before - np.float32(top_p)))
+            vals = np.where(before >= np.float32(top_p), np.float32(bf16(np.float32(-1e9))), vals)
+        z = bf16(vals + np.asarray(gumbel[b], np.float32))
+        tokens[b] = order[int(np.argmax(z))]
+    return tokens, margins

@@ -85,3 +85,15 @@ def test_moe_gate_weights(ref):
 
 def test_argmax_ties_pick_first(ref):
     assert ref.argmax_first(np.array([[1.0, 3.0, 3.0, 2.0]]))[0] == 1
+
+
+def test_sample_tokens_limits(ref):
+    """The sampling restatement: zero noise and no filtering is the first argmax; a
+    top-p that keeps only the leading candidate returns it whatever the noise."""
+    rng = np.random.default_rng(0)
+    lg = ref.bf16(rng.standard_normal((3, 500), dtype=np.float32))
+    tok, _ = ref.sample_tokens(lg, None, np.zeros((3, 200), np.float32), 1.0, 1.0, 0, 1.0)
+    assert np.array_equal(tok, ref.argmax_first(lg))
+    noise = ref.bf16(rng.standard_normal((3, 10), dtype=np.float32) * np.float32(5.0))
+    tok, _ = ref.sample_tokens(lg, None, noise, 1.0, 1.0, 10, 1e-6)
+    assert np.array_equal(tok, ref.argmax_first(lg))
