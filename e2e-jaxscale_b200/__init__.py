@@ -10,6 +10,6 @@ from .config import ModelConfig  # noqa: F401
 from .glm4 import DecodeGraph, DecodeState, GLM4ForCausalLM, PrefillState  # noqa: F401
 from .flash import GLM4FlashForCausalLM  # noqa: F401
 from .mesh import Comm, Mesh, create_mesh  # noqa: F401
-from .runner import JittedModel, greedy_generate  # noqa: F401
+from .runner import JittedModel, greedy_generate, sample_generate  # noqa: F401
 
 __version__ = "0.1.0"

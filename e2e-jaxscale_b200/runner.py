@@ -1,4 +1,4 @@
-"""Generation runner (runner.py:1-308): masks, positions, greedy generation.
+"""Generation runner (runner.py:1-460): masks, positions, greedy and sampling generation.
 
 The reference jit-compiles one XLA program per shape and syncs with the host
 after every decode step (the EOS check, runner.py:300-306).  Here each step is
@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import torch
 
+from . import kernels as K
 from .glm4 import WIDE_MIN_TOKENS, DecodeGraph, DecodeState, GLM4ForCausalLM, PrefillState
 
 NEG = -1e9
@@ -107,6 +108,66 @@ def greedy_generate(model, input_ids, max_new_tokens: int = 128, max_cache_len: 
     out = [st.ids.to("cpu")]
     for _ in range(max_new_tokens - 1):
         g.decode()
+        out.append(st.ids.to("cpu"))
+        if _eos_hit(out[-1], eos_token_id):
+            break
+    return torch.cat([ids] + [t[:, None] for t in out], dim=1)
+
+
+def _full_logits(model: GLM4ForCausalLM, local: torch.Tensor) -> torch.Tensor:
+    """[B, V/tp] vocab shard -> [B, V] (all-gather over the tensor axis)."""
+    if model.tp == 1:
+        return local
+    import torch.distributed as dist
+    parts = [torch.empty_like(local) for _ in range(model.tp)]
+    dist.all_gather(parts, local.contiguous(), group=model.mesh.group("tensor"))
+    return torch.cat(parts, dim=-1).contiguous()
+
+
+def sample_generate(model: GLM4ForCausalLM, input_ids, max_new_tokens: int = 128, max_cache_len: int | None = None,
+                    temperature: float = 0.8, top_k: int = 0, top_p: float = 0.8, repetition_penalty: float = 1.1,
+                    eos_token_id=None, seed: int = 42) -> torch.Tensor:
+    """runner.py:366-460: prefill, then decode with the sampling of runner.py:315-359
+    (jsx_sample) on the full-vocabulary logits of every step.  The presence mask of the
+    repetition penalty marks the prompt tokens and every sampled token.  The categorical
+    draw's Gumbel noise comes from a torch generator seeded with `seed` (the reference
+    draws the same distribution from jax.random with its own key, so the sampled ids
+    are not the reference's).  Returns [B, prompt_len + generated] int32 on the host."""
+    m = model
+    dev, V = m.device, m.config.vocab_size
+    ids = torch.as_tensor(input_ids, dtype=torch.int32)
+    B, S = ids.shape
+    L = max_cache_len or (S + max_new_tokens)
+    k = top_k if top_k > 0 else 200
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    ids_dev = ids.to(dev)
+    presence = torch.zeros(B, V, dtype=torch.uint8, device=dev)
+    presence.scatter_(1, ids_dev.long(), 1)
+    st = DecodeState(m, B, L, want_logits=True)
+
+    def draw(local_logits):
+        u = torch.rand(B, k, generator=gen, device=dev).clamp_(1e-20, 1.0)
+        g = (-torch.log(-torch.log(u))).to(torch.bfloat16)
+        tok = K.sample(_full_logits(m, local_logits), g, presence=presence, repetition_penalty=repetition_penalty,
+                       temperature=temperature, top_k=top_k, top_p=top_p)
+        presence.scatter_(1, tok.long()[:, None], 1)
+        return tok
+
+    if S > 1 and B * S >= WIDE_MIN_TOKENS:
+        ps = PrefillState(m, B, S, L, caches=st.caches, want_logits=True)
+        m.prefill(ps, ids_dev)
+        st.ids.copy_(draw(ps.logits))
+    else:
+        for s in range(S):
+            st.ids.copy_(ids_dev[:, s])
+            m.step(st, head=(s == S - 1))
+        st.pos.fill_(S)
+        st.ids.copy_(draw(st.logits))
+    st.pos.fill_(S)
+    out = [st.ids.to("cpu")]
+    for _ in range(max_new_tokens - 1):
+        m.step(st, head=True)  # logits of the fed token's next position
+        st.ids.copy_(draw(st.logits))
         out.append(st.ids.to("cpu"))
         if _eos_hit(out[-1], eos_token_id):
             break

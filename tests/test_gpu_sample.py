@@ -44,3 +44,20 @@ def test_sample_greedy_limit(jsx, ref, cuda):
     lg = ref.bf16(rng.standard_normal((4, 151552), dtype=np.float32) * np.float32(2.0))
     got = jsx.kernels.sample(bf(lg, cuda), torch.zeros(4, 200, dtype=torch.bfloat16, device=cuda)).cpu().numpy()
     assert np.array_equal(got, ref.argmax_first(lg))
+
+
+@pytest.mark.parametrize("S", [5, 40])
+def test_sample_generate_top1_is_greedy(jsx, ref, cuda, S):
+    """runner.sample_generate with one candidate (top_k 1), no penalty and temperature 1
+    reproduces greedy_generate, with the prompt token by token (S = 5) and in one pass
+    (2 x 40 tokens)."""
+    from test_gpu_model import small_cfg, to_model_config
+    rc = small_cfg(ref)
+    params = ref.init_params(rc, seed=15)
+    model = jsx.GLM4ForCausalLM(to_model_config(jsx, rc), jsx.create_mesh(1))
+    model.load_state(params)
+    prompt = np.random.default_rng(16).integers(0, rc.vocab_size, (2, S))
+    a = jsx.sample_generate(model, prompt, max_new_tokens=5, max_cache_len=S + 8, temperature=1.0, top_k=1,
+                            top_p=1.0, repetition_penalty=1.0).numpy()
+    b = jsx.greedy_generate(model, prompt, max_new_tokens=5, max_cache_len=S + 8).numpy()
+    assert np.array_equal(a, b), (a, b)
