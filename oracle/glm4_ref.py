@@ -530,3 +530,46 @@ def sample_tokens(logits, presence, gumbel, repetition_penalty, temperature, top
         z = bf16(vals + np.asarray(gumbel[b], np.float32))
         tokens[b] = order[int(np.argmax(z))]
     return tokens, margins
+
+
+def mla_attention_absorbed(p: MLAParams, x, positions, mask, latent, cache_position, nh, nope, rope_d, vdim, eps,
+                           inv_freq):
+    """MLA with the kv_b projection absorbed into the query and the output (the
+    latent-cache decode form; the reference computes the expanded form,
+    layers/mla_attention.py:101-193).  The cache holds per token the normalised
+    latent c (kv_lora values) and the rotated shared rope key (rope_d values):
+    latent [B, L, kv_lora + rope_d], updated in place.  With W_k[h] and W_v[h]
+    the key and value columns of kv_b for head h:
+        q.k = (W_k[h] q_nope) . c + q_rope . k_rope,     out_h = (sum_l p_l c_l) W_v[h]
+    equal to the expanded form up to where it rounds to bf16 (k_nope and v are
+    never materialised here), so it agrees with mla_attention to the bf16
+    tolerance, not bit for bit.  Returns the output [B, S, H]."""
+    B, S, _ = x.shape
+    kv_lora = p.kv_a_ln.shape[0]
+    qc = rmsnorm(linear(x, p.q_a), p.q_a_ln, eps)
+    q = linear(qc, p.q_b).reshape(B, S, nh, nope + rope_d)
+    kvc = linear(x, p.kv_a)
+    c = rmsnorm(kvc[..., :kv_lora], p.kv_a_ln, eps)                        # [B, S, kv_lora]
+    k_rope = kvc[..., kv_lora:]                                             # [B, S, rope_d]
+    qr, kr = rope(np.asarray(positions).reshape(-1), q[..., nope:].reshape(-1, nh, rope_d),
+                  k_rope.reshape(-1, 1, rope_d), inv_freq)
+    q_rope = qr.reshape(B, S, nh, rope_d)
+    start = min(max(int(np.asarray(cache_position)[0]), 0), latent.shape[1] - S)
+    latent[:, start:start + S, :kv_lora] = c
+    latent[:, start:start + S, kv_lora:] = kr.reshape(B, S, rope_d)
+    wkv = np.asarray(p.kv_b, np.float32).reshape(kv_lora, nh, nope + vdim)
+    w_k, w_v = wkv[..., :nope], wkv[..., nope:]                             # [kv_lora, nh, nope|vdim]
+    q_abs = bf16(np.einsum("bshn,lhn->bshl", q[..., :nope], w_k, dtype=np.float32))   # [B, S, nh, kv_lora]
+    lat = np.asarray(latent, np.float32)
+    scale = np.float32((nope + rope_d) ** -0.5)
+    scores = (np.einsum("bshl,btl->bhst", q_abs, lat[..., :kv_lora], dtype=np.float32) +
+              np.einsum("bshr,btr->bhst", q_rope, lat[..., kv_lora:], dtype=np.float32))
+    scores = bf16(bf16(scores) * scale)
+    if mask is not None:
+        scores = bf16(scores + np.asarray(mask, np.float32))
+    m = scores.max(axis=-1, keepdims=True)
+    e = np.exp(scores - m)
+    probs = bf16(e / e.sum(axis=-1, keepdims=True, dtype=np.float32))
+    ctx = bf16(np.einsum("bhst,btl->bshl", probs, lat[..., :kv_lora], dtype=np.float32))  # [B, S, nh, kv_lora]
+    out = bf16(np.einsum("bshl,lhv->bshv", ctx, w_v, dtype=np.float32)).reshape(B, S, nh * vdim)
+    return linear(out, p.o)

@@ -97,3 +97,31 @@ def test_sample_tokens_limits(ref):
     noise = ref.bf16(rng.standard_normal((3, 10), dtype=np.float32) * np.float32(5.0))
     tok, _ = ref.sample_tokens(lg, None, noise, 1.0, 1.0, 10, 1e-6)
     assert np.array_equal(tok, ref.argmax_first(lg))
+
+
+def test_mla_absorbed_matches_expanded(ref):
+    """The latent-cache (absorbed) MLA form against the reference's expanded form
+    (pinned by test_oracle_pin), GLM-4.7-Flash head shapes at reduced width: a
+    5-token prefill then a decode step; the latent cache holds 64 + 16 values per
+    token instead of 4 x (64 + 64)."""
+    rng = np.random.default_rng(21)
+    H, nh, ql, kl, nope, rd, vd = 256, 4, 96, 64, 48, 16, 64
+    r = lambda *s_: ref.bf16(rng.standard_normal(s_, dtype=np.float32) * np.float32(0.05))
+    p = ref.MLAParams(q_a=r(H, ql), q_a_ln=ref.bf16(1 + 0.1 * rng.standard_normal(ql).astype(np.float32)),
+                      q_b=r(ql, nh * (nope + rd)), kv_a=r(H, kl + rd),
+                      kv_a_ln=ref.bf16(1 + 0.1 * rng.standard_normal(kl).astype(np.float32)),
+                      kv_b=r(kl, nh * (nope + vd)), o=r(nh * vd, H))
+    inv = ref.rope_inv_freq(rd, theta=1000000.0, partial=1.0)
+    B, S, L = 2, 5, 12
+    x = ref.bf16(rng.standard_normal((B, S, H), dtype=np.float32))
+    x2 = ref.bf16(rng.standard_normal((B, 1, H), dtype=np.float32))
+    kv = (np.zeros((B, L, nh, nope + rd), np.float32), np.zeros((B, L, nh, vd), np.float32))
+    lat = np.zeros((B, L, kl + rd), np.float32)
+    pos = np.broadcast_to(np.arange(S), (B, S))
+    for xi, pi, mask, cp in ((x, pos, ref.make_prefill_mask(S, L), np.arange(S)),
+                             (x2, np.full((B, 1), S), ref.make_decode_mask(S, L), [S])):
+        want = ref.mla_attention(p, xi, pi, mask, kv, cp, nh, nope, rd, vd, 1e-5, inv)
+        got = ref.mla_attention_absorbed(p, xi, pi, mask, lat, cp, nh, nope, rd, vd, 1e-5, inv)
+        err = np.max(np.abs(got - want)) / np.max(np.abs(want))
+        cos = float(np.sum(got * want) / (np.linalg.norm(got) * np.linalg.norm(want)))
+        assert err <= 2e-2 and cos >= 0.999, (err, cos)
