@@ -2,7 +2,7 @@
 layer 0, MoE layers after) against the oracle's composition of the pinned MLA and
 MoE restatements (oracle/glm4_ref.py flash_forward, models/glm4_flash.py:93-205),
 on seeded random weights: a 4-token prompt and one decode step.  Bar: the
-north-star tolerance on logits (max relative error 2e-2, cosine 0.999)."""
+model-level tolerance on logits (max relative error 2e-2, cosine 0.999)."""
 
 import importlib
 

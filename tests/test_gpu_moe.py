@@ -5,7 +5,7 @@ tests/test_oracle_pin.py::test_moe_layer).
 The expert GEMVs accumulate in fp32 in another order than numpy's einsum and round
 to bf16 at the reference's points, so outputs agree to about one bf16 ulp: max
 relative error <= 1e-2, cosine >= 0.9999, most elements bit-identical.  The layer
-test uses the north-star tolerance (2e-2, cosine 0.999) because its router computes
+test uses the model-level tolerance (2e-2, cosine 0.999) because its router computes
 its own logits; router ids on identical logits are checked bit-exact in
 tests/test_gpu_ops.py."""
 
