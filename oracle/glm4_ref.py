@@ -1,7 +1,7 @@
 """CPU oracle: a numpy + ml_dtypes restatement of JaxScale's GLM-4 decoder step.
 
 TEST INFRASTRUCTURE ONLY.  Only tests/, __graft_entry__.smoke() and bench.py's
-CPU-baseline legs import this module, and only as the checker or as the timed
+CPU-baseline legs import this module, and only to check results or as the timed
 CPU baseline.  The product path (the e2e-jaxscale_b200 package) never imports it.
 
 Parity status: PINNED ONLY AGAINST THE REFERENCE'S OWN CODE THROUGH A STAND-IN.
