@@ -1,7 +1,8 @@
 """Host-side tensor-parallel logic on CPU ranks (gloo, world size 2 and 4):
 mesh coordinates and groups, per-rank weight shards and KV-head assignment,
-and the row-parallel exchange the fused kernel performs, emulated with a gloo
-all-reduce of the per-rank fp32 partials."""
+the row-parallel exchange the fused kernel performs, emulated with a gloo
+all-reduce of the per-rank fp32 partials, and the vocabulary-shard gather of
+the sampling loop (runner._full_logits)."""
 
 import importlib
 import os
@@ -45,6 +46,16 @@ def _worker(rank, world, port, tp, q):
         y = ref.bf16(t.numpy())
         out["row_parallel_err"] = float(np.max(np.abs(y - ref.linear(x, w))))
         out["kv_heads"] = jsx.layers.kv_cache.local_kv_heads(32, 2, tp, r)
+        # the sampling loop's full-vocabulary logits: the tensor ranks' vocab shards in rank order
+        V = 40
+
+        class _Model:  # the two attributes runner._full_logits reads
+            pass
+        m = _Model()
+        m.tp, m.mesh = tp, mesh
+        local = torch.arange(V // tp, dtype=torch.float32)[None].repeat(3, 1) + r * (V // tp)
+        full = jsx.runner._full_logits(m, local)
+        out["gathered_ok"] = bool(torch.equal(full, torch.arange(V, dtype=torch.float32)[None].repeat(3, 1)))
         q.put((rank, out))
         dist.barrier()
         dist.destroy_process_group()
@@ -70,6 +81,7 @@ def test_mesh_and_row_parallel_on_cpu_ranks(world, tp):
         assert res[r]["coords"] == {"data": r // tp, "tensor": r % tp}
         assert res[r]["tensor_ranks"] == [(r // tp) * tp + i for i in range(tp)]
         assert res[r]["row_parallel_err"] <= 0.01
+        assert res[r]["gathered_ok"]
         first, n = res[r]["kv_heads"]
         if tp <= 2:
             assert (first, n) == (r % tp * (2 // tp), 2 // tp)
