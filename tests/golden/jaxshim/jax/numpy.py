@@ -21,7 +21,18 @@ zeros = _np.zeros
 ones = _np.ones
 full = _np.full
 arange = _np.arange
-where = _np.where
+def where(cond, x=None, y=None):
+    """jnp.where with JAX's weak typing: a Python scalar branch takes the other
+    branch's dtype (numpy would promote a bf16 array and a float to float64)."""
+    if x is None and y is None:
+        return _np.where(cond)
+    if isinstance(x, (int, float)) and isinstance(y, _np.ndarray):
+        x = _np.asarray(x).astype(y.dtype)
+    if isinstance(y, (int, float)) and isinstance(x, _np.ndarray):
+        y = _np.asarray(y).astype(x.dtype)
+    return _np.where(cond, x, y)
+
+
 broadcast_to = _np.broadcast_to
 expand_dims = _np.expand_dims
 concatenate = _np.concatenate
@@ -31,6 +42,11 @@ sin = _np.sin
 exp = _np.exp
 take_along_axis = _np.take_along_axis
 isin = _np.isin
+cumsum = _np.cumsum
+
+
+def argsort(a, axis=-1):
+    return _np.argsort(a, axis=axis, kind="stable")  # jnp.argsort is stable
 clip = _np.clip
 
 

@@ -1,6 +1,6 @@
 """Generates tests/golden/reference_golden.npz by executing the REFERENCE's own
 source files (layers/*.py incl. the MoE and MLA layers, models/glm4.py,
-models/glm4_flash.py, runner.py of sdh1014/e2e-JaxScale)
+models/glm4_flash.py, runner.py incl. its sampling step, of sdh1014/e2e-JaxScale)
 on the CPU through the numpy stand-in under tests/golden/jaxshim/ (JAX and Flax
 are not installable here).  The fixture pins the oracle (oracle/glm4_ref.py)
 to the reference's composition of operations: where it rounds to bf16, adds
@@ -250,6 +250,23 @@ def main():
     flg2, fkv = fm(fnext, np.full((Bf, 1), Sf, np.int32), runner.make_decode_mask(Sf, Lf, dtype=BF),
                    kv_caches=fkv, cache_position=np.array([Sf], np.int32))
     out.update(flash_prompt=fprompt, flash_logits=flg, flash_next=fnext, flash_logits2=flg2)
+
+    # Sampling step (runner.py:315-359, _jit_sample): penalty, temperature, top-k, top-p and the
+    # categorical draw, the draw's Gumbel noise carried by the key (jaxshim NoiseKey)
+    from jax import random as jrandom
+    Bs, Vs = 4, 3000
+    s_logits = rnd((Bs, Vs), 2.0)
+    s_pres = (rng.random((Bs, Vs)) < 0.05).astype(np.float32)
+    out.update(samp_logits=s_logits, samp_presence=s_pres)
+    for j, (rp, temp, tk, tp) in enumerate(((1.1, 0.8, 0, 0.8), (1.3, 1.0, 50, 1.0), (1.0, 1.5, 10, 0.5))):
+        kk = tk if tk > 0 else 200
+        noise = (-np.log(-np.log(rng.random((Bs, kk))))).astype(np.float32).astype(BF)
+        # a Python float meeting a bf16 array stays bf16 in JAX (weak typing): the scalars
+        # are given as bf16 values so that numpy keeps the reference's arithmetic in bf16
+        tok, _ = runner._jit_sample(s_logits, s_pres, jrandom.NoiseKey(noise), BF(rp), BF(temp), tk, tp)
+        out[f"samp{j}_noise"] = noise
+        out[f"samp{j}_tokens"] = np.asarray(tok).reshape(-1)
+        out[f"samp{j}_params"] = np.array([rp, temp, tk, tp], np.float64)
 
     ser = {}
     for k_, v in out.items():

@@ -1,6 +1,6 @@
 """Pins the CPU oracle to the reference's own code: tests/golden/reference_golden.npz
 was produced by running the reference's layers/, models/glm4.py, models/glm4_flash.py
-and runner.py
+and runner.py (greedy loop and sampling step)
 (through the numpy stand-in for jax/flax, tests/golden/make_golden.py).  The
 oracle must reproduce every recorded output bit for bit on the same inputs."""
 
@@ -145,3 +145,13 @@ def test_flash_model_prefill_then_decode(ref, g):
     same(lg, g["flash_logits"])
     lg2 = ref.flash_forward(p, g["flash_next"], np.full((B, 1), S), ref.make_decode_mask(S, L), kv, [S])
     same(lg2, g["flash_logits2"])
+
+
+def test_sampling_step(ref, g):
+    """runner.py:315-359 (_jit_sample): penalty, temperature, top-k, top-p and the
+    categorical draw with the recorded Gumbel noise, three parameter sets."""
+    for j in range(3):
+        rp, temp, tk, tp = g[f"samp{j}_params"]
+        tok, _ = ref.sample_tokens(g["samp_logits"], g["samp_presence"] > 0, g[f"samp{j}_noise"], float(rp),
+                                   float(temp), int(tk), float(tp))
+        assert np.array_equal(tok, g[f"samp{j}_tokens"]), j
