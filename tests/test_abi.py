@@ -43,6 +43,11 @@ def test_abi_version(jsx):
     ("jsx_set_launch_flags", (0x10,)),
     ("jsx_tc_linear", (None, None, 0.0, None, None, None, 16, 64, 8, None, 0, None)),
     ("jsx_tc_workspace_size", (33, 4096, 4096, None)),
+    ("jsx_sample", (256, None, 256, 256, 1, 1000, 1.0, 1.0, 300, 1.0, None)),    # k above 256
+    ("jsx_sample", (256, None, 256, 256, 1, 1000, 1.0, 0.0, 0, 1.0, None)),      # temperature 0
+    ("jsx_attn_prefill", (256, 256, 256, 256, 1, 8, 4, 4, 2, 128, 10, 0.1, None)),  # start + S > max_seq
+    ("jsx_comm_create_tiles", (0, 9, 4096, 4096, 0, None)),
+    ("jsx_wide_row_linear_allreduce", (None, 256, 256, 256, 64, 4096, 33, 256, 1 << 20, None)),  # odd N
 ])
 def test_invalid_arguments_are_rejected_on_the_host(jsx, call, args):
     lib = jsx._lib
@@ -108,3 +113,11 @@ def test_moe_experts_workspace_and_limits(jsx):
     assert n.value >= 65 * 4 + 3 * P * 4 + P * 1536 * 2 + P * 2048 * 2
     with pytest.raises(lib.JsxError):   # 33 tokens per call
         lib.call("jsx_moe_experts", 1, 1, 1, None, 0, 33, 4, 64, 2048, 1536, 1, 1, 1, 1, 1 << 30, None)
+
+
+def test_unsupported_shapes_answer_enotsup(jsx):
+    """The prefill attention kernel takes head_dim 128; others are refused before any launch."""
+    lib = jsx._lib
+    with pytest.raises(lib.JsxError) as e:
+        lib.call("jsx_attn_prefill", 256, 256, 256, 256, 1, 8, 0, 4, 2, 64, 16, 0.1, None)
+    assert e.value.status == lib.JSX_ENOTSUP
