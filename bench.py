@@ -19,11 +19,20 @@ value:  B / step time, whole job (the TP ranks cooperate on the same tokens:
 e2e:    the same metric through the public API with host buffers: every step
         copies the fed token ids from pinned host memory, replays the step and
         reads the greedy ids back (the reference's per-step host sync).
+parity: before timing, at every GPU count, a 2-layer GLM-4-9B-shaped model
+        (vocabulary 8192, host-seeded weights) runs teacher-forced through the
+        same kernels (whole-step kernel at batch 1, tensor-core chain at batch
+        32) and its logits, hidden states and greedy ids are compared with the
+        oracle's outputs stored in tests/golden/tp_parity.npz (max relative
+        error <= 2e-2, cosine >= 0.999, ids equal unless the oracle's own
+        top-1/top-2 margin is within twice the measured logit error).  The
+        run exits non-zero, after its JSON line, when the gate fails, when a
+        peer wait timed out, or when the ranks' greedy ids disagree.
 --impl reference: the reference's algorithm on the host cores.  JAX/Flax (the
         reference's runtime) is not installable on this image, so this times
         the numpy restatement under oracle/ (kind "port") on a bounded sample
-        (one GLM-4-9B decoder layer at context C plus the LM head, scaled to 40
-        layers), rank 0 only.
+        (whole 40-layer decode steps at context C, one layer's weights shared
+        by the 40 layers), rank 0 only, on every host core.
 """
 
 from __future__ import annotations
@@ -79,6 +88,13 @@ def parse():
 # CPU arm (oracle restatement, host cores)
 # ---------------------------------------------------------------------------
 
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
 def blas_threads() -> int:
     try:
         from threadpoolctl import threadpool_info
@@ -88,39 +104,53 @@ def blas_threads() -> int:
         return 1
 
 
-def cpu_decode_sample(ctx: int, reps: int = 2) -> dict:
-    """One GLM-4-9B decoder layer (batch 1, KV cache of ctx rows) and the final
-    norm + LM head, timed with the oracle; tok/s = 1 / (40 * t_layer + t_head)."""
+def cpu_decode_sample(ctx: int, steps: int = 3) -> dict:
+    """Whole GLM-4-9B decode steps at batch 1 on the host cores with the oracle:
+    embedding, 40 decoder layers (each with its own KV cache of ctx rows), final
+    norm, LM head and argmax.  The 40 layers share one layer's weights (40 distinct
+    layers would need 72 GB of float32 host arrays; 1.8 GB per layer already
+    streams past the host caches, so the work per layer is the same).  BLAS uses
+    every core this process may run on, whatever OMP_NUM_THREADS says (torchrun
+    sets it to 1), so the figure is the same at every GPU count."""
+    from threadpoolctl import threadpool_limits
+    cores = host_cores()
     ref = importlib.import_module("oracle.glm4_ref")
     cfg = ref.GLMConfig(num_hidden_layers=1)
     p = ref.init_params(ref.GLMConfig(num_hidden_layers=1, vocab_size=8), seed=0)  # one layer's shapes
     lp = p.layers[0]
     rng = np.random.default_rng(0)
+    embed = ref.bf16(rng.standard_normal((cfg.vocab_size, cfg.hidden_size), dtype=np.float32) * 0.02)
     lm_head = ref.bf16(rng.standard_normal((cfg.vocab_size, cfg.hidden_size), dtype=np.float32) * 0.02)
     norm = np.ones(cfg.hidden_size, np.float32)
-    L = ctx + 1
-    kc = ref.bf16(rng.standard_normal((1, L, cfg.num_key_value_heads, cfg.head_dim), dtype=np.float32))
-    vc = ref.bf16(rng.standard_normal((1, L, cfg.num_key_value_heads, cfg.head_dim), dtype=np.float32))
-    h = ref.bf16(rng.standard_normal((1, 1, cfg.hidden_size), dtype=np.float32))
+    L = ctx + steps + 2
+    nl = 40
+    caches = [(ref.bf16(rng.standard_normal((1, L, cfg.num_key_value_heads, cfg.head_dim), dtype=np.float32)),
+               ref.bf16(rng.standard_normal((1, L, cfg.num_key_value_heads, cfg.head_dim), dtype=np.float32)))
+              for _ in range(nl)]
     inv = ref.rope_inv_freq(cfg.head_dim)
-    pos = np.full((1, 1), ctx, np.int32)
-    mask = ref.make_decode_mask(ctx, L)
-    t_layer, t_head = [], []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        y = ref.decoder_layer(lp, cfg, h, pos, mask, (kc, vc), np.array([ctx]), inv)
-        t1 = time.perf_counter()
-        logits = ref.bf16(ref.rmsnorm(y, norm, cfg.rms_norm_eps) @ lm_head.T)
-        ref.argmax_first(logits[:, -1])
-        t2 = time.perf_counter()
-        t_layer.append(t1 - t0)
-        t_head.append(t2 - t1)
-    tl, th = min(t_layer), min(t_head)
-    per_tok = 40 * tl + th
-    return {"value": 1.0 / per_tok, "unit": "tok/s", "cores": blas_threads(), "kind": "port",
-            "sample": (f"numpy oracle (oracle/glm4_ref.py), batch 1: one GLM-4-9B decoder layer at "
-                       f"context {ctx} ({tl * 1e3:.1f} ms) x 40 + final norm/LM head/argmax "
-                       f"({th * 1e3:.1f} ms), best of {reps}; reference JAX runtime not installable")}
+    tok = np.array([[1]], np.int64)
+    times = []
+    with threadpool_limits(limits=cores, user_api="blas"):
+        for s_ in range(steps + 1):  # the first step is a warm-up
+            cur = ctx + s_
+            pos = np.full((1, 1), cur, np.int32)
+            mask = ref.make_decode_mask(cur, L)
+            t0 = time.perf_counter()
+            h = embed[tok]
+            for i in range(nl):
+                h = ref.decoder_layer(lp, cfg, h, pos, mask, caches[i], np.array([cur]), inv)
+            logits = ref.bf16(ref.rmsnorm(h, norm, cfg.rms_norm_eps) @ lm_head.T)
+            tok = ref.argmax_first(logits[:, -1])[:, None]
+            t1 = time.perf_counter()
+            if s_ > 0:
+                times.append(t1 - t0)
+        threads = blas_threads()
+    per_tok = statistics.median(times)
+    return {"value": 1.0 / per_tok, "unit": "tok/s", "cores": threads, "kind": "port",
+            "sample": (f"numpy oracle (oracle/glm4_ref.py) on {threads} BLAS threads ({cores} cores available), "
+                       f"batch 1: {steps} whole decode steps (embedding, 40 decoder layers sharing one layer's "
+                       f"weights, KV caches of {ctx}+ rows, final norm, LM head, argmax), median "
+                       f"{per_tok * 1e3:.0f} ms; the reference's JAX runtime is not installable here")}
 
 
 def run_reference(args) -> None:
@@ -229,6 +259,107 @@ def ncu_traffic(key: str):
         return None
 
 
+PARITY_FIXTURE = os.path.join(ROOT, "tests", "golden", "tp_parity.npz")
+PARITY_REL, PARITY_COS = 2e-2, 0.999
+
+
+def _bf16_bits_to_f32(a: np.ndarray) -> np.ndarray:
+    return (np.asarray(a, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def parity_gate(jsx, mesh, dev, world: int) -> dict:
+    """Teacher-forced decode of the stored parity model on this mesh (TP = world),
+    compared with the oracle's outputs in tests/golden/tp_parity.npz (written by
+    tests/golden/make_tp_parity.py).  Batch 1 runs the whole-step kernel, batch
+    32 the tensor-core chain with its separate all-reduce kernel.  Every rank
+    runs the same calls; logits are gathered over the tensor ranks."""
+    import torch
+    import torch.distributed as dist
+
+    K = jsx.kernels
+    fx = np.load(PARITY_FIXTURE)
+    V, nl = int(fx["vocab"]), int(fx["layers"])
+    cfg = jsx.ModelConfig(num_hidden_layers=nl, vocab_size=V)
+    params = jsx.weights.random_reference_params(cfg, seed=int(fx["seed"]))
+    model = jsx.GLM4ForCausalLM(cfg, mesh)
+    model.load_state(params)
+    del params
+    group = mesh.group("tensor")
+
+    def gather_logits(st, rows):
+        local = st.logits[:rows].float().contiguous()
+        if world == 1:
+            return local.cpu().numpy().astype(np.float64)
+        if dist.get_backend(group) == "gloo":  # CPU process groups (the multi-GPU tests)
+            local = local.cpu()
+        parts = [torch.empty_like(local) for _ in range(world)]
+        dist.all_gather(parts, local, group=group)
+        return torch.cat(parts, dim=-1).cpu().numpy().astype(np.float64)
+
+    res = {"max_rel": 0.0, "min_cos": 1.0, "ids": 0, "ids_equal": 0, "flips": [], "steps": 0}
+
+    def compare(name, a, b):
+        err = float(np.max(np.abs(a - b)) / np.max(np.abs(b)))
+        cos = float(np.sum(a * b) / (np.linalg.norm(a) * np.linalg.norm(b)))
+        res["max_rel"] = max(res["max_rel"], err)
+        res["min_cos"] = min(res["min_cos"], cos)
+        return err <= PARITY_REL and cos >= PARITY_COS
+
+    ok = True
+    for case, B in (("b1", 1), ("b32", 32)):
+        prompt, toks = fx[f"{case}_prompt"], fx[f"{case}_tokens"]
+        S, T = prompt.shape[1], toks.shape[1]
+        want_lg = _bf16_bits_to_f32(fx[f"{case}_logits"]).astype(np.float64)
+        st = jsx.DecodeState(model, B, S + T, want_logits=True)
+        for s_ in range(S):
+            st.ids.copy_(torch.from_numpy(prompt[:, s_]).to(dev))
+            model.step(st, head=(s_ == S - 1))
+        for t in range(T):
+            if t > 0:
+                st.ids.copy_(torch.from_numpy(toks[:, t - 1]).to(dev))
+                model.step(st, head=True)
+            ids = st.ids.cpu().numpy()
+            if case == "b1":
+                lg = gather_logits(st, 1)
+                ok &= compare("logits", lg[0], want_lg[t])
+                ok &= compare("hidden", st.h[0].float().cpu().numpy().astype(np.float64),
+                              _bf16_bits_to_f32(fx["b1_hidden"][t]).astype(np.float64))
+                srt = np.sort(want_lg[t])
+                margins = np.array([srt[-1] - srt[-2]])
+                bound = float(np.max(np.abs(lg[0] - want_lg[t])))
+            else:
+                nchk = want_lg.shape[1]
+                lg = gather_logits(st, nchk)
+                for b in range(nchk):
+                    ok &= compare("logits", lg[b], want_lg[t, b])
+                margins = fx["b32_margin"][t]
+                bound = float(np.max(np.abs(lg - want_lg[t])))
+            want_ids = toks[:, t]
+            res["ids"] += len(ids)
+            res["ids_equal"] += int(np.sum(ids == want_ids))
+            for b in np.nonzero(ids != want_ids)[0]:
+                res["flips"].append({"case": case, "step": t, "seq": int(b), "margin": float(margins[b]),
+                                     "logit_err": bound})
+                ok &= bool(margins[b] <= 2 * bound)
+            res["steps"] += 1
+        del st
+    torch.cuda.synchronize()
+    if model.comm is not None:
+        try:
+            model.comm.check()
+        except jsx._lib.JsxError:
+            ok = False
+            res["timeout"] = True
+    ok &= K.device_error() == 0
+    del model
+    torch.cuda.synchronize()
+    res["ok"] = bool(ok)
+    res["tolerance"] = f"max rel {PARITY_REL}, cosine {PARITY_COS}, ids equal outside the margin rule"
+    res["model"] = (f"GLM-4-9B-shaped, {nl} layers, vocabulary {V}, host-seeded weights; batch 1 (whole-step "
+                    f"kernel) and 32 (tensor-core chain), teacher-forced against the oracle's stored outputs")
+    return res
+
+
 def run_gpu(args) -> None:
     import torch
     import torch.distributed as dist
@@ -259,10 +390,35 @@ def run_gpu(args) -> None:
         return float(t.item())
 
     mesh = jsx.create_mesh(tp=args.gpus)
+    # correctness first: the same kernels on the stored parity model, at this TP
+    parity = parity_gate(jsx, mesh, dev, world)
+    failures = [] if parity["ok"] else ["parity gate"]
     cfg = jsx.ModelConfig(num_hidden_layers=args.layers, vocab_size=args.vocab)
     model = jsx.GLM4ForCausalLM(cfg, mesh)
     model.init_random(seed=args.seed)
     peak, peak_kind = measured_hbm_peak()
+
+    def run_checks(st) -> dict:
+        """After a timed run, on every rank: no peer or barrier wait timed out, and the
+        greedy ids are identical on every rank."""
+        out = {"timeout": False, "ids_agree": True}
+        torch.cuda.synchronize()
+        if model.comm is not None:
+            try:
+                model.comm.check()
+            except jsx._lib.JsxError:
+                out["timeout"] = True
+        if K.device_error() != 0:
+            out["timeout"] = True
+        if world > 1:
+            ids = st.ids.clone()
+            parts = [torch.empty_like(ids) for _ in range(world)]
+            dist.all_gather(parts, ids)
+            out["ids_agree"] = all(torch.equal(parts[0], x) for x in parts)
+            flag = torch.tensor([1.0 if out["timeout"] else 0.0], device=dev)
+            dist.all_reduce(flag, op=dist.ReduceOp.MAX)
+            out["timeout"] = bool(flag.item() > 0)
+        return out
     stream = torch.cuda.current_stream()
     c = cfg
 
@@ -325,6 +481,7 @@ def run_gpu(args) -> None:
         barrier()
         e2e_ms = max_over_ranks((t1 - t0) * 1e3 / e2e_steps)
         clk = clocks.stop() if clocks else None
+        checks = run_checks(st)
 
         # step bytes: weights streamed + KV rows read/written + embedding rows
         kv_bytes = B * c.num_hidden_layers * 2 * (C + args.warmup + args.steps) * model.nkv_l * c.head_dim * 2
@@ -339,7 +496,7 @@ def run_gpu(args) -> None:
         mbu_ref = ref_model_bytes / (ms * 1e-3) / (peak * 1e9 * args.gpus)
 
         fused = model.fused_step and st.step_args is not None
-        phase_us = None
+        phase_us, exposed = None, None
         if fused:
             # the whole step is one kernel launch: its duration is the timed step
             kern_name = "jsx_decode_step (k_decode_step<M>): the whole decode step, one launch per step"
@@ -348,10 +505,16 @@ def run_gpu(args) -> None:
             # per-phase breakdown from the kernel's %globaltimer trace (CTA 0, after each grid barrier)
             nl = c.num_hidden_layers
             tr = torch.zeros(2 + 13 * nl, dtype=torch.int64, device=dev)
+            tar = torch.zeros(4 * nl, dtype=torch.int64, device=dev)
             st.step_args.trace = tr.data_ptr()
-            acc, sub = None, None
+            st.step_args.trace_ar = tar.data_ptr()
+            acc, sub, exp_ = None, None, None
             for _ in range(8):
+                tar.zero_()
                 model.step(st, head=True)
+                ta = tar.cpu().numpy().astype(np.float64).reshape(nl, 2, 2)
+                e_ = (ta[:, :, 1] - ta[:, :, 0]) / 1e3  # [layer][o_proj, down]
+                exp_ = e_ if exp_ is None else exp_ + e_
                 t = tr.cpu().numpy().astype(np.float64)
                 d = np.diff(t[:2 + 5 * nl]) / 1e3
                 acc = d if acc is None else acc + d
@@ -360,8 +523,18 @@ def run_gpu(args) -> None:
                 s5 = (t[2 + 5 * nl:].reshape(nl, 8) - start[:, None]) / 1e3
                 sub = s5 if sub is None else sub + s5
             st.step_args.trace = None
+            st.step_args.trace_ar = None
             acc /= 8
             sub /= 8
+            exp_ /= 8
+            exposed = {"per_layer_us": max_over_ranks(float(exp_.sum(axis=1).mean())),
+                       "o_proj_us": max_over_ranks(float(exp_[:, 0].mean())),
+                       "down_us": max_over_ranks(float(exp_[:, 1].mean())),
+                       "definition": ("per row-parallel phase: latest time any CTA finished its rank-ordered "
+                                      "sums minus the latest time any CTA had pushed its partials (the phase's "
+                                      "critical path beyond its own product: what a local no-op exchange would "
+                                      "remove); mean over layers of o_proj + down, 8 traced eager steps, max "
+                                      "over ranks")}
             per = acc[:5 * nl].reshape(nl, 5)
             names = ["qkv", "attention", "o_proj_allreduce", "gate_up", "down_allreduce"]
             phase_us = {n: float(per[:, i].mean()) for i, n in enumerate(names)}
@@ -405,7 +578,7 @@ def run_gpu(args) -> None:
         torch.cuda.synchronize()
         return {
             "B": B, "ms": ms, "e2e_ms": e2e_ms, "clocks": clk, "mbu": mbu, "mbu_ref": mbu_ref,
-            "step_bytes": step_bytes, "phase_us": phase_us,
+            "step_bytes": step_bytes, "phase_us": phase_us, "exposed": exposed, "checks": checks,
             "roofline": {"bound": "hbm", "kernel": kern_name,
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"{peak_kind} hbm_gbs (burst, kernel timed alone)",
@@ -420,6 +593,12 @@ def run_gpu(args) -> None:
         if b != args.batch:
             extra[b] = measure(b, with_clocks=False)
     cpu = cpu_decode_sample(args.ctx) if (rank == 0 and world == 1) else None
+
+    for b, x in [(args.batch, main_res)] + list(extra.items()):
+        if x["checks"]["timeout"]:
+            failures.append(f"batch {b}: a peer or grid-barrier wait timed out")
+        if not x["checks"]["ids_agree"]:
+            failures.append(f"batch {b}: greedy ids differ across ranks")
 
     if rank == 0:
         r = main_res
@@ -437,7 +616,6 @@ def run_gpu(args) -> None:
             "e2e": {"value": B / (r["e2e_ms"] * 1e-3), "unit": "tok/s", "ms_per_step": r["e2e_ms"],
                     "h2d_bytes_per_step": B * 4, "d2h_bytes_per_step": B * 4},
             "gpu_launches": r["launches"],
-            "phase_us": r["phase_us"],
             "pdl": K.pdl_enabled(),
             "clocks": r["clocks"],
         }
@@ -447,14 +625,23 @@ def run_gpu(args) -> None:
                 "bytes_per_step_per_gpu": x["step_bytes"],
                 "e2e": {"value": b / (x["e2e_ms"] * 1e-3), "unit": "tok/s", "ms_per_step": x["e2e_ms"],
                         "h2d_bytes_per_step": b * 4, "d2h_bytes_per_step": b * 4},
-                "roofline": x["roofline"], "gpu_launches": x["launches"], "phase_us": x["phase_us"],
+                "roofline": x["roofline"], "gpu_launches": x["launches"], "checks": x["checks"],
                 "note": "same workload and timing at this batch, measured after the headline batch in the same run",
             }
+        # last, so they stay in view at the end of the line
+        line["phase_us"] = r["phase_us"]
+        line["exposed_comm_us"] = r["exposed"]
+        line["checks"] = r["checks"]
+        line["parity"] = parity
+        line["failures"] = failures
         print(json.dumps(line), flush=True)
     barrier()
     mesh.close()
     if world > 1:
         dist.destroy_process_group()
+    if failures:
+        print("bench: FAILED: " + "; ".join(failures), file=sys.stderr, flush=True)
+        raise SystemExit(1)
 
 
 def run_rowpar(args) -> None:

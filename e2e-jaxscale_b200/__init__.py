@@ -6,6 +6,7 @@ importing fails if the library has not been built.
 """
 
 from . import kernels  # noqa: F401  (loads libjsx.so, raises if missing)
+from . import weights  # noqa: F401
 from .config import ModelConfig  # noqa: F401
 from .glm4 import DecodeGraph, DecodeState, GLM4ForCausalLM, PrefillState  # noqa: F401
 from .flash import GLM4FlashForCausalLM  # noqa: F401

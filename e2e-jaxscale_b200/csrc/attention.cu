@@ -41,10 +41,13 @@ extern "C" int jsx_attn_decode_workspace_size(int B, int nq, int nkv, int head_d
   return JSX_OK;
 }
 
-extern "C" int jsx_attn_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
-                               const int32_t* positions, int B, int nq, int nkv, int head_dim,
-                               int max_seq, float scale, void* workspace, size_t workspace_bytes,
-                               void* stream) {
+namespace jsx {
+
+// Argument checks of jsx_attn_decode other than the workspace (shared with
+// jsx_attn_decode_noalloc, which must reject a call before it touches its
+// static scratch).
+int attn_decode_check(const void* q, const void* k_cache, const void* v_cache, const void* out,
+                      const int32_t* positions, int B, int nq, int nkv, int head_dim, int max_seq) {
   JSX_REQUIRE(q && k_cache && v_cache && out && positions, "null pointer argument");
   JSX_REQUIRE(B >= 1 && nq >= 1 && nkv >= 1 && nq % nkv == 0, "bad heads nq=%d nkv=%d", nq, nkv);
   JSX_REQUIRE(head_dim >= 8 && head_dim % 8 == 0 && head_dim <= 512, "head_dim=%d must be a multiple of 8",
@@ -52,7 +55,20 @@ extern "C" int jsx_attn_decode(const void* q, const void* k_cache, const void* v
   JSX_REQUIRE(max_seq >= 1, "max_seq=%d", max_seq);
   JSX_REQUIRE(aligned16(k_cache) && aligned16(v_cache) && aligned16(out),
               "caches and out must be 16-byte aligned");
-  const int G = nq / nkv;
+  const AttnLayout lay = attn_layout(B, nq, nkv, head_dim, max_seq);
+  JSX_REQUIRE(attn_smem(lay.gi, head_dim, lay.splits) <= 200 * 1024, "attention tile too large (G=%d hd=%d)",
+              nq / nkv, head_dim);
+  return JSX_OK;
+}
+
+}  // namespace jsx
+
+extern "C" int jsx_attn_decode(const void* q, const void* k_cache, const void* v_cache, void* out,
+                               const int32_t* positions, int B, int nq, int nkv, int head_dim,
+                               int max_seq, float scale, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  const int st = attn_decode_check(q, k_cache, v_cache, out, positions, B, nq, nkv, head_dim, max_seq);
+  if (st != JSX_OK) return st;
   size_t need = 0;
   jsx_attn_decode_workspace_size(B, nq, nkv, head_dim, max_seq, &need);
   JSX_REQUIRE(workspace && workspace_bytes >= need && aligned16(workspace),
@@ -60,7 +76,6 @@ extern "C" int jsx_attn_decode(const void* q, const void* k_cache, const void* v
   const AttnLayout lay = attn_layout(B, nq, nkv, head_dim, max_seq);
   const int splits = lay.splits;
   const size_t smem = attn_smem(lay.gi, head_dim, splits);
-  JSX_REQUIRE(smem <= 200 * 1024, "attention tile too large (G=%d hd=%d)", G, head_dim);
   AttnArgs a;
   a.q = (const bf16*)q; a.kc = (const bf16*)k_cache; a.vc = (const bf16*)v_cache;
   a.out = (bf16*)out; a.pos = positions; a.B = B; a.nq = nq; a.nkv = nkv; a.hd = head_dim;

@@ -111,6 +111,33 @@ __device__ __forceinline__ void prefetch(Batch& bt, const bf16* w, int K, int N)
   if (g < N / kRows) load_batch(bt, reinterpret_cast<const uint4*>(w) + (size_t)g * kRows * nvec, nvec, 0, lane);
 }
 
+// L2 prefetch of this warp's first row pairs of a later GEMV phase: bytes
+// [from, to) of the concatenation of the groups gemv_phase will hand it
+// (g = block + grid * warp + k * grid * warps); from and to are multiples of 16.
+// Bulk prefetches issued by lane 0; the bytes land in L2 while this phase's
+// tail, its exchange and the barrier run, so the next phase's weight reads
+// start as L2 hits.
+__device__ __forceinline__ void l2_prefetch_groups(const bf16* w, int K, int N, uint32_t from, uint32_t to) {
+  if (to <= from || (threadIdx.x & 31) != 0) return;
+  const int warp = threadIdx.x >> 5, G = gridDim.x, ngroups = N / kRows;
+  const uint32_t pair = (uint32_t)kRows * (uint32_t)K * 2u;  // K % 8 == 0: a multiple of 16
+  uint32_t at = 0;  // byte offset of group g in the warp's concatenation
+  for (int g = blockIdx.x + G * warp; g < ngroups && at < to; g += G * kWarps, at += pair) {
+    const uint32_t lo = from > at ? from - at : 0u;
+    const uint32_t hi = to - at < pair ? to - at : pair;
+    if (hi <= lo) continue;
+    const char* p = reinterpret_cast<const char*>(w) + (size_t)g * pair + lo;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(hi - lo) : "memory");
+  }
+}
+
+// Latest %globaltimer of any CTA at this point (trace of the exchange phases).
+__device__ __forceinline__ void trace_max(uint64_t* slot) {
+  if (slot == nullptr) return;
+  __syncthreads();
+  if (threadIdx.x == 0) atomicMax(reinterpret_cast<unsigned long long*>(slot), (unsigned long long)globaltimer());
+}
+
 // One GEMV phase (bt holds the first batch of this warp's first group).
 template <int M, int EPI>
 __device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c, bool multi, uint32_t epoch,
@@ -176,10 +203,23 @@ __device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c,
 
 // Row-parallel exchange of one all-reduce phase: the rows this CTA computed,
 // read from every rank's LL slots once they carry the phase's epoch, summed in
-// rank order and added to the residual.
+// rank order and added to the residual.  The residual and every rank's slot of
+// an entry are loaded before any is waited on (one round trip when the peers'
+// pushes have landed); a slot whose epoch is not there yet is then polled.
+__device__ __forceinline__ unsigned long long ll_load(const unsigned long long* slot) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(slot) : "memory");
+  return w;
+}
+
+// Out of line: the loop-invariant addressing of the exchange is not hoisted
+// into the GEMV loops, where registers are scarce.  `slots` = this rank's LL
+// words of the phase's parity, [src][max_tokens][n] u64.
 template <int M>
-__device__ __forceinline__ void allreduce_rows(const GemvArgs& ga, const CommDev& c, uint32_t epoch) {
-  const int ngroups = ga.N / kRows, G = gridDim.x;
+__device__ __noinline__ void allreduce_rows_impl(bf16* h, int n, const unsigned long long* slots, size_t sstride,
+                                                 int world, int max_tokens, uint32_t* state,
+                                                 unsigned long long timeout_ns, uint32_t epoch) {
+  const int ngroups = n / kRows, G = gridDim.x;
   const int my_groups = (ngroups - (int)blockIdx.x + G - 1) / G;
   const int entries = my_groups * kRows * M;
   for (int e = threadIdx.x; e < entries; e += blockDim.x) {
@@ -187,11 +227,54 @@ __device__ __forceinline__ void allreduce_rows(const GemvArgs& ga, const CommDev
     const int rem = e - gl * kRows * M;
     const int r = rem / M, m = rem - (rem / M) * M;
     const int row = (blockIdx.x + G * gl) * kRows + r;
+    bf16* hp = h + (size_t)m * n + row;
+    const float h0 = __bfloat162float(__ldcg(hp));
+    // slot of source src: p0 + src * sstride; every source's slot is loaded
+    // before any is checked
+    const unsigned long long* p0 = slots + (size_t)m * n + row;
+    unsigned long long w[kMaxRanks];
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src)
+      if (src < world) w[src] = ll_load(p0 + src * sstride);
     float s = 0.f;
-    for (int src = 0; src < c.world; ++src) s += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
-    bf16* hp = ga.h + (size_t)m * ga.N + row;
-    *hp = __float2bfloat16_rn(__bfloat162float(__ldcg(hp)) + rbf(s));
+    bool all = true;
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src) {
+      if (src < world) {
+        all = all && (uint32_t)(w[src] >> 32) == epoch;
+        s += __uint_as_float((uint32_t)w[src]);
+      }
+    }
+    if (!all) {
+      // some push has not landed yet: poll every slot in rank order (bounded by the comm timeout)
+      s = 0.f;
+      const uint64_t t0 = globaltimer();
+#pragma unroll 1
+      for (int src = 0; src < world; ++src) {
+        const unsigned long long* p = p0 + src * sstride;
+        unsigned long long v = ll_load(p);
+        for (uint32_t it = 1; (uint32_t)(v >> 32) != epoch; ++it) {
+          if (*reinterpret_cast<volatile uint32_t*>(state + kError)) break;
+          if ((it & 15u) == 0) {
+            if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
+              atomicOr(state + kError, 1u);
+              break;
+            }
+            __nanosleep(20);
+          }
+          v = ll_load(p);
+        }
+        s += (uint32_t)(v >> 32) == epoch ? __uint_as_float((uint32_t)v) : 0.f;
+      }
+    }
+    *hp = __float2bfloat16_rn(h0 + rbf(s));
   }
+}
+
+template <int M>
+__device__ __forceinline__ void allreduce_rows(const GemvArgs& ga, const CommDev& c, uint32_t epoch) {
+  allreduce_rows_impl<M>(ga.h, ga.N, data_ptr(c, c.rank, epoch & 1, 0, 0), (size_t)c.max_tokens * c.hidden,
+                         c.world, c.max_tokens, c.state, c.timeout_ns, epoch);
 }
 
 template <int M>
@@ -278,6 +361,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.max_seq = a.max_seq; ga.tps = 1;
       stage_x<M, false, true>(ga, xs);
       gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best);
+      l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden, 0u, a.l2_next_bytes);
     }
     at.trace = a.trace ? a.trace + (2 + 5 * a.n_layers) + 8 * l : nullptr;
     at.kc = reinterpret_cast<const bf16*>(L.k_cache);
@@ -290,6 +374,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
+    // HBM is idle while the attention's short dependency chain runs: gate/up rows go to L2
+    l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter, 0u, a.l2_attn_bytes);
     for (int it = blockIdx.x; it < attn_items; it += gridDim.x) {
       if (attn_pre && it == (int)blockIdx.x)
         attn_item_mma<kThreads, true, true, true>(at, it % at.splits, it / at.splits, smem_raw, pre_cur);
@@ -310,7 +396,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       const uint32_t ep = epoch0 + 2u * l;
       stage_x<M, false, true>(ga, xs);
       gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
+      uint64_t* ar = a.trace_ar ? a.trace_ar + 4 * l : nullptr;
+      trace_max(ar);
+      l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter, a.l2_attn_bytes,
+                         a.l2_next_bytes);
       if (multi) allreduce_rows<M>(ga, c, ep);
+      trace_max(ar ? ar + 1 : nullptr);
     }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter);
@@ -327,6 +418,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.y = reinterpret_cast<bf16*>(a.act);
       stage_x<M, false, true>(ga, xs);
       gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0u, xs, bt, best);
+      l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden, 0u, a.l2_next_bytes);
     }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden);
@@ -342,7 +434,16 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       const uint32_t ep = epoch0 + 2u * l + 1u;
       stage_x<M, false, true>(ga, xs);
       gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
+      uint64_t* ar = a.trace_ar ? a.trace_ar + 4 * l + 2 : nullptr;
+      trace_max(ar);
+      if (l + 1 < a.n_layers)
+        l2_prefetch_groups(reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows, 0u,
+                           a.l2_next_bytes);
+      else if (a.head)
+        l2_prefetch_groups(reinterpret_cast<const bf16*>(a.lm_head), a.hidden, a.vocab_local, 0u,
+                           a.l2_next_bytes);
       if (multi) allreduce_rows<M>(ga, c, ep);
+      trace_max(ar ? ar + 1 : nullptr);
     }
     grid_arrive(bar, gen);
     if (l + 1 < a.n_layers)
@@ -471,6 +572,8 @@ static int check_step(const jsx_decode_step_args* a) {
               "tensors must be 16-byte aligned");
   JSX_REQUIRE(a->workspace_bytes >= step_workspace(*a), "workspace of %zu bytes required",
               step_workspace(*a));
+  JSX_REQUIRE(a->l2_next_bytes % 16 == 0 && a->l2_attn_bytes % 16 == 0,
+              "L2 prefetch sizes %u / %u must be multiples of 16", a->l2_next_bytes, a->l2_attn_bytes);
   return JSX_OK;
 }
 

@@ -75,6 +75,73 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
   }
   __shared__ float red[M][kWarps];
   __shared__ float rstd[M];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
+  if constexpr (M <= 2) {
+    // one pass: every vector a thread needs (at most 2 per token, K <= 16 * NT)
+    // is held in registers between the sum of squares and the scaling; same
+    // summation order and arithmetic as the two-pass form below
+    if (nvec <= 2 * NT) {
+      uint4 xr[M][2];
+      float ss[M];
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int v = threadIdx.x + jj * NT;
+#pragma unroll
+        for (int m = 0; m < M; ++m)
+          xr[m][jj] = v < nvec ? ld_act(xv + m * nvec + v, kCoherent) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) ss[m] = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        if (threadIdx.x + jj * NT < nvec) {
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            float f[8];
+            unpack8(xr[m][jj], f);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss[m] = fmaf(f[j], f[j], ss[m]);
+          }
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        float s = warp_sum(ss[m]);
+        if (lane == 0) red[m][warp] = s;
+      }
+      stage_sync<kNamed>();
+      if (threadIdx.x < M) {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) t += red[threadIdx.x][w];
+        rstd[threadIdx.x] = 1.0f / sqrtf(t / (float)a.K + a.eps);
+      }
+      stage_sync<kNamed>();
+#pragma unroll
+      for (int jj = 0; jj < 2; ++jj) {
+        const int v = threadIdx.x + jj * NT;
+        if (v < nvec) {
+          float g[8];
+          unpack8(gv[v], g);
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            float f[8];
+            unpack8(xr[m][jj], f);
+            const float r = rstd[m];
+            uint4 o;
+            o.x = pack2((f[0] * r) * g[0], (f[1] * r) * g[1]);
+            o.y = pack2((f[2] * r) * g[2], (f[3] * r) * g[3]);
+            o.z = pack2((f[4] * r) * g[4], (f[5] * r) * g[5]);
+            o.w = pack2((f[6] * r) * g[6], (f[7] * r) * g[7]);
+            sv[m * nvec + v] = o;
+          }
+        }
+      }
+      stage_sync<kNamed>();
+      return;
+    }
+  }
   float ss[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) ss[m] = 0.f;
@@ -87,7 +154,6 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
       for (int j = 0; j < 8; ++j) ss[m] = fmaf(f[j], f[j], ss[m]);
     }
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     float s = warp_sum(ss[m]);
@@ -101,7 +167,6 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
     rstd[threadIdx.x] = 1.0f / sqrtf(t / (float)a.K + a.eps);
   }
   stage_sync<kNamed>();
-  const uint4* gv = reinterpret_cast<const uint4*>(a.gamma);
   for (int i = threadIdx.x; i < M * nvec; i += NT) {
     const int m = i / nvec, v = i - m * nvec;
     float f[8], g[8];

@@ -21,13 +21,21 @@
 //    from several host threads without ordering — race on the array;
 //  * the first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it; make that
-//    first call before any stream capture begins.
+//    first call before any stream capture begins.  The cached address belongs
+//    to the device's primary context: after cudaDeviceReset (or anything else
+//    that destroys and recreates that context) the module is loaded again, the
+//    array may move, and this entry point must not be called again in the
+//    process;
+//  * a call whose arguments are rejected returns before it touches the array.
 #include <mutex>
 
 #include "attn_core.cuh"
 #include "common.cuh"
 
 namespace jsx {
+
+int attn_decode_check(const void* q, const void* k_cache, const void* v_cache, const void* out,
+                      const int32_t* positions, int B, int nq, int nkv, int head_dim, int max_seq);  // attention.cu
 
 constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;
 constexpr int kMaxDevices = 128;
@@ -56,8 +64,11 @@ using namespace jsx;
 extern "C" int jsx_attn_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
                                        void* out, const int32_t* positions, int B, int nq, int nkv,
                                        int head_dim, int max_seq, float scale, void* stream) {
+  // every argument check of jsx_attn_decode runs before the shared array is cleared
+  int st = attn_decode_check(q, k_cache, v_cache, out, positions, B, nq, nkv, head_dim, max_seq);
+  if (st != JSX_OK) return st;
   size_t need = 0;
-  const int st = jsx_attn_decode_workspace_size(B, nq, nkv, head_dim, max_seq, &need);
+  st = jsx_attn_decode_workspace_size(B, nq, nkv, head_dim, max_seq, &need);
   if (st != JSX_OK) return st;
   JSX_REQUIRE(need <= kNoAllocScratchBytes,
               "this shape needs %zu bytes of attention scratch; the static scratch holds %zu "

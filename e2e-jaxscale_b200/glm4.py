@@ -39,6 +39,13 @@ TC_MIN_BATCH = int(os.environ.get("JSX_TC_MIN_BATCH", "3"))
 # smallest prompt block (batch x prompt tokens) prefilled in one pass on the wide
 # tensor-core GEMM and the prefill attention; smaller prompts run token by token
 WIDE_MIN_TOKENS = int(os.environ.get("JSX_WIDE_MIN_TOKENS", "64"))
+# whole-step kernel: per warp, bytes of the next projection's rows requested into
+# L2 once the warp has read its rows of the current one, and bytes of the
+# gate/up rows requested while the attention runs (multiples of 16; 0 = none).
+# Off by default: at TP=1, batch 1 and 2, every setting measured slower (the
+# prefetches compete with the current phase's last reads and the attention's).
+L2_NEXT_BYTES = int(os.environ.get("JSX_L2_NEXT_BYTES", "0")) & ~15
+L2_ATTN_BYTES = int(os.environ.get("JSX_L2_ATTN_BYTES", "0")) & ~15
 
 
 class DecodeState:
@@ -90,6 +97,7 @@ class DecodeState:
         a.advance, a.head = 1, 1
         a.h, a.q, a.attn, a.act = self.h.data_ptr(), self.q.data_ptr(), self.attn.data_ptr(), self.act.data_ptr()
         a.logits = None if self.logits is None else self.logits.data_ptr()
+        a.l2_next_bytes, a.l2_attn_bytes = L2_NEXT_BYTES, L2_ATTN_BYTES
         self.step_ws = K.step_workspace(a, dev)
         a.workspace, a.workspace_bytes = self.step_ws.data_ptr(), self.step_ws.numel()
         self.step_args = a

@@ -50,6 +50,15 @@ def pdl_enabled() -> bool:
     return bool(lib.jsx_get_launch_flags() & JSX_LAUNCH_PDL)
 
 
+def device_error() -> int:
+    """jsx_device_error: JSX_ETIMEDOUT (3) when a bounded wait of the whole-step kernel,
+    the streaming GEMV or the tensor-core projections gave up since the last call,
+    else 0 (reads and clears the error words; synchronous)."""
+    out = ctypes.c_int(0)
+    call("jsx_device_error", ctypes.byref(out))
+    return out.value
+
+
 def sm_count() -> int:
     out = ctypes.c_int(0)
     call("jsx_device_sm_count", ctypes.byref(out))
@@ -465,7 +474,9 @@ class StepArgs(ctypes.Structure):
                                                   "ids", "positions")]
                 + [("advance", ctypes.c_int), ("head", ctypes.c_int)]
                 + [(n, ctypes.c_void_p) for n in ("h", "q", "attn", "act", "logits", "workspace")]
-                + [("workspace_bytes", ctypes.c_size_t), ("trace", ctypes.c_void_p)])
+                + [("workspace_bytes", ctypes.c_size_t), ("trace", ctypes.c_void_p),
+                   ("trace_ar", ctypes.c_void_p), ("l2_next_bytes", ctypes.c_uint32),
+                   ("l2_attn_bytes", ctypes.c_uint32)])
 
 
 def layer_table(layers, caches, device) -> torch.Tensor:

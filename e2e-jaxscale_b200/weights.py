@@ -106,3 +106,19 @@ class RandomLayerSource:
         d["wu"] = self.normal(H, I)
         d["wd"] = self.normal(I, H)
         return d
+
+
+def random_reference_params(cfg, seed: int = 0, std: float = 0.02) -> dict:
+    """A whole model's reference-layout parameters drawn on the host: N(0, std)
+    bf16 from torch's CPU generator seeded `seed` (the same values on every
+    host with the same torch build), in the draw order of
+    GLM4ForCausalLM.init_random (embedding, each layer's q/k/v/o with biases and
+    gate/up/down, LM head); RMSNorm gains are 1.  For load_state on any number
+    of ranks, and for checking a run against stored outputs of the same model."""
+    src = RandomLayerSource(cfg, torch.device("cpu"), seed, std)
+    H = cfg.hidden_size
+    params = {"embed": src.normal(cfg.vocab_size, H)}
+    params["layers"] = [src.layer() for _ in range(cfg.num_hidden_layers)]
+    params["norm"] = torch.ones(H, dtype=torch.bfloat16)
+    params["lm_head"] = src.normal(cfg.vocab_size, H)
+    return params

@@ -317,6 +317,16 @@ typedef struct {
                                       then per layer 8 attention stamps of head group 0: split 0
                                       started, staged, scored, softmax, P.V done, counted; the
                                       merge done; one spare */
+  uint64_t* trace_ar;              /* NULL, or [n_layers][2][2] u64, zero before the call: for each
+                                      row-parallel phase (o_proj, down) the latest %globaltimer over
+                                      CTAs at which a CTA had pushed its partials to every rank, and
+                                      the latest at which a CTA had finished its rank-ordered sums
+                                      (the second minus the first is the exchange's exposed time) */
+  uint32_t l2_next_bytes;          /* per warp: bytes of its first row pairs of the next projection
+                                      requested into L2 (bulk prefetch) once it has read its rows
+                                      of the current one; 0 = none */
+  uint32_t l2_attn_bytes;          /* per warp: bytes of its first gate/up row pairs requested into
+                                      L2 while the attention runs; 0 = none */
 } jsx_decode_step_args;
 
 int jsx_decode_step_workspace_size(const jsx_decode_step_args* args, size_t* bytes);

@@ -6,7 +6,8 @@ are not installable here).  The fixture pins the oracle (oracle/glm4_ref.py)
 to the reference's composition of operations: where it rounds to bf16, adds
 biases and residuals, splits RoPE halves, builds masks and loops greedily.
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH
+    (or with JSX_REFERENCE_DIR=PATH in the environment)
 
 Inputs are seeded; model weights come from oracle.glm4_ref.init_params (a
 checksum of them is stored so a drift of the numpy generator is detected).
@@ -37,9 +38,12 @@ def params_checksum(p) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("JSX_REFERENCE_DIR"),
+                    help="checkout of the reference (default: $JSX_REFERENCE_DIR)")
     ap.add_argument("--out", default=os.path.join(HERE, "reference_golden.npz"))
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference PATH (or JSX_REFERENCE_DIR) is required")
 
     sys.path.insert(0, os.path.join(HERE, "jaxshim"))
     sys.path.insert(1, args.reference)

@@ -1,13 +1,15 @@
-"""Tensor parallelism on 2 GPUs (skipped with fewer): one spawned process per
-GPU, jsx_comm over CUDA IPC, the fused row-parallel all-reduce and the
-vocab-sharded LM-head argmax checked against the oracle (GEMV and tensor-core
-forms), TP=2 models at batch 2 (whole-step kernel) and batch 6 (tensor-core
-projections) against the oracle's teacher-forced logits, an expert-parallel MoE
-layer (EP=2) against the oracle's MoELayer, the wide row-parallel product with
-its tile-exchange all-reduce at 300-1024 tokens, and a peer that never arrives: the waiting
-rank's kernel gives up after the comm timeout, jsx_comm_check reports
-JSX_ETIMEDOUT and the context stays usable.  NVLS is off (NCCL_NVLS_ENABLE=0);
-the kernels use plain peer stores."""
+"""Tensor parallelism on 2, 4 and 8 GPUs (each skipped with fewer): one spawned
+process per GPU, jsx_comm over CUDA IPC, the fused row-parallel all-reduce and
+the vocab-sharded LM-head argmax checked against the oracle (GEMV and
+tensor-core forms), TP=N models at batch 2 (whole-step kernel) and batch 6
+(tensor-core projections) against the oracle's teacher-forced logits (at TP > 2
+with the kv heads replicated: each rank keeps the one kv head its query heads
+read), the GLM-4-9B-shaped parity gate that bench.py runs before timing, an
+expert-parallel MoE layer (EP=N) against the oracle's MoELayer, the wide
+row-parallel product with its tile-exchange all-reduce at 300-1024 tokens, and a
+peer that never arrives: the waiting rank's kernel gives up after the comm
+timeout, jsx_comm_check reports JSX_ETIMEDOUT and the context stays usable.
+NVLS is off (NCCL_NVLS_ENABLE=0); the kernels use plain peer stores."""
 
 import importlib
 import os
@@ -92,15 +94,16 @@ def _worker(rank, world, port, q):
         out["lm_ids"] = ids.cpu().tolist()
         out["lm_ids_want"] = np.argmax(full, axis=-1).tolist()
 
-        # (c) TP=2 model, teacher-forced against the oracle
-        rc = ref.GLMConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
-                           head_dim=128, intermediate_size=384, vocab_size=1000)
+        # (c) TP=N model, teacher-forced against the oracle (query heads: 4, or one per rank)
+        nqh, voc = max(4, world), 1000 if world <= 4 else 1024
+        rc = ref.GLMConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=nqh, num_key_value_heads=2,
+                           head_dim=128, intermediate_size=384, vocab_size=voc)
         params = ref.init_params(rc, seed=0)
-        prompt = np.random.default_rng(1).integers(0, 1000, (2, 5))
+        prompt = np.random.default_rng(1).integers(0, voc, (2, 5))
         rec = []
         toks = ref.greedy_generate(params, prompt, 4, max_cache_len=16, record=rec)[:, 5:]
-        cfg = jsx.ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
-                              head_dim=128, intermediate_size=384, vocab_size=1000)
+        cfg = jsx.ModelConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=nqh, num_key_value_heads=2,
+                              head_dim=128, intermediate_size=384, vocab_size=voc)
         model = jsx.GLM4ForCausalLM(cfg, mesh)
         model.load_state(params)
         st = jsx.DecodeState(model, 2, 16, want_logits=True)
@@ -109,7 +112,7 @@ def _worker(rank, world, port, q):
             st.ids.copy_(torch.from_numpy(prompt[:, s].astype(np.int32)))
             model.step(st, head=(s == 4))
         for t in range(4):
-            parts = [torch.empty(2, 1000 // world) for _ in range(world)]
+            parts = [torch.empty(2, voc // world) for _ in range(world)]
             dist.all_gather(parts, st.logits.float().cpu())
             lg = torch.cat(parts, dim=1).numpy()
             errs.append(float(np.max(np.abs(lg - rec[t][0])) / np.max(np.abs(rec[t][0]))))
@@ -151,7 +154,7 @@ def _worker(rank, world, port, q):
         c4.close()
 
         # (f) TP=2 model at batch 6 (tensor-core projections), teacher-forced against the oracle
-        prompt6 = np.random.default_rng(2).integers(0, 1000, (6, 4))
+        prompt6 = np.random.default_rng(2).integers(0, voc, (6, 4))
         rec6 = []
         toks6 = ref.greedy_generate(params, prompt6, 3, max_cache_len=16, record=rec6)[:, 4:]
         st6 = jsx.DecodeState(model, 6, 16, want_logits=True)
@@ -161,7 +164,7 @@ def _worker(rank, world, port, q):
             st6.ids.copy_(torch.from_numpy(prompt6[:, s].astype(np.int32)))
             model.step(st6, head=(s == 3))
         for t in range(3):
-            parts = [torch.empty(6, 1000 // world) for _ in range(world)]
+            parts = [torch.empty(6, voc // world) for _ in range(world)]
             dist.all_gather(parts, st6.logits.float().cpu())
             lg = torch.cat(parts, dim=1).numpy()
             errs6.append(float(np.max(np.abs(lg - rec6[t][0])) / np.max(np.abs(rec6[t][0]))))
@@ -226,7 +229,12 @@ def _worker(rank, world, port, q):
             dist.all_gather(allw, hdw.cpu())
             out["wide_identical"].append(all(torch.equal(allw[0], t) for t in allw))
 
-        # (d) a peer that never arrives: rank 1 skips the call
+        # (i) the GLM-4-9B-shaped parity gate of bench.py at this TP
+        sys.path.insert(0, ROOT)
+        bench = importlib.import_module("bench")
+        out["parity"] = bench.parity_gate(jsx, mesh, dev, world)
+
+        # (d) a peer that never arrives: ranks 1.. skip the call
         dist.barrier()
         c3 = jsx.mesh.Comm(rank, world, 8, 64, group=None, timeout_s=0.5)
         if rank == 0:
@@ -251,22 +259,23 @@ def _worker(rank, world, port, q):
     q.put((rank, out))
 
 
-def test_tensor_parallel_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = dict(q.get(timeout=600) for _ in range(2))
+    res = dict(q.get(timeout=900) for _ in range(world))
     for p in procs:
         p.join(timeout=120)
         if p.is_alive():
             p.kill()
-    for r in range(2):
+    for r in range(world):
         assert "error" not in res[r], res[r]["error"]
         assert res[r]["ar_err"] <= 1e-2
         assert res[r]["ar_identical"]
@@ -280,5 +289,6 @@ def test_tensor_parallel_two_gpus():
         assert res[r]["moe_identical"]
         assert max(res[r]["wide_errs"]) <= 1e-2, res[r]["wide_errs"]
         assert all(res[r]["wide_identical"])
+        assert res[r]["parity"]["ok"], res[r]["parity"]
     assert res[0]["timeout_status"] == 3  # JSX_ETIMEDOUT
     assert res[0]["after_timeout"] == 8 * 64.0
