@@ -78,6 +78,8 @@ def parse():
                     help="GLM-4.7-Flash-shaped MoE + MLA decode, 4-layer slice (configuration 4)")
     ap.add_argument("--no-pdl", action="store_true",
                     help="launch without programmatic dependent launch (on by default)")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the short runs of configurations 2-4 that follow the decode measurement")
     # profiling-only shape overrides (a smaller device footprint for ncu captures)
     ap.add_argument("--layers", type=int, default=40, help=argparse.SUPPRESS)
     ap.add_argument("--vocab", type=int, default=151552, help=argparse.SUPPRESS)
@@ -592,6 +594,9 @@ def run_gpu(args) -> None:
     for b in args.also_batch:
         if b != args.batch:
             extra[b] = measure(b, with_clocks=False)
+    configs = None
+    if not args.no_configs:
+        configs = run_configs(jsx, model, mesh, dev, world, rank, args)
     cpu = cpu_decode_sample(args.ctx) if (rank == 0 and world == 1) else None
 
     for b, x in [(args.batch, main_res)] + list(extra.items()):
@@ -628,11 +633,20 @@ def run_gpu(args) -> None:
                 "roofline": x["roofline"], "gpu_launches": x["launches"], "checks": x["checks"],
                 "note": "same workload and timing at this batch, measured after the headline batch in the same run",
             }
-        # last, so they stay in view at the end of the line
-        line["phase_us"] = r["phase_us"]
-        line["exposed_comm_us"] = r["exposed"]
+        if configs is not None:
+            line["configs"] = configs
+        # last and compact, so they stay in view at the end of the line
+        if r["phase_us"] is not None:
+            line["phase_us"] = {k: (round(v, 2) if isinstance(v, float) else
+                                    {kk: round(vv, 2) for kk, vv in v.items()} if isinstance(v, dict) else v)
+                                for k, v in r["phase_us"].items() if k != "note"}
+        if r["exposed"] is not None:
+            line["exposed_comm_us"] = {k: round(v, 2) for k, v in r["exposed"].items() if k != "definition"}
         line["checks"] = r["checks"]
-        line["parity"] = parity
+        line["parity"] = {"ok": parity["ok"], "tp": world, "max_rel": round(parity["max_rel"], 4),
+                          "min_cos": round(parity["min_cos"], 6),
+                          "ids_equal": f"{parity['ids_equal']}/{parity['ids']}",
+                          "flips_within_margin": len(parity["flips"]), "steps": parity["steps"]}
         line["failures"] = failures
         print(json.dumps(line), flush=True)
     barrier()
@@ -644,28 +658,19 @@ def run_gpu(args) -> None:
         raise SystemExit(1)
 
 
-def run_rowpar(args) -> None:
-    """Isolated row-parallel projection (o_proj W[4096 x 4096], down_proj W[13696 x 4096], bf16
-    N(0, 0.02); activations N(0, 1)): the fused product + NVLink all-reduce + residual of
-    this library against cuBLAS (torch.matmul) followed by NCCL all_reduce and the residual
-    add, M = 1, 8, 32, 256, 4096 tokens, K split over the N ranks.  Time per call = CUDA events over
-    `--steps` back-to-back calls after `--warmup`, max over ranks; rel_err compares the two
-    results."""
+def measure_rowpar(jsx, mesh, dev, world: int, rank: int, steps: int, warmup: int,
+                   Ms=(1, 8, 32, 256, 4096)) -> list:
+    """Configuration 2 on `mesh` (TP = world): o_proj W[4096 x 4096] and down_proj
+    W[13696 x 4096] (bf16 N(0, 0.02)), activations N(0, 1), K split over the ranks: this
+    library's fused product + NVLink all-reduce + residual against cuBLAS (torch.matmul)
+    then NCCL all_reduce and the residual add.  Time per call = CUDA events over `steps`
+    back-to-back calls after `warmup`, max over ranks; rel_err compares the two results."""
     import torch
     import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
-    jsx = importlib.import_module("e2e-jaxscale_b200")
     K = jsx.kernels
-    mesh = jsx.create_mesh(tp=world)
     comm = mesh.comm(K.TC_MAX_TOKENS, 4096)
-    comm_t = mesh.comm_tiles(4096, 4096)
+    comm_t = mesh.comm_tiles(max(Ms), 4096) if any(M > K.TC_MAX_TOKENS for M in Ms) else None
     stream = torch.cuda.current_stream()
 
     def max_over_ranks(x: float) -> float:
@@ -676,18 +681,18 @@ def run_rowpar(args) -> None:
         return float(t.item())
 
     def timed(fn) -> float:
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        for _ in range(args.steps):
+        for _ in range(steps):
             fn()
         b.record(stream)
         torch.cuda.synchronize()
-        return max_over_ranks(a.elapsed_time(b) * 1e3 / args.steps)
+        return max_over_ranks(a.elapsed_time(b) * 1e3 / steps)
 
     g = torch.Generator(device=dev).manual_seed(1234)
     results = []
@@ -697,22 +702,22 @@ def run_rowpar(args) -> None:
         w_full = (torch.randn(N, Kfull, generator=g, device=dev) * 0.02).to(torch.bfloat16)
         w = w_full[:, rank * kl:(rank + 1) * kl].contiguous()          # this rank's [N, K/t]
         del w_full
-        for M in (1, 8, 32, 256, 4096):
+        for M in Ms:
             x_full = torch.randn(M, Kfull, generator=g, device=dev).to(torch.bfloat16)
             x = x_full[:, rank * kl:(rank + 1) * kl].contiguous()
             h0 = torch.randn(M, N, generator=g, device=dev).to(torch.bfloat16)
             h_f = h0.clone()
             if M <= K.MAX_DECODE_TOKENS:
                 fused = lambda: K.row_linear_allreduce(comm, x, w, h_f)
-                path = "GEMV (k_gemv<M,EPI_ROWAR>) + LL all-reduce"
+                path = "gemv"
             elif M <= K.TC_MAX_TOKENS:
                 ws = K.tc_workspace(M, [(kl, N)], dev)
                 fused = lambda: K.tc_row_linear_allreduce(comm, x, w, h_f, ws)
-                path = "tcgen05 (k_tc_gemm<EPI_ROWAR>) + LL all-reduce"
+                path = "tcgen05"
             else:
                 ws = K.wide_workspace(M, [(kl, N)], dev, norm=False)
                 fused = lambda: K.wide_row_linear_allreduce(comm_t, x, w, h_f, ws)
-                path = "tcgen05 128x256 tiles (k_wide_gemm<EPI_ROWAR>) + in-epilogue tile exchange"
+                path = "tcgen05-wide+tile-exchange"
             h_b = h0.clone()
 
             def unfused():
@@ -731,11 +736,68 @@ def run_rowpar(args) -> None:
             err = float((h_f.float() - ref_).abs().max() / ref_.abs().max())
             t_f = timed(fused)
             t_u = timed(unfused)
-            results.append({"op": name, "K": Kfull, "N": N, "M": M, "fused_us": t_f, "gemm_nccl_us": t_u,
-                            "speedup": t_u / t_f, "rel_err": err, "fused_path": path})
+            r_ = {"op": name, "M": M, "fused_us": t_f, "gemm_nccl_us": t_u, "speedup": t_u / t_f,
+                  "rel_err": err, "fused_path": path}
+            if world > 1 and M > K.TC_MAX_TOKENS:
+                # how much of the exchange the tile pipeline hides: the same product without
+                # the exchange (one rank's local shard), and NCCL's all-reduce of the result alone
+                h_l = h0.clone()
+                t_g = timed(lambda: K.wide_row_linear_allreduce(None, x, w, h_l, ws))
+                y_ = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+                t_ar = timed(lambda: dist.all_reduce(y_))
+                r_.update({"gemm_only_us": t_g, "nccl_allreduce_us": t_ar,
+                           "hidden_frac": max(0.0, 1.0 - (t_f - t_g) / t_ar)})
+            results.append(r_)
     for c_ in (comm, comm_t):
         if c_ is not None:
             c_.check()
+    return results
+
+
+def run_configs(jsx, model, mesh, dev, world: int, rank: int, args) -> dict:
+    """Short runs of configurations 2, 3 and 4 at this GPU count after the decode
+    measurement (same processes, same mesh for 2 and 3; TP = min(2, N) x EP = N / TP for
+    4), summarised compactly for the JSON line."""
+    import torch
+
+    out = {}
+    rp = measure_rowpar(jsx, mesh, dev, world, rank, steps=20, warmup=3)
+    out["rowpar_us"] = {f"{r['op']}_M{r['M']}": [round(r["fused_us"], 1), round(r["gemm_nccl_us"], 1)]
+                        for r in rp}
+    out["rowpar_note"] = "[fused, cuBLAS+NCCL] us per call, configuration 2, K split over the N ranks"
+    hid = {f"{r['op']}_M{r['M']}": round(r["hidden_frac"], 3) for r in rp if "hidden_frac" in r}
+    if hid:
+        out["allreduce_hidden_frac"] = hid
+    out["rowpar_max_rel_err"] = round(max(r["rel_err"] for r in rp), 5)
+    pf = measure_prefill(jsx, model, dev, world, 32, 1024, steps=2, warmup=1)
+    out["prefill_32x1024"] = {"tok_s": round(pf["value"], 1), "ms": round(pf["ms_per_prefill"], 2),
+                              "mfu": round(pf["mfu"], 4), "tflops_per_gpu": round(pf["achieved_tflops_per_gpu"], 1)}
+    torch.cuda.empty_cache()
+    tp = min(2, world)
+    fmesh = jsx.create_mesh(tp=tp, ep=world // tp)
+    fl = measure_flash(jsx, fmesh, dev, world, args.ctx, steps=20, warmup=3, seed=args.seed, vocab=args.vocab)
+    fmesh.close()
+    out["flash_tok_s"] = {k: round(v["value"], 1) for k, v in fl.items()}
+    out["flash_mesh"] = f"tp{tp}xep{world // tp}"
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_rowpar(args) -> None:
+    """Isolated row-parallel projection (configuration 2): measure_rowpar on TP = N ranks."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
+    jsx = importlib.import_module("e2e-jaxscale_b200")
+    mesh = jsx.create_mesh(tp=world)
+    results = measure_rowpar(jsx, mesh, dev, world, rank, args.steps, args.warmup)
     if rank == 0:
         print(json.dumps({"mode": "rowpar", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                           "dtype": "bf16", "data": "synthetic N(0,0.02) weights, N(0,1) activations (seed 1234)",
@@ -747,14 +809,69 @@ def run_rowpar(args) -> None:
         dist.destroy_process_group()
 
 
+def prefill_peak() -> tuple[float, str]:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            pk = json.load(f)
+        return float(pk["bf16_tflops_sustained"]), "measured bf16_tflops_sustained (cuBLAS, long loop)"
+    except Exception:
+        return 1400.0, "fallback sustained bf16"
+
+
+def measure_prefill(jsx, model, dev, world: int, B: int, S: int, steps: int, warmup: int) -> dict:
+    """Configuration 3 on the model's mesh: B x S seeded uniform prompt ids prefilled in one
+    pass per rank (GLM4ForCausalLM.prefill: wide tcgen05 projections, prefill attention,
+    row-parallel products with the in-epilogue tile exchange at TP > 1, the greedy token of
+    every sequence's last position).  Time per prefill = CUDA events over `steps` prefills
+    after `warmup`, max over ranks.  MFU counts the matmul flops of every position without
+    the all-position LM head (this path computes last-position logits only; the reference
+    all of them), the causal attention flops and the last-position LM head.  The share of
+    the all-reduce hidden behind the GEMM is measured on the row-parallel products alone
+    (measure_rowpar, M = 4096: hidden_frac)."""
+    import torch
+    import torch.distributed as dist
+
+    cfg = model.config
+    ps = jsx.PrefillState(model, B, S, S)
+    g = torch.Generator().manual_seed(1)
+    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g, dtype=torch.int32).to(dev)
+    for _ in range(max(warmup, 1)):
+        model.prefill(ps, ids)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    steps = max(steps, 1)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        model.prefill(ps, ids)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    if ps.comm is not None:
+        ps.comm.check()
+    H, I, nq, hd, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_attention_heads, cfg.head_dim, \
+        cfg.num_hidden_layers
+    qkv_rows = (nq + 2 * cfg.num_key_value_heads) * hd
+    mm_per_tok = 2.0 * L * H * (qkv_rows + H + 3 * I)
+    attn = 4.0 * nq * hd * (S + 1) / 2 * L
+    flops = B * S * (mm_per_tok + attn) + 2.0 * B * H * cfg.vocab_size
+    peak, peak_src = prefill_peak()
+    tflops = flops / (ms * 1e-3) / 1e12
+    del ps
+    torch.cuda.synchronize()
+    return {"value": B * S / (ms * 1e-3), "unit": "tok/s", "ms_per_prefill": ms, "batch": B, "seq": S,
+            "flops_per_prefill": flops, "achieved_tflops_per_gpu": tflops / world, "mfu": tflops / world / peak,
+            "peak_tflops": peak, "peak_source": peak_src}
+
+
 def run_prefill(args) -> None:
     """Configuration 3: GLM-4-9B-shaped prefill of --batch x --seq seeded uniform prompt ids
-    (random-init bf16 weights, causal, cache length --seq) in one pass per rank: wide tcgen05
-    projections, prefill attention, row-parallel products with the in-epilogue tile exchange
-    at TP > 1, and the greedy token of every sequence's last position.  Time per prefill =
-    CUDA events over --steps prefills after --warmup, max over ranks.  MFU counts the
-    matmul flops without the LM head of every position (this path computes last-position
-    logits only, the reference all of them) plus the causal attention flops."""
+    (random-init bf16 weights, causal, cache length --seq), measure_prefill on TP = N ranks."""
     import torch
     import torch.distributed as dist
 
@@ -774,64 +891,96 @@ def run_prefill(args) -> None:
     model.init_random(seed=args.seed)
     B = args.batch if args.batch > 1 else 32
     S = args.seq
-    ps = jsx.PrefillState(model, B, S, S)
-    g = torch.Generator().manual_seed(1)
-    ids = torch.randint(0, cfg.vocab_size, (B, S), generator=g, dtype=torch.int32).to(dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    for _ in range(max(args.warmup, 1)):
-        model.prefill(ps, ids)
-    torch.cuda.synchronize()
-    barrier()
     clocks = ClockSampler(local)
-    steps = max(args.steps, 1)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        model.prefill(ps, ids)
-    b.record()
-    torch.cuda.synchronize()
+    res = measure_prefill(jsx, model, dev, world, B, S, args.steps, args.warmup)
     clk = clocks.stop()
-    ms = a.elapsed_time(b) / steps
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    if ps.comm is not None:
-        ps.comm.check()
-    H, I, nq, hd, L = cfg.hidden_size, cfg.intermediate_size, cfg.num_attention_heads, cfg.head_dim, args.layers
-    qkv_rows = (nq + 2 * cfg.num_key_value_heads) * hd
-    mm_per_tok = 2.0 * L * H * (qkv_rows + H + 3 * I)
-    attn = 4.0 * nq * hd * (S + 1) / 2 * L
-    flops = B * S * (mm_per_tok + attn) + 2.0 * B * H * cfg.vocab_size
-    try:
-        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
-            pk = json.load(f)
-        peak, peak_src = float(pk["bf16_tflops_sustained"]), "measured bf16_tflops_sustained (cuBLAS, long loop)"
-    except Exception:
-        peak, peak_src = 1400.0, "fallback sustained bf16"
-    tflops = flops / (ms * 1e-3) / 1e12
     if rank == 0:
         print(json.dumps({
             "mode": "prefill", "metric": "GLM-4-9B prefill tok/s and MFU (configuration 3)",
-            "value": B * S / (ms * 1e-3), "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
-            "ms_per_prefill": ms, "higher_is_better": True, "dtype": "bf16",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "bf16",
             "data": "synthetic: random-init N(0,0.02) bf16 weights (device RNG), uniform prompt ids seed 1",
             "config": {"workload": f"GLM-4-9B-shaped prefill, batch {B} x {S} tokens, causal, cache {S}, "
                                    f"{args.layers} layers, TP={world}", "batch": B, "seq": S, "tp": world,
                        "parallelism": f"tp{world}"},
-            "flops_per_prefill": flops, "achieved_tflops_per_gpu": tflops / world,
-            "mfu": tflops / world / peak, "peak_tflops": peak, "peak_source": peak_src,
+            **res,
             "flops_note": "matmul flops of every position without the all-position LM head, causal attention "
                           "flops, and the last-position LM head",
             "clocks": clk}), flush=True)
     mesh.close()
     if world > 1:
-        barrier()
+        dist.barrier()
         dist.destroy_process_group()
+
+
+def flash_config(jsx, vocab: int):
+    """GLM-4.7-Flash-shaped 4-layer slice (configuration 4)."""
+    return jsx.ModelConfig(hidden_size=2048, num_hidden_layers=4, num_attention_heads=20, num_key_value_heads=20,
+                           intermediate_size=10240, vocab_size=vocab, rms_norm_eps=1e-5,
+                           rope_theta=1000000.0, n_routed_experts=64, n_shared_experts=1, num_experts_per_tok=4,
+                           moe_intermediate_size=1536, routed_scaling_factor=1.8, norm_topk_prob=True,
+                           first_k_dense_replace=1, q_lora_rank=768, kv_lora_rank=512, qk_nope_head_dim=192,
+                           qk_rope_head_dim=64, v_head_dim=256, attention_bias=False, partial_rotary_factor=1.0)
+
+
+def measure_flash(jsx, mesh, dev, world: int, ctx: int, steps: int, warmup: int, seed: int, vocab: int,
+                  batches=(1, 32)) -> dict:
+    """Decode steps of the configuration-4 slice on `mesh` for both MLA forms (the
+    reference's expanded per-head cache, and the absorbed-weight latent cache), each a
+    CUDA graph of one step replayed `steps` times; ms per step = max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    cfg = flash_config(jsx, vocab)
+    out = {}
+    for absorbed in (False, True):
+        model = jsx.GLM4FlashForCausalLM(cfg, mesh, absorbed_mla=absorbed)
+        model.init_random(seed=seed)
+        form = "latent" if absorbed else "expanded"
+        for B in batches:
+            L = ctx + warmup + max(steps, 1) + 1
+            caches = model.init_kv_caches(B, L)
+            g = torch.Generator(device=dev).manual_seed(7)
+            for c_ in caches:
+                c_.k[:, :ctx].normal_(generator=g)
+                if c_.v.numel():
+                    c_.v[:, :ctx].normal_(generator=g)
+            ids = torch.from_numpy(np.random.default_rng(1).integers(0, cfg.vocab_size, (B, 1))
+                                   .astype(np.int32)).to(dev)
+            pos = torch.full((B, 1), ctx, dtype=torch.int32, device=dev)
+
+            def step():
+                model(ids, pos, None, kv_caches=caches, cache_position=None)
+                pos.add_(1)
+
+            for _ in range(max(warmup, 1)):  # eager: creates every lazily built resource
+                step()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                step()
+            pos.fill_(ctx + max(warmup, 1))
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(max(steps, 1)):
+                graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            del graph
+            ms = a.elapsed_time(b) / max(steps, 1)
+            if world > 1:
+                t = torch.tensor([ms], dtype=torch.float64, device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            cache_bytes = sum(c_.k.numel() + c_.v.numel() for c_ in caches) * 2 * (ctx + 1) // L
+            out[f"{form}_batch_{B}"] = {"value": B / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms,
+                                        "cache_bytes_read_per_step": cache_bytes}
+            del caches
+        del model
+        torch.cuda.synchronize()
+    return out
 
 
 def run_flash(args) -> None:
@@ -839,11 +988,11 @@ def run_flash(args) -> None:
     q_lora 768 / kv_lora 512 / nope 192 / rope 64 / v 256 / 20 heads, 64 routed experts of 1536
     with top-4 softmax routing and one shared expert of 1536, a dense SwiGLU MLP of 10240 in
     layer 0), random-init bf16 weights N(0, 0.02), batch 1 and 32 at context 1024 (the cache
-    rows before the position hold seeded random values).  Each step is the reference-signature
-    forward of one token per sequence through GLM4FlashForCausalLM on device-resident ids and
-    positions, captured once in a CUDA graph (the position advances inside the graph) and
-    replayed; time per step = CUDA events over --steps replays after --warmup, max over ranks.
-    Mesh: TP = min(2, N), EP = N / TP."""
+    rows before the position hold seeded random values), both MLA forms.  Each step is the
+    reference-signature forward of one token per sequence through GLM4FlashForCausalLM on
+    device-resident ids and positions, captured once in a CUDA graph (the position advances
+    inside the graph) and replayed; time per step = CUDA events over --steps replays after
+    --warmup, max over ranks.  Mesh: TP = min(2, N), EP = N / TP."""
     import torch
     import torch.distributed as dist
 
@@ -859,54 +1008,8 @@ def run_flash(args) -> None:
     K.set_pdl(not args.no_pdl)
     tp = min(2, world)
     mesh = jsx.create_mesh(tp=tp, ep=world // tp)
-    cfg = jsx.ModelConfig(hidden_size=2048, num_hidden_layers=4, num_attention_heads=20, num_key_value_heads=20,
-                          intermediate_size=10240, vocab_size=args.vocab, rms_norm_eps=1e-5,
-                          rope_theta=1000000.0, n_routed_experts=64, n_shared_experts=1, num_experts_per_tok=4,
-                          moe_intermediate_size=1536, routed_scaling_factor=1.8, norm_topk_prob=True,
-                          first_k_dense_replace=1, q_lora_rank=768, kv_lora_rank=512, qk_nope_head_dim=192,
-                          qk_rope_head_dim=64, v_head_dim=256, attention_bias=False, partial_rotary_factor=1.0)
-    model = jsx.GLM4FlashForCausalLM(cfg, mesh)
-    model.init_random(seed=args.seed)
     ctx = args.ctx
-    out = {}
-    for B in (1, 32):
-        L = ctx + args.warmup + max(args.steps, 1) + 1
-        caches = model.init_kv_caches(B, L)
-        g = torch.Generator(device=dev).manual_seed(7)
-        for c_ in caches:
-            c_.k[:, :ctx].normal_(generator=g)
-            c_.v[:, :ctx].normal_(generator=g)
-        ids = torch.from_numpy(np.random.default_rng(1).integers(0, cfg.vocab_size, (B, 1)).astype(np.int32)).to(dev)
-        pos = torch.full((B, 1), ctx, dtype=torch.int32, device=dev)
-
-        def step():
-            model(ids, pos, None, kv_caches=caches, cache_position=None)
-            pos.add_(1)
-
-        for _ in range(max(args.warmup, 1)):  # eager: creates every lazily built resource
-            step()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            step()
-        pos.fill_(ctx + max(args.warmup, 1))
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(max(args.steps, 1)):
-            graph.replay()
-        b.record()
-        torch.cuda.synchronize()
-        del graph
-        ms = a.elapsed_time(b) / max(args.steps, 1)
-        if world > 1:
-            t = torch.tensor([ms], dtype=torch.float64, device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            ms = float(t.item())
-        out[f"batch_{B}"] = {"value": B / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms}
-        del caches
+    out = measure_flash(jsx, mesh, dev, world, ctx, args.steps, args.warmup, args.seed, args.vocab)
     if rank == 0:
         print(json.dumps({"mode": "flash", "metric": "GLM-4.7-Flash-shaped MoE decode tok/s (configuration 4)",
                           "n_gpus": world, "mesh": {"tensor": tp, "expert": world // tp}, "steps": args.steps,
@@ -914,7 +1017,8 @@ def run_flash(args) -> None:
                           "data": "synthetic: random-init N(0,0.02) bf16 weights, random cache rows, seeded ids",
                           "config": {"workload": "GLM-4.7-Flash-shaped 4-layer slice, decode, context "
                                                  f"{ctx}, TP={tp} x EP={world // tp}"},
-                          "note": "one decode step captured in a CUDA graph and replayed",
+                          "note": ("one decode step captured in a CUDA graph and replayed; expanded = the "
+                                   "reference's per-head MLA cache, latent = the absorbed-weight form"),
                           **out}), flush=True)
     mesh.close()
     if world > 1:

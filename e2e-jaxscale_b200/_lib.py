@@ -71,6 +71,10 @@ SIGNATURES = {
     "jsx_wide_row_linear_allreduce": [P, P, P, P, I, I, I, P, SZ, P],
     "jsx_moe_gate": [P, P, P, P, P, I, I, I, I, F, I, P],
     "jsx_mla_rope_cache": [P, P, P, P, P, P, P, P, I, I, I, I, I, I, I, P],
+    "jsx_mla_latent_cache": [P, P, P, P, P, P, P, I, I, I, I, I, I, I, P],
+    "jsx_mla_absorb": [P, I, I, P, P, I, I, I, I, P],
+    "jsx_mla_decode_workspace_size": [I, I, I, I, P],
+    "jsx_mla_decode": [P, P, P, P, P, I, I, I, I, I, F, P, SZ, P],
     "jsx_moe_experts_workspace_size": [I, I, I, I, I, P],
     "jsx_moe_experts": [P, P, P, P, I, I, I, I, I, I, P, P, P, P, SZ, P],
     "jsx_row_linear_allreduce_add": [P, P, P, P, P, I, I, I, P],

@@ -19,7 +19,7 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(HERE, "libjsx.so")
 
-SOURCES = ["lib.cu", "gemv.cu", "attention.cu", "misc.cu", "comm.cu", "noalloc.cu", "decode_step.cu", "tc_gemm.cu", "tc_wide.cu", "attn_prefill.cu", "sample.cu", "moe.cu", "mla.cu"]
+SOURCES = ["lib.cu", "gemv.cu", "attention.cu", "misc.cu", "comm.cu", "noalloc.cu", "decode_step.cu", "tc_gemm.cu", "tc_wide.cu", "attn_prefill.cu", "sample.cu", "moe.cu", "mla.cu", "mla_absorbed.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

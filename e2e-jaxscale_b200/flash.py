@@ -30,12 +30,14 @@ from .layers.normalization import RMSNorm
 class GLM4FlashDecoderLayer:
     """models/glm4_flash.py:26-110."""
 
-    def __init__(self, config: ModelConfig, mesh, layer_id: int = 0, dtype=torch.bfloat16):
+    def __init__(self, config: ModelConfig, mesh, layer_id: int = 0, dtype=torch.bfloat16,
+                 absorbed_mla: bool = False):
         c = config
         self.layer_id = layer_id
         self.self_attn = MLAAttention(c.hidden_size, c.num_attention_heads, c.q_lora_rank, c.kv_lora_rank,
                                       c.qk_nope_head_dim, c.qk_rope_head_dim, c.v_head_dim,
-                                      c.max_position_embeddings, c.rope_theta, c.rms_norm_eps, mesh, dtype)
+                                      c.max_position_embeddings, c.rope_theta, c.rms_norm_eps, mesh, dtype,
+                                      absorbed=absorbed_mla)
         if layer_id < c.first_k_dense_replace:
             self.mlp = DenseMLP(c.hidden_size, c.intermediate_size, mesh, dtype)
         else:
@@ -58,14 +60,17 @@ class GLM4FlashDecoderLayer:
 
 class GLM4FlashForCausalLM:
     """models/glm4_flash.py:113-205: __call__(input_ids, positions, attention_mask,
-    kv_caches, cache_position) -> (logits [B, S, V], caches)."""
+    kv_caches, cache_position) -> (logits [B, S, V], caches).  absorbed_mla: the
+    attention runs in the latent-cache form (MLAAttention(absorbed=True)) and
+    init_kv_caches returns latent caches."""
 
-    def __init__(self, config: ModelConfig, mesh, dtype=torch.bfloat16):
+    def __init__(self, config: ModelConfig, mesh, dtype=torch.bfloat16, absorbed_mla: bool = False):
         self.config, self.mesh, self.dtype = config, mesh, dtype
+        self.absorbed_mla = absorbed_mla
         self.device = mesh.device if mesh is not None and mesh.device is not None else torch.device("cuda")
         c = config
         self.embed_tokens = Embed(c.vocab_size, c.hidden_size, dtype, mesh)
-        self.layers = [GLM4FlashDecoderLayer(c, mesh, i, dtype) for i in range(c.num_hidden_layers)]
+        self.layers = [GLM4FlashDecoderLayer(c, mesh, i, dtype, absorbed_mla) for i in range(c.num_hidden_layers)]
         self.norm = RMSNorm(c.hidden_size, epsilon=c.rms_norm_eps, param_dtype=dtype)
         self.lm_head = ParallelLMHead(c.vocab_size, c.hidden_size, dtype, mesh)
 
@@ -106,7 +111,10 @@ class GLM4FlashForCausalLM:
 
     def init_kv_caches(self, batch_size: int, max_seq_len: int) -> list[KVCache]:
         """Expanded per-head caches (layers/mla_attention.py:125-139): k [B, L, nh_l, nope + rope],
-        v [B, L, nh_l, v_head_dim] per layer, zero-initialised."""
+        v [B, L, nh_l, v_head_dim] per layer, zero-initialised; with absorbed_mla the latent
+        caches k [B, L, kv_lora + rope] (v empty)."""
+        if self.absorbed_mla:
+            return [lyr.self_attn.init_latent_cache(batch_size, max_seq_len, self.device) for lyr in self.layers]
         c = self.config
         tp = 1 if self.mesh is None else self.mesh.shape.get("tensor", 1)
         nh = c.num_attention_heads // tp

@@ -437,6 +437,50 @@ def mla_rope_cache(q_in, kv_in, k_rope, inv_freq, positions, q_out, k_cache, v_c
          _p(k_cache), _p(v_cache), M, tokens_per_seq, nh, nope, rope, vdim, k_cache.shape[1], _stream())
 
 
+def mla_latent_cache(q_in, c, k_rope, inv_freq, positions, q_rope, latent_cache, nh, nope, rope,
+                     tokens_per_seq=1):
+    """Absorbed-weight MLA: RoPE of the query's rope slice -> q_rope [M, nh, rope], and the
+    latent cache row [c | rope(k_rope)] of every token at its position
+    (latent_cache [B, L, kv_lora + rope])."""
+    for t, n in ((q_in, "q_in"), (c, "c"), (k_rope, "k_rope"), (q_rope, "q_rope"),
+                 (latent_cache, "latent_cache")):
+        _need(t, n)
+    _need(inv_freq, "inv_freq", torch.float32)
+    _need(positions, "positions", torch.int32)
+    M = positions.numel()
+    kv_lora = c.shape[-1]
+    call("jsx_mla_latent_cache", _p(q_in), _p(c), _p(k_rope), _p(inv_freq), _p(positions), _p(q_rope),
+         _p(latent_cache), M, tokens_per_seq, nh, nope, rope, kv_lora, latent_cache.shape[1], _stream())
+
+
+def mla_absorb(x, token_stride, head_stride, w, out, M, nh, R, K):
+    """out[m, h, r] = bf16(sum_k w[h, r, k] x[m, h, k]); x of token m, head h starts at
+    element m * token_stride + h * head_stride; w [nh, R, K]; out [M, nh, R]."""
+    _need(x, "x")
+    _need(w, "w")
+    _need(out, "out")
+    call("jsx_mla_absorb", _p(x), token_stride, head_stride, _p(w), _p(out), M, nh, R, K, _stream())
+
+
+def mla_decode_workspace(B, nh, kv_lora, max_seq, device) -> torch.Tensor:
+    n = ctypes.c_size_t(0)
+    call("jsx_mla_decode_workspace_size", B, nh, kv_lora, max_seq, ctypes.byref(n))
+    return torch.empty(n.value, dtype=torch.uint8, device=device)
+
+
+def mla_decode(q_abs, q_rope, latent_cache, ctx, positions, scale, workspace):
+    """Multi-query attention of every head over the latent cache rows [0, position]:
+    ctx [B, nh, kv_lora] = bf16(softmax(bf16(bf16(q_abs.c + q_rope.kr) * scale)) . c)."""
+    for t, n in ((q_abs, "q_abs"), (q_rope, "q_rope"), (latent_cache, "latent_cache"), (ctx, "ctx")):
+        _need(t, n)
+    _need(positions, "positions", torch.int32)
+    _need(workspace, "workspace", torch.uint8)
+    B, L, D = latent_cache.shape
+    nh, kv_lora = ctx.shape[-2], ctx.shape[-1]
+    call("jsx_mla_decode", _p(q_abs), _p(q_rope), _p(latent_cache), _p(ctx), _p(positions), B, nh, kv_lora,
+         D - kv_lora, L, ctypes.c_float(scale), _p(workspace), workspace.numel(), _stream())
+
+
 def moe_gate(x, w_nk, k, scale, norm=True, correction_bias=None, logits_given=False):
     """Router of layers/moe.py:54-79.  With logits_given, x holds bf16 logits [N, E]."""
     _need(x, "x")

@@ -350,6 +350,36 @@ int jsx_mla_rope_cache(const void* q_in, const void* kv_in, const void* k_rope, 
                        int tokens_per_seq, int nh, int nope, int rope, int vdim, int max_seq,
                        void* stream);
 
+/* Absorbed-weight MLA decode over a latent cache (the decode form that
+ * replaces the expanded per-head cache of layers/mla_attention.py:139-172 and
+ * the attention of :174-190; README.md:67 names it as the reference's fix).
+ * The cache holds per token the normalised kv latent c and the rotated shared
+ * rope key: latent_cache [B][max_seq][kv_lora + rope] bf16.
+ * jsx_mla_latent_cache: q_rope [M][nh][rope] = RoPE of the rope slice of q_in
+ *   [M][nh][nope + rope]; cache row of token m at positions[m] (sequence
+ *   m / tokens_per_seq) = [c[m] | RoPE(k_rope[m])] (rotary.py:56-58, :88-91). */
+int jsx_mla_latent_cache(const void* q_in, const void* c, const void* k_rope, const float* inv_freq,
+                         const int32_t* positions, void* q_rope, void* latent_cache, int M,
+                         int tokens_per_seq, int nh, int nope, int rope, int kv_lora, int max_seq,
+                         void* stream);
+/* Per-head absorption GEMV: out[m][h][r] = bf16(sum_k w[h][r][k] x[m][h][k]),
+ * x of (m, h) at x + m * x_token_stride + h * x_head_stride (elements).  With w
+ * = the key columns of kv_b per head ([nh][kv_lora][nope]) it forms q_abs from
+ * q_nope; with the value columns ([nh][v][kv_lora]) the head outputs from the
+ * latent context.  M <= 32, K <= 512 (multiple of 8). */
+int jsx_mla_absorb(const void* x, int x_token_stride, int x_head_stride, const void* w, void* out,
+                   int M, int nh, int R, int K, void* stream);
+/* Multi-query attention of nh <= 32 heads over the latent cache rows
+ * [0, positions[b]]: s = bf16(bf16(q_abs . c + q_rope . kr) * scale) (the
+ * reference rounds q.k, then the scaled score, to bf16), fp32 softmax,
+ * ctx[b][h] = bf16(P . c) [B][nh][kv_lora].  kv_lora a multiple of 256,
+ * kv_lora + rope <= 576.  Split over the context (64 rows) and merged in a
+ * second launch; workspace of jsx_mla_decode_workspace_size bytes. */
+int jsx_mla_decode_workspace_size(int B, int nh, int kv_lora, int max_seq, size_t* bytes);
+int jsx_mla_decode(const void* q_abs, const void* q_rope, const void* latent_cache, void* ctx,
+                   const int32_t* positions, int B, int nh, int kv_lora, int rope, int max_seq,
+                   float scale, void* workspace, size_t workspace_bytes, void* stream);
+
 /* MoE experts of one rank (layers/moe.py:194-267, _forward_ep / _topk_local_forward):
  * x[N][H] normalised hidden states, topk_w[N][K] bf16 and topk_idx[N][K] from
  * jsx_moe_gate; expert_owner[E] (device int32) names the rank that computes each

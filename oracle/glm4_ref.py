@@ -560,16 +560,26 @@ def mla_attention_absorbed(p: MLAParams, x, positions, mask, latent, cache_posit
     wkv = np.asarray(p.kv_b, np.float32).reshape(kv_lora, nh, nope + vdim)
     w_k, w_v = wkv[..., :nope], wkv[..., nope:]                             # [kv_lora, nh, nope|vdim]
     q_abs = bf16(np.einsum("bshn,lhn->bshl", q[..., :nope], w_k, dtype=np.float32))   # [B, S, nh, kv_lora]
-    lat = np.asarray(latent, np.float32)
     scale = np.float32((nope + rope_d) ** -0.5)
+    ctx = mla_latent_attention(q_abs, q_rope, latent, mask, scale)         # [B, S, nh, kv_lora]
+    out = bf16(np.einsum("bshl,lhv->bshv", ctx, w_v, dtype=np.float32)).reshape(B, S, nh * vdim)
+    return linear(out, p.o)
+
+
+def mla_latent_attention(q_abs, q_rope, latent, mask, scale):
+    """The attention step of mla_attention_absorbed: every head of q_abs [B, S, nh, kv_lora]
+    / q_rope [B, S, nh, rope] against the latent cache [B, L, kv_lora + rope] (key = the
+    whole row, value = its first kv_lora columns), scores rounded like the expanded form
+    (bf16(q.k), then bf16(* scale), layers/mla_attention.py:176-184), + mask [.., S, L],
+    fp32 softmax, bf16 probabilities; returns ctx = bf16(P . c) [B, S, nh, kv_lora]."""
+    kv_lora = q_abs.shape[-1]
+    lat = np.asarray(latent, np.float32)
     scores = (np.einsum("bshl,btl->bhst", q_abs, lat[..., :kv_lora], dtype=np.float32) +
               np.einsum("bshr,btr->bhst", q_rope, lat[..., kv_lora:], dtype=np.float32))
-    scores = bf16(bf16(scores) * scale)
+    scores = bf16(bf16(scores) * np.float32(scale))
     if mask is not None:
         scores = bf16(scores + np.asarray(mask, np.float32))
     m = scores.max(axis=-1, keepdims=True)
     e = np.exp(scores - m)
     probs = bf16(e / e.sum(axis=-1, keepdims=True, dtype=np.float32))
-    ctx = bf16(np.einsum("bhst,btl->bshl", probs, lat[..., :kv_lora], dtype=np.float32))  # [B, S, nh, kv_lora]
-    out = bf16(np.einsum("bshl,lhv->bshv", ctx, w_v, dtype=np.float32)).reshape(B, S, nh * vdim)
-    return linear(out, p.o)
+    return bf16(np.einsum("bhst,btl->bshl", probs, lat[..., :kv_lora], dtype=np.float32))
