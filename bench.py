@@ -83,6 +83,9 @@ def parse():
     # profiling-only shape overrides (a smaller device footprint for ncu captures)
     ap.add_argument("--layers", type=int, default=40, help=argparse.SUPPRESS)
     ap.add_argument("--vocab", type=int, default=151552, help=argparse.SUPPRESS)
+    # profiling only: build the model, set the positions to --ctx (cache rows of zeros; the
+    # kernels read the same bytes) and run this many eager decode steps at --batch, nothing else
+    ap.add_argument("--profile-steps", type=int, default=0, help=argparse.SUPPRESS)
     return ap.parse_args()
 
 
@@ -392,6 +395,21 @@ def run_gpu(args) -> None:
         return float(t.item())
 
     mesh = jsx.create_mesh(tp=args.gpus)
+    if args.profile_steps:
+        cfg = jsx.ModelConfig(num_hidden_layers=args.layers, vocab_size=args.vocab)
+        model = jsx.GLM4ForCausalLM(cfg, mesh)
+        model.init_random(seed=args.seed)
+        st = jsx.DecodeState(model, args.batch, args.ctx + args.profile_steps + 1)
+        st.pos.fill_(args.ctx)
+        for _ in range(args.profile_steps):
+            model.step(st, head=True)
+        torch.cuda.synchronize()
+        print(json.dumps({"mode": "profile", "steps": args.profile_steps, "batch": args.batch,
+                          "layers": args.layers, "vocab": args.vocab,
+                          "kernels_per_step": model.kernels_per_step(args.batch),
+                          "weight_bytes": model.weight_bytes()}), flush=True)
+        mesh.close()
+        return
     # correctness first: the same kernels on the stored parity model, at this TP
     parity = parity_gate(jsx, mesh, dev, world)
     failures = [] if parity["ok"] else ["parity gate"]

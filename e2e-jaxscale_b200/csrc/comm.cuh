@@ -153,4 +153,51 @@ __device__ __forceinline__ float ll_get(const CommDev& c, const unsigned long lo
   }
 }
 
+// Slow path of ll_sum_ranks: every slot polled in rank order (bounded by the
+// comm timeout; on timeout the error word is set and the slot counts as 0).
+static __device__ __noinline__ float ll_sum_ranks_poll(const unsigned long long* p0, size_t sstride, int world,
+                                                uint32_t* state, unsigned long long timeout_ns, uint32_t epoch) {
+  float s = 0.f;
+  const uint64_t t0 = globaltimer();
+  for (int src = 0; src < world; ++src) {
+    const unsigned long long* p = p0 + src * sstride;
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    for (uint32_t it = 1; (uint32_t)(w >> 32) != epoch; ++it) {
+      if (*reinterpret_cast<volatile uint32_t*>(state + kError)) break;
+      if ((it & 15u) == 0) {
+        if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
+          atomicOr(state + kError, 1u);
+          break;
+        }
+        __nanosleep(20);
+      }
+      asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    }
+    s += (uint32_t)(w >> 32) == epoch ? __uint_as_float((uint32_t)w) : 0.f;
+  }
+  return s;
+}
+
+// Sum in rank order of one value's LL slots (slot of rank src at p0 + src *
+// sstride) once they carry `epoch`: every rank's slot is loaded before any is
+// checked, so the sum costs one round trip when the pushes have landed.
+__device__ __forceinline__ float ll_sum_ranks(const CommDev& c, const unsigned long long* p0, size_t sstride,
+                                              uint32_t epoch) {
+  unsigned long long w[kMaxRanks];
+#pragma unroll
+  for (int src = 0; src < kMaxRanks; ++src)
+    if (src < c.world) asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w[src]) : "l"(p0 + src * sstride) : "memory");
+  float s = 0.f;
+  bool all = true;
+#pragma unroll
+  for (int src = 0; src < kMaxRanks; ++src) {
+    if (src < c.world) {
+      all = all && (uint32_t)(w[src] >> 32) == epoch;
+      s += __uint_as_float((uint32_t)w[src]);
+    }
+  }
+  return all ? s : ll_sum_ranks_poll(p0, sstride, c.world, c.state, c.timeout_ns, epoch);
+}
+
 }  // namespace jsx

@@ -139,8 +139,8 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a, CommDev c) {
         const int rem = e - gl * kRows * M;
         const int r = rem / M, m = rem - (rem / M) * M;
         const int row = (blockIdx.x + grid * gl) * kRows + r;
-        float s = 0.f;
-        for (int src = 0; src < c.world; ++src) s += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
+        const float s = ll_sum_ranks(c, data_ptr(c, c.rank, epoch & 1, 0, m) + row, (size_t)c.max_tokens * c.hidden,
+                                     epoch);
         bf16* hp = a.h + (size_t)m * a.N + row;
         *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(s));
       }
@@ -459,9 +459,8 @@ __global__ void __launch_bounds__(kStreamThreads, 1) k_gemv_stream(GemvArgs a, C
       const int rows = 2 * (b1 - b0);
       for (int e = threadIdx.x; e < rows * M; e += kThreads) {
         const int m = e / rows, row = 2 * b0 + (e - (e / rows) * rows);
-        float sum = 0.f;
-        for (int src = 0; src < c.world; ++src)
-          sum += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
+        const float sum = ll_sum_ranks(c, data_ptr(c, c.rank, epoch & 1, 0, m) + row,
+                                       (size_t)c.max_tokens * c.hidden, epoch);
         bf16* hp = a.h + (size_t)m * a.N + row;
         *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(sum));
       }

@@ -30,9 +30,10 @@
 // so the epilogue of tile i overlaps the main loop of tile i + 1.
 //
 // Across tensor-parallel ranks the row-parallel projection writes its summed
-// rank-local fp32 rows to the workspace and k_tc_rows_allreduce pushes them to
-// every peer as epoch-tagged LL words (P2P stores, comm.cuh), sums the ranks'
-// words in rank order and adds the residual.
+// rank-local fp32 rows to the workspace and k_tc_rows_allreduce exchanges them
+// in two shots (reduce-scatter to the owner of each row pair, owner sums in
+// rank order and adds the residual, all-gather of the result) as epoch-tagged
+// LL words carrying bf16 pairs (P2P stores, comm.cuh).
 //
 // No multicast anywhere.  Every mbarrier wait is time-bounded; on a timeout the
 // kernel sets its error word (jsx_device_error), the other roles of the CTA
@@ -273,6 +274,55 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
       uint32_t src[kTcMaxCluster];
 #pragma unroll
       for (int s = 0; s < kTcMaxCluster; ++s) src[s] = s < S ? cl_map(s_u32(xb), (uint32_t)s) : 0u;
+      if (EPI == EPI_ROWAR && !t.store_only) {
+        // single rank: h += bf16(sum); four entries at a time, every residual (and addend)
+        // pair loaded before any store (no load waits behind a store it cannot be
+        // proven not to alias)
+        for (int e0 = et; e0 < np * t.M; e0 += 4 * 128) {
+          float v0[4], v1[4];
+          uint32_t hv[4], ad[4];
+          size_t idx[4];
+          bool ok[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int e = e0 + 128 * u;
+            ok[u] = false;
+            v0[u] = v1[u] = 0.f;
+            idx[u] = 0;
+            if (e < np * t.M) {
+              const int m = e / np, p = pp0 + (e - m * np);
+              const uint32_t off = (uint32_t)(m * kTcBM + 2 * p) * 4u;
+#pragma unroll
+              for (int s = 0; s < kTcMaxCluster; ++s) {
+                if (s < S) {
+                  const float2 f = cl_ld2(src[s] + off);
+                  v0[u] += f.x;
+                  v1[u] += f.y;
+                }
+              }
+              const int row0 = tile * kTcBM + 2 * p;
+              ok[u] = row0 < t.N;
+              idx[u] = (size_t)m * t.N + row0;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            hv[u] = ok[u] ? *reinterpret_cast<const uint32_t*>(a.h + idx[u]) : 0u;
+            ad[u] = (ok[u] && a.addend) ? *reinterpret_cast<const uint32_t*>(a.addend + idx[u]) : 0u;
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (!ok[u]) continue;
+            float w0 = v0[u], w1 = v1[u];
+            if (a.addend) {
+              w0 += __uint_as_float(ad[u] << 16);
+              w1 += __uint_as_float(ad[u] & 0xffff0000u);
+            }
+            *reinterpret_cast<uint32_t*>(a.h + idx[u]) =
+                pack2(__uint_as_float(hv[u] << 16) + rbf(w0), __uint_as_float(hv[u] & 0xffff0000u) + rbf(w1));
+          }
+        }
+      } else
       for (int e = et; e < np * t.M; e += 128) {
         const int m = e / np, p = pp0 + (e - m * np);
         const uint32_t off = (uint32_t)(m * kTcBM + 2 * p) * 4u;
@@ -358,25 +408,103 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
 // CTA b owns row pairs [p0, p1); pushes this rank's fp32 rows to every rank's
 // LL slots, then reads its rows from every rank's slots once they carry the
 // call's epoch, sums them in rank order and adds the residual (comm.cuh).
+// Two-shot exchange of the rank-local fp32 rows `part` [M][N] that k_tc_gemm
+// (store_only) left in the workspace, as epoch-tagged LL words whose payload is
+// a bf16 pair (each rank's partial rounded to bf16, the reference's per-rank
+// result; the wide path rounds the same way):
+//   reduce-scatter: row pair g belongs to rank g / ppr; every rank stores its
+//     packed partial of pair g into the owner's slot [source rank][m][g - owner ppr];
+//   the owner sums the ranks' bf16 partials in fp32 in rank order, adds the
+//     residual, rounds once (h is then identical on every rank), stores h and
+//     pushes the packed result into every peer's gather slot [m][g];
+//   gather: the pairs other ranks own are read from the gather slots into h.
+// Each rank sends 2 x (world - 1) / world x M x N / 2 words, against world x M x N
+// words for a one-shot push of fp32 partials.  Waits: an owner waits only for
+// pushes that never wait; a gather waits only for owners.  Every CTA has
+// started (PDL trigger at entry) before a dependent kernel may occupy an SM.
+// Slots: the comm's LL words of the call's parity, gather slots after the
+// world x max_tokens x hidden / 2 reduce-scatter slots.
+__device__ __forceinline__ void ll_put_raw(unsigned long long* slot, uint32_t payload, uint32_t epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | payload;
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(slot), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load_raw(const unsigned long long* slot) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(slot) : "memory");
+  return w;
+}
+// bounded poll of one slot for `epoch`; on timeout the comm's error word is set and 0 returned
+__device__ __noinline__ uint32_t ll_wait_raw(uint32_t* state, unsigned long long timeout_ns,
+                                             const unsigned long long* slot, uint32_t epoch) {
+  if (*reinterpret_cast<volatile uint32_t*>(state + kError)) return 0u;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    const unsigned long long w = ll_load_raw(slot);
+    if ((uint32_t)(w >> 32) == epoch) return (uint32_t)w;
+    if ((it & 15u) == 0) {
+      if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
+        atomicOr(state + kError, 1u);
+        return 0u;
+      }
+      __nanosleep(20);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(256) k_tc_rows_allreduce(GemvArgs a, const float* __restrict__ part, CommDev c) {
   pdl_wait();
   pdl_launch_dependents();
-  const int M = a.M, NB = a.N >> 1;
-  const int p0 = (int)((long long)blockIdx.x * NB / gridDim.x);
-  const int p1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
+  const int M = a.M, NB = a.N >> 1, W = c.world;
+  const int ppr = (NB + W - 1) / W;  // row pairs per owner
   const uint32_t epoch = read_epoch(c);
-  for (int e = threadIdx.x; e < (p1 - p0) * M; e += blockDim.x) {
-    const int m = e / (p1 - p0), g = p0 + (e - m * (p1 - p0));
+  const int par = epoch & 1;
+  const size_t rs_words = (size_t)W * c.max_tokens * (c.hidden >> 1);
+  const int nthreads = gridDim.x * blockDim.x, tid = blockIdx.x * blockDim.x + threadIdx.x;
+  // reduce-scatter pushes
+  for (int e = tid; e < M * NB; e += nthreads) {
+    const int m = e / NB, g = e - m * NB;
     const float2 v = __ldcg(reinterpret_cast<const float2*>(part + (size_t)m * a.N + 2 * g));
-    epi_pair<EPI_ROWAR>(a, c, true, epoch, g, m, v.x, v.y);
+    const int d = g / ppr;
+    unsigned long long* slot = data_ptr(c, d, par, 0, 0) + ((size_t)c.rank * c.max_tokens + m) * ppr + (g - d * ppr);
+    ll_put_raw(slot, pack2(v.x, v.y), epoch);
   }
-  const int rows = 2 * (p1 - p0);
-  for (int e = threadIdx.x; e < rows * M; e += blockDim.x) {
-    const int m = e / rows, row = 2 * p0 + (e - (e / rows) * rows);
-    float sum = 0.f;
-    for (int src = 0; src < c.world; ++src) sum += ll_get(c, data_ptr(c, c.rank, epoch & 1, src, m) + row, epoch);
-    bf16* hp = a.h + (size_t)m * a.N + row;
-    *hp = __float2bfloat16_rn(__bfloat162float(*hp) + rbf(sum));
+  // owner: sum the ranks' partials of the pairs this rank owns, residual, push the result
+  const int g0 = c.rank * ppr, gn = max(0, min(NB, g0 + ppr) - g0);  // pairs [g0, g0 + gn) are this rank's
+  const unsigned long long* mine = data_ptr(c, c.rank, par, 0, 0);
+  for (int e = tid; e < M * gn; e += nthreads) {
+    const int m = e / gn, pl = e - m * gn, g = g0 + pl;
+    uint32_t* hp = reinterpret_cast<uint32_t*>(a.h + (size_t)m * a.N + 2 * g);
+    const uint32_t hv = *hp;
+    unsigned long long w[kMaxRanks];
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src)
+      if (src < W) w[src] = ll_load_raw(mine + ((size_t)src * c.max_tokens + m) * ppr + pl);
+    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src) {
+      if (src < W) {
+        const uint32_t pv = (uint32_t)(w[src] >> 32) == epoch
+                                ? (uint32_t)w[src]
+                                : ll_wait_raw(c.state, c.timeout_ns, mine + ((size_t)src * c.max_tokens + m) * ppr + pl,
+                                              epoch);
+        s0 += __uint_as_float(pv << 16);
+        s1 += __uint_as_float(pv & 0xffff0000u);
+      }
+    }
+    const uint32_t hn = pack2(__uint_as_float(hv << 16) + rbf(s0), __uint_as_float(hv & 0xffff0000u) + rbf(s1));
+    *hp = hn;
+    for (int d = 0; d < W; ++d)
+      if (d != c.rank) ll_put_raw(data_ptr(c, d, par, 0, 0) + rs_words + (size_t)m * (c.hidden >> 1) + g, hn, epoch);
+  }
+  // gather the pairs the other ranks own
+  const int others = NB - gn;
+  for (int e = tid; e < M * others; e += nthreads) {
+    const int m = e / others, k = e - m * others;
+    const int g = k < g0 ? k : k + gn;
+    const unsigned long long* slot = mine + rs_words + (size_t)m * (c.hidden >> 1) + g;
+    const unsigned long long w = ll_load_raw(slot);
+    const uint32_t hn = (uint32_t)(w >> 32) == epoch ? (uint32_t)w : ll_wait_raw(c.state, c.timeout_ns, slot, epoch);
+    *reinterpret_cast<uint32_t*>(a.h + (size_t)m * a.N + 2 * g) = hn;
   }
   __syncthreads();
   if (threadIdx.x == 0) {

@@ -376,13 +376,42 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
           if (lane == 0) tc_arrive(acce + b);
         }
         const int m0 = tt * kWBN + 32 * ch + 16 * odd;
+        if constexpr (EPI == EPI_ROWAR) {
+          // residual (and addend) pairs of the 16 tokens loaded before any store: the
+          // compiler cannot prove the stores do not alias the next loads, so loads
+          // issued between them would each wait for a round trip
+          uint32_t hv[16], ad[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          // even lane: rows (own, partner) of token j; odd lane: (partner, own) of token 16 + j
-          const float own = odd ? v[16 + j] : v[j];
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[16 + j], 1);
-          const int m = m0 + j;
-          if (live && m < t.M) wide_pair<EPI>(a, g, m, odd ? other : own, odd ? own : other, b0, b1);
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + j;
+            const bool ok = live && m < t.M;
+            hv[j] = ok ? *reinterpret_cast<const uint32_t*>(a.h + (size_t)m * a.N + row0) : 0u;
+            ad[j] = (ok && a.addend) ? *reinterpret_cast<const uint32_t*>(a.addend + (size_t)m * a.N + row0) : 0u;
+          }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const float own = odd ? v[16 + j] : v[j];
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[16 + j], 1);
+            const int m = m0 + j;
+            if (live && m < t.M) {
+              float v0 = odd ? other : own, v1 = odd ? own : other;
+              if (a.addend) {
+                v0 += __uint_as_float(ad[j] << 16);
+                v1 += __uint_as_float(ad[j] & 0xffff0000u);
+              }
+              *reinterpret_cast<uint32_t*>(a.h + (size_t)m * a.N + row0) =
+                  pack2(__uint_as_float(hv[j] << 16) + rbf(v0), __uint_as_float(hv[j] & 0xffff0000u) + rbf(v1));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            // even lane: rows (own, partner) of token j; odd lane: (partner, own) of token 16 + j
+            const float own = odd ? v[16 + j] : v[j];
+            const float other = __shfl_xor_sync(0xffffffffu, odd ? v[j] : v[16 + j], 1);
+            const int m = m0 + j;
+            if (live && m < t.M) wide_pair<EPI>(a, g, m, odd ? other : own, odd ? own : other, b0, b1);
+          }
         }
       }
     }

@@ -2,11 +2,16 @@
 parallel, bias), partial neox RoPE, static-cache write, SDPA over the cache,
 o_proj (row-parallel, all-reduced over the tensor axis).
 
-Kernels: jsx_qkv_rope_cache (projections + bias + RoPE + cache write in one
-weight stream), jsx_attn_decode (GQA over cache rows [0, position]),
-jsx_row_linear_allreduce (o_proj + all-reduce).  Queries are processed one
-sequence position at a time, which is the causal prefill of the reference
-(mask of runner.py:33-46) and its decode step (runner.py:49-63).
+Kernels, decode (one new position per sequence, or short prompts):
+jsx_qkv_rope_cache (projections + bias + RoPE + cache write in one weight
+stream), jsx_attn_decode (GQA over cache rows [0, position]),
+jsx_row_linear_allreduce (o_proj + all-reduce), one position at a time.
+Prompt blocks of 64 tokens or more whose positions run start .. start + S - 1
+for every sequence go through in one pass: jsx_wide_qkv_rope_cache (tcgen05
+projections + bias + RoPE + cache write), jsx_attn_prefill (causal, rows
+[0, start + i]), jsx_wide_row_linear_allreduce (o_proj + the tile-exchange
+all-reduce) — the reference's prefill with the mask of runner.py:33-46.
+Workspaces and scratch buffers are allocated once per shape and reused.
 
 Masks: the attention_mask argument is accepted for signature compatibility and
 not read; attention always covers cache rows [0, position], which is exactly
@@ -16,6 +21,7 @@ cache_position (true for every call the runner makes).
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from .. import kernels as K
@@ -49,6 +55,7 @@ class GQAAttention:
                                           partial_rotary_factor)
         self._packed = None
         self._key = None
+        self._bufs = {}
 
     # --- per-rank shapes ---
     @property
@@ -100,9 +107,12 @@ class GQAAttention:
         nq_l = self.local_heads
         _, nkv_l = self.kv_range()
         w_qkv, b_qkv, w_o = self.packed(dev)
-        pos = positions.to(device=dev, dtype=torch.int32).reshape(B, S)
+        pos = torch.as_tensor(np.asarray(positions) if not torch.is_tensor(positions) else positions)
+        pos = pos.to(device=dev, dtype=torch.int32).reshape(B, S)
         if cache_position is not None:
-            cp = cache_position.to(device=dev, dtype=torch.int32).reshape(1, S)
+            cp = torch.as_tensor(np.asarray(cache_position) if not torch.is_tensor(cache_position)
+                                 else cache_position)
+            cp = cp.to(device=dev, dtype=torch.int32).reshape(1, S)
             if not torch.equal(pos, cp.expand(B, S)):
                 raise ValueError("positions must equal cache_position for every sequence")
         if kv_cache is None:
@@ -112,12 +122,34 @@ class GQAAttention:
             cache = kv_cache
         L = cache.k.shape[1]
         inv = self.rotary_emb.inv_freq(dev)
-        ws = K.attn_workspace(B, nq_l, nkv_l, hd, L, dev)
-        comm = self.mesh.comm(K.MAX_DECODE_TOKENS, H) if self.tp > 1 else None
         x = hidden_states.contiguous()
+        rot = self.rotary_emb.rotary_dim
+        start = int(pos[0, 0])
+        if S > 1 and B * S >= 64 and torch.equal(
+                pos, (torch.arange(S, dtype=torch.int32, device=dev) + start).expand(B, S)):
+            # the whole block in one pass
+            M = B * S
+            key = ("wide", M, str(dev))
+            if key not in self._bufs:
+                self._bufs[key] = (
+                    K.wide_workspace(M, [(H, w_qkv.shape[0]), (nq_l * hd, H)], dev),
+                    torch.empty((M, nq_l * hd), dtype=torch.bfloat16, device=dev),
+                    torch.empty((M, nq_l * hd), dtype=torch.bfloat16, device=dev))
+            ws, q, o = self._bufs[key]
+            K.wide_qkv_rope_cache(x.reshape(M, H), ln_gamma, eps, w_qkv, b_qkv, inv, pos.reshape(-1), q,
+                                  cache.k, cache.v, nq_l, nkv_l, hd, rot, ws, tokens_per_seq=S)
+            K.attn_prefill(q, cache.k, cache.v, nq_l, nkv_l, hd, S, start_pos=start, scale=self.scaling, out=o)
+            y = torch.zeros((M, H), dtype=torch.bfloat16, device=dev)
+            K.wide_row_linear_allreduce(self.mesh.comm_tiles(M, H) if self.tp > 1 else None, o, w_o, y, ws)
+            return y.reshape(B, S, H), (cache if kv_cache is not None else None)
+        key = ("decode", B, L, str(dev))
+        if key not in self._bufs:
+            self._bufs[key] = (K.attn_workspace(B, nq_l, nkv_l, hd, L, dev),
+                               torch.empty((B, nq_l * hd), dtype=torch.bfloat16, device=dev),
+                               torch.empty((B, nq_l * hd), dtype=torch.bfloat16, device=dev))
+        ws, q, o = self._bufs[key]
+        comm = self.mesh.comm(K.MAX_DECODE_TOKENS, H) if self.tp > 1 else None
         out = torch.zeros((B, S, H), dtype=torch.bfloat16, device=dev)
-        q = torch.empty((B, nq_l * hd), dtype=torch.bfloat16, device=dev)
-        o = torch.empty((B, nq_l * hd), dtype=torch.bfloat16, device=dev)
         step = K.MAX_DECODE_TOKENS
         for s in range(S):
             xs = x[:, s].contiguous()
@@ -125,12 +157,12 @@ class GQAAttention:
             for b0 in range(0, B, step):
                 b1 = min(B, b0 + step)
                 K.qkv_rope_cache(xs[b0:b1], ln_gamma, eps, w_qkv, b_qkv, inv, ps[b0:b1], q[b0:b1],
-                                 cache.k[b0:b1], cache.v[b0:b1], nq_l, nkv_l, hd,
-                                 self.rotary_emb.rotary_dim)
+                                 cache.k[b0:b1], cache.v[b0:b1], nq_l, nkv_l, hd, rot)
             K.attn_decode(q, cache.k, cache.v, o, ps, self.scaling, ws)
-            ys = torch.zeros((B, H), dtype=torch.bfloat16, device=dev)
+            ys = out[:, s]
             for b0 in range(0, B, step):
                 b1 = min(B, b0 + step)
-                K.row_linear_allreduce(comm, o[b0:b1], w_o, ys[b0:b1])
-            out[:, s] = ys
+                yb = torch.zeros((b1 - b0, H), dtype=torch.bfloat16, device=dev)
+                K.row_linear_allreduce(comm, o[b0:b1], w_o, yb)
+                ys[b0:b1] = yb
         return out, (cache if kv_cache is not None else None)

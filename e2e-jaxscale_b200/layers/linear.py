@@ -4,7 +4,13 @@ kernel_axes (None, "tensor") = column-parallel: this rank computes its output
 shard; ("tensor", None) = row-parallel: this rank holds an input shard and the
 result is all-reduced over the tensor axis (the XLA all-reduce implied by the
 replicated output constraint at layers/linear.py:72-78) inside the fused
-jsx_row_linear_allreduce kernel.
+row-parallel kernels: up to 8 tokens the CUDA-core GEMV with the LL-word
+all-reduce (jsx_row_linear_allreduce), up to 32 the tensor-core product
+(jsx_tc_row_linear_allreduce), beyond that the wide tensor-core GEMM with its
+in-epilogue tile exchange (jsx_wide_row_linear_allreduce).  A row-parallel bias
+(replicated, layers/linear.py:80-81) is added after the all-reduce: the output
+rows start as the bias and the kernels add bf16(sum of the partials), which is
+the reference's bf16(bf16(x @ W) + b).
 """
 
 from __future__ import annotations
@@ -29,6 +35,7 @@ class LinearBase:
         self.bias = Param(None) if use_bias else None
         self._packed = None
         self._key = None
+        self._ws = {}
 
     # --- sharding (utils/weight_utils.py:248-265) ---
     @property
@@ -74,16 +81,30 @@ class LinearBase:
             self._key = key
         return self._packed
 
+    def _workspace(self, kind: str, M: int, K_: int, N: int, device) -> torch.Tensor:
+        key = (kind, M, str(device))
+        if key not in self._ws:
+            self._ws[key] = (K.tc_workspace(M, [(K_, N)], device) if kind == "tc"
+                             else K.wide_workspace(M, [(K_, N)], device, norm=False))
+        return self._ws[key]
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         w_nk, b = self._ensure_packed(x.device)
         if self.is_row_parallel:
+            N, K_ = w_nk.shape
+            x2 = x.reshape(-1, K_).contiguous()
+            M = x2.shape[0]
             if b is not None:
-                raise NotImplementedError("row-parallel LinearBase with a bias is not on the GLM-4 path")
-            comm = self.mesh.comm(K.MAX_DECODE_TOKENS, w_nk.shape[0])
-            x2 = x.reshape(-1, w_nk.shape[1]).contiguous()
-            y = torch.zeros((x2.shape[0], w_nk.shape[0]), dtype=torch.bfloat16, device=x.device)
-            for m0 in range(0, x2.shape[0], K.MAX_DECODE_TOKENS):
-                m1 = min(x2.shape[0], m0 + K.MAX_DECODE_TOKENS)
-                K.row_linear_allreduce(comm, x2[m0:m1], w_nk, y[m0:m1])
-            return y.reshape(*x.shape[:-1], w_nk.shape[0])
+                y = b.reshape(1, N).expand(M, N).contiguous()
+            else:
+                y = torch.zeros((M, N), dtype=torch.bfloat16, device=x.device)
+            if M <= K.MAX_DECODE_TOKENS:
+                K.row_linear_allreduce(self.mesh.comm(K.TC_MAX_TOKENS, N), x2, w_nk, y)
+            elif M <= K.TC_MAX_TOKENS:
+                K.tc_row_linear_allreduce(self.mesh.comm(K.TC_MAX_TOKENS, N), x2, w_nk, y,
+                                          self._workspace("tc", M, K_, N, x.device))
+            else:
+                K.wide_row_linear_allreduce(self.mesh.comm_tiles(M, N), x2, w_nk, y,
+                                            self._workspace("wide", M, K_, N, x.device))
+            return y.reshape(*x.shape[:-1], N)
         return K.linear(x.contiguous(), w_nk, bias=b)

@@ -229,6 +229,29 @@ def _worker(rank, world, port, q):
             dist.all_gather(allw, hdw.cpu())
             out["wide_identical"].append(all(torch.equal(allw[0], t) for t in allw))
 
+        # (j) the reference-API row-parallel LinearBase with a bias (layers/linear.py:72-81):
+        #     GEMV, tensor-core and wide paths by token count, the bias added after the all-reduce
+        lin_mod = importlib.import_module("e2e-jaxscale_b200.layers.linear")
+        Kl, Nl = 1024, 512
+        wlin = ref.bf16(rng.standard_normal((Kl, Nl)) * 0.03)
+        blin = ref.bf16(rng.standard_normal(Nl) * 0.1)
+        lin = lin_mod.LinearBase(Kl, Nl, mesh, use_bias=True, kernel_axes=("tensor", None))
+        lin.weight.value, lin.bias.value = wlin, blin
+        out["lin_errs"], out["lin_identical"] = [], []
+        for Ml in (3, 20, 100):
+            xl = ref.bf16(rng.standard_normal((Ml, Kl)))
+            xs_l = ref.shard_columns(xl, world, rank)
+            yl = lin(_bf(xs_l, dev))
+            torch.cuda.synchronize()
+            want_l = ref.bf16(ref.row_parallel_reference([ref.shard_columns(xl, world, r) for r in range(world)],
+                                                         [ref.shard_rows(wlin, world, r) for r in range(world)])
+                              + blin)
+            got_l = yl.float().cpu().numpy()
+            out["lin_errs"].append(float(np.max(np.abs(got_l - want_l)) / np.max(np.abs(want_l))))
+            all_l = [torch.empty_like(yl.cpu()) for _ in range(world)]
+            dist.all_gather(all_l, yl.cpu())
+            out["lin_identical"].append(all(torch.equal(all_l[0], t) for t in all_l))
+
         # (i) the GLM-4-9B-shaped parity gate of bench.py at this TP
         sys.path.insert(0, ROOT)
         bench = importlib.import_module("bench")
@@ -290,5 +313,7 @@ def test_tensor_parallel(world):
         assert max(res[r]["wide_errs"]) <= 1e-2, res[r]["wide_errs"]
         assert all(res[r]["wide_identical"])
         assert res[r]["parity"]["ok"], res[r]["parity"]
+        assert max(res[r]["lin_errs"]) <= 1e-2, res[r]["lin_errs"]
+        assert all(res[r]["lin_identical"])
     assert res[0]["timeout_status"] == 3  # JSX_ETIMEDOUT
     assert res[0]["after_timeout"] == 8 * 64.0
