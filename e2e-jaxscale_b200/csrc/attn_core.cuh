@@ -31,6 +31,8 @@ struct AttnArgs {
   uint64_t* trace; // null, or 8 %globaltimer stamps of group 0: item (0, 0) start, staged,
                    // scores, softmax, P.V done, completion counted; the group's merge done,
                    // the group's merge start (its last split counted)
+  int no_merge;    // items only write their split records; the consumer merges them
+                   // (whole-step kernel, small groups: the o_proj staging)
 };
 
 __device__ __forceinline__ void attn_stamp(const AttnArgs& a, int vb, int s, int k) {
@@ -128,6 +130,7 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int s, in
   // the next kernel may launch once every item has reached this point (only
   // the merges remain), not earlier: its CTAs would take SMs from later items
   pdl_launch_dependents();
+  if (a.no_merge) return;  // the records are merged by their consumer after a grid barrier
   __threadfence();
   __syncthreads();
   if (tid == 0) is_last = atomicAdd(a.cnt + vb, 1u) == (uint32_t)(a.splits - 1);

@@ -127,7 +127,7 @@ class Mesh:
         if self.tp == 1:
             return None
         key = (max_tokens, hidden)
-        if key not in self._comms:
+        if key not in self._comms or not self._comms[key].handle:
             self._comms[key] = Comm(self.tp_rank, self.tp, max_tokens, hidden,
                                     group=self.group("tensor"), timeout_s=timeout_s)
         return self._comms[key]
@@ -138,7 +138,7 @@ class Mesh:
         if self.tp == 1:
             return None
         key = ("tiles", max_tokens, hidden)
-        if key not in self._comms:
+        if key not in self._comms or not self._comms[key].handle:
             self._comms[key] = Comm(self.tp_rank, self.tp, max_tokens, hidden,
                                     group=self.group("tensor"), timeout_s=timeout_s, tiles=True)
         return self._comms[key]
@@ -159,7 +159,7 @@ class Mesh:
         if self.moe_world == 1:
             return None
         key = ("moe", max_tokens, hidden)
-        if key not in self._comms:
+        if key not in self._comms or not self._comms[key].handle:
             self._comms[key] = Comm(self.moe_rank, self.moe_world, max_tokens, hidden,
                                     group=self.group_moe(), timeout_s=timeout_s)
         return self._comms[key]
