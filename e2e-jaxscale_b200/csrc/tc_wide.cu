@@ -238,6 +238,24 @@ __device__ __forceinline__ void wide_exchange_tile(const CommDev& c, const WideA
   }
 }
 
+// The k-th tile this CTA computes (tiles.. from blockIdx.x in steps of the grid),
+// t.tiles past the end.  With the tile exchange, the tiles other ranks own come
+// first (their partials are pushed without waiting) and this rank's own tiles
+// last, so by the time the owner sums a tile its peers have had the whole first
+// part of the schedule to push their partials of it: the owner's epilogue, and
+// with it the tensor cores, no longer idle at every owned tile.  Deadlock-free:
+// the first part never waits, the second part waits only on it.
+template <int EPI>
+__device__ __forceinline__ int wide_tile_at(const WideArgs& t, const CommDev& c, int k) {
+  const int G = gridDim.x, b = blockIdx.x;
+  if (!(EPI == EPI_ROWAR && c.world > 1)) return b + k * G < t.tiles ? b + k * G : t.tiles;
+  int seen = 0;
+  for (int pass = 0; pass < 2; ++pass)
+    for (int tile = b; tile < t.tiles; tile += G)
+      if (((tile % c.world) == c.rank) == (pass == 1) && seen++ == k) return tile;
+  return t.tiles;
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constant__ CUtensorMap tw,
                                                             const __grid_constant__ CUtensorMap tx, const WideArgs t,
@@ -287,7 +305,8 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
       pdl_wait();  // the activations come from the previous kernel
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < t.tiles && ok; tile += gridDim.x) {
+      for (int k = 0, tile = wide_tile_at<EPI>(t, c, 0); tile < t.tiles && ok;
+           ++k, tile = wide_tile_at<EPI>(t, c, k)) {
         int ft, tt;
         wide_tile(t, tile, ft, tt);
         for (int kb = 0; kb < t.kblocks; ++kb, ++it) {
@@ -312,7 +331,8 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
     if (lane == 0) {
       uint32_t it = 0, ai = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < t.tiles && ok; tile += gridDim.x, ++ai) {
+      for (int k = 0, tile = wide_tile_at<EPI>(t, c, 0); tile < t.tiles && ok;
+           ++k, tile = wide_tile_at<EPI>(t, c, k), ++ai) {
         const uint32_t b = ai & 1;
         if (ai >= 2 && !w_wait(acce + b, ((ai >> 1) - 1) & 1, abort_flag)) break;
         tc_fence_after();
@@ -346,7 +366,8 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
     const bool xchg = EPI == EPI_ROWAR && c.world > 1;
     const uint32_t epoch = xchg ? read_epoch(c) : 0u;
     uint32_t ai = 0;
-    for (int tile = blockIdx.x; tile < t.tiles; tile += gridDim.x, ++ai) {
+    for (int k = 0, tile = wide_tile_at<EPI>(t, c, 0); tile < t.tiles;
+         ++k, tile = wide_tile_at<EPI>(t, c, k), ++ai) {
       const uint32_t b = ai & 1;
       // warp-uniform: the tcgen05.ld below needs the whole warp
       if (!__all_sync(0xffffffffu, w_wait(accf + b, (ai >> 1) & 1, abort_flag))) break;

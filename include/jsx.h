@@ -186,7 +186,10 @@ int jsx_lmhead_argmax(jsx_comm* comm, const void* h, const void* norm_gamma, flo
  * models/glm4.py:118-120, :47-49, :193, layers/embedding.py:79-92) for
  * batches where one weight element feeds 2*M >= 18 flops.  Sums are fp32
  * like the GEMV path but in a different order, so results agree with it to
- * fp32 rounding, not bitwise.
+ * fp32 rounding, not bitwise.  Across ranks, jsx_tc_row_linear_allreduce
+ * rounds each rank's partial to bf16 (the reference's per-rank result) and
+ * exchanges in two shots (row pairs to their owner rank, owner sum in rank
+ * order + residual, gather), as bf16-pair LL words in the comm buffer.
  * workspace: jsx_tc_workspace_size(M, K, N) bytes, 16-byte aligned; for
  * jsx_tc_lmhead_argmax its first 512 bytes must be zero on the first call
  * (they are left zero). */
