@@ -430,11 +430,20 @@ __device__ __forceinline__ void stage_attn_merge(const AttnArgs& at, bf16* xs, f
     const float2* r2 = reinterpret_cast<const float2*>(at.part + (size_t)vb * at.splits * stride);
     const float* w = cw + (size_t)vb * at.splits * gi;
     float2 o = make_float2(0.f, 0.f);
-    for (int t = 0; t < used; ++t) {
-      const float wt = w[t * gi + h];
-      const float2 v = __ldcg(r2 + (size_t)t * (stride >> 1) + k);
-      o.x = fmaf(v.x, wt, o.x);
-      o.y = fmaf(v.y, wt, o.y);
+    // eight splits' loads in flight before their products (the same t order)
+    for (int t0 = 0; t0 < used; t0 += 8) {
+      float2 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[u] = t0 + u < used ? __ldcg(r2 + (size_t)(t0 + u) * (stride >> 1) + k) : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (t0 + u < used) {
+          const float wt = w[(t0 + u) * gi + h];
+          o.x = fmaf(v[u].x, wt, o.x);
+          o.y = fmaf(v[u].y, wt, o.y);
+        }
+      }
     }
     const int col = (kvh * G + j * gi) * hd + (k << 1);
     *reinterpret_cast<uint32_t*>(xs + (size_t)b * qd + col) = pack2(o.x, o.y);
