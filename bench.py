@@ -19,6 +19,13 @@ value:  B / step time, whole job (the TP ranks cooperate on the same tokens:
 e2e:    the same metric through the public API with host buffers: every step
         copies the fed token ids from pinned host memory, replays the step and
         reads the greedy ids back (the reference's per-step host sync).
+configs: after the decode measurement the same ranks time short versions of
+        configuration 2 (isolated row-parallel op, fused vs cuBLAS + NCCL),
+        configuration 3 (32 x 1024-token prefill, MFU) and configuration 4 (the
+        GLM-4.7-Flash slice in both MLA forms, TP = min(2, N) x EP = N / TP),
+        reported compactly under "configs" (--no-configs skips them).
+exposed_comm_us: per layer, the row-parallel exchanges' time on the critical
+        path beyond their products (whole-step kernel stamps, max over ranks).
 parity: before timing, at every GPU count, a 2-layer GLM-4-9B-shaped model
         (vocabulary 8192, host-seeded weights) runs teacher-forced through the
         same kernels (whole-step kernel at batch 1, tensor-core chain at batch
@@ -255,11 +262,18 @@ def measured_hbm_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def ncu_traffic(key: str):
+def ncu_traffic(key: str, layers: int, lm_head_bytes: int):
+    """DRAM bytes of one step from the ncu fit in profiles/ncu_traffic.json (captured at 2 and
+    4 layers with a 16384-entry vocabulary, TP=1): per_layer * layers + fixed, the captured
+    LM head replaced by this run's.  None where no capture exists (TP > 1: ncu does not run
+    on multi-rank commands)."""
     path = os.path.join(ROOT, "profiles", "ncu_traffic.json")
     try:
         with open(path) as f:
-            return json.load(f).get(key)
+            e = json.load(f).get(key)
+        if not e:
+            return None
+        return e["per_layer"] * layers + e["fixed"] - e["lm_head_capture"] + lm_head_bytes
     except Exception:
         return None
 
@@ -517,11 +531,12 @@ def run_gpu(args) -> None:
 
         fused = model.fused_step and st.step_args is not None
         phase_us, exposed = None, None
+        lm_bytes = model.lm_head.numel() * 2
+        traffic = ncu_traffic(f"decode_step_tp{args.gpus}_b{B}", c.num_hidden_layers, lm_bytes)
         if fused:
             # the whole step is one kernel launch: its duration is the timed step
             kern_name = "jsx_decode_step (k_decode_step<M>): the whole decode step, one launch per step"
             kern_ms, kern_bytes = ms, step_bytes
-            trafkey = f"decode_step_tp{args.gpus}_b{B}"
             # per-phase breakdown from the kernel's %globaltimer trace (CTA 0, after each grid barrier)
             nl = c.num_hidden_layers
             tr = torch.zeros(2 + 13 * nl, dtype=torch.int64, device=dev)
@@ -568,32 +583,11 @@ def run_gpu(args) -> None:
                                 "phase including its barrier; CTA 0 %globaltimer over 8 eager steps; "
                                 "attention_group0_us: head group 0 from the start of the attention phase")
         else:
-            # dominant op: fused gate/up + SwiGLU, one call per layer's weights (every layer once:
-            # 40 x 224 MB streams past the L2 between two calls on the same weights)
-            lp0 = model.layers[0]
-            if st.tc:
-                m = min(B, K.TC_MAX_TOKENS)
-                gu = lambda lp: K.tc_gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m],
-                                                    st.tc_ws)
-                kern_name = ("jsx_tc_gate_up_swiglu (k_rmsnorm_vec + k_tc_gemm<EPI_SWIGLU>: tcgen05/TMA, "
-                             "K split across thread-block clusters), the two launches timed together")
-                trafkey = f"tc_gate_up_swiglu_tp{args.gpus}_m{m}"
-            else:
-                m = min(B, K.MAX_DECODE_TOKENS)
-                gu = lambda lp: K.gate_up_swiglu(st.h[:m], lp.ln2, cfg.rms_norm_eps, lp.w_gu, st.act[:m])
-                kern_name = "jsx_gate_up_swiglu (k_gemv<M,EPI_SWIGLU>)"
-                trafkey = f"gate_up_swiglu_tp{args.gpus}_m{m}"
-            gu(lp0)  # loads the module
-            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in model.layers]
-            torch.cuda.synchronize()
-            for (ea, eb), lp in zip(ev, model.layers):
-                ea.record(stream)
-                gu(lp)
-                eb.record(stream)
-            torch.cuda.synchronize()
-            kern_ms = statistics.median([ea.elapsed_time(eb) for ea, eb in ev])
-            kern_bytes = lp0.w_gu.numel() * 2 + m * cfg.hidden_size * 2 + m * model.I_l * 2 + cfg.hidden_size * 2
+            # the tensor-core chain: the step is one CUDA graph of its launches; its algorithmic
+            # bytes over its time
+            kern_name = (f"the batch-{B} step: {model.kernels_per_step(B)} launches (RMSNorm, tcgen05 GEMMs "
+                         "k_tc_gemm<EPI>, decode attention, two-shot exchanges at TP > 1) in one CUDA graph")
+            kern_ms, kern_bytes = ms, step_bytes
         achieved = kern_bytes / (kern_ms * 1e-3) / 1e9
         graph.release()
         del st, graph
@@ -603,8 +597,8 @@ def run_gpu(args) -> None:
             "step_bytes": step_bytes, "phase_us": phase_us, "exposed": exposed, "checks": checks,
             "roofline": {"bound": "hbm", "kernel": kern_name,
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                         "peak_source": f"{peak_kind} hbm_gbs (burst, kernel timed alone)",
-                         "traffic": ncu_traffic(trafkey), "algorithmic_bytes_per_launch": kern_bytes,
+                         "peak_source": f"{peak_kind} hbm_gbs (burst)",
+                         "traffic": traffic, "algorithmic_bytes_per_launch": kern_bytes,
                          "launch_ms": kern_ms},
             "launches": model.kernels_per_step(B, head=True) * args.steps,
         }

@@ -598,6 +598,7 @@ static TcPlan tc_plan(int M, int K, int N) {
 CommDev comm_view(jsx_comm* comm);
 
 static uint64_t* g_trace_buf = nullptr;  // jsx_tc_set_trace
+uint64_t* tc_trace_buffer() { return g_trace_buf; }  // also stamped by the wide GEMM (tc_wide.cu)
 
 template <int EPI>
 static int tc_run(jsx_comm* comm, GemvArgs ga, void* workspace, size_t workspace_bytes, cudaStream_t s) {

@@ -75,7 +75,15 @@ __device__ __forceinline__ bool w_wait(uint64_t* b, uint32_t parity, volatile ui
 struct WideArgs {
   int M, N, K, kblocks;
   int ntt, nft, tiles;  // token tiles, weight tiles, ntt * nft
+  uint64_t* trace;      // null, or [grid][8] %globaltimer stamps (jsx_tc_set_trace): 0 entry,
+                        // 1 first accumulator at the epilogue, 2 epilogue done with the tiles
+                        // other ranks own, 3 with every tile, 4 finished tiles gathered,
+                        // 5 last MMA commit, 6 last TMA load issued, 7 exit
 };
+
+__device__ __forceinline__ void wide_stamp(const WideArgs& t, int k) {
+  if (t.trace) t.trace[(size_t)blockIdx.x * 8 + k] = globaltimer();
+}
 
 // tile -> (weight tile ft, token tile tt): groups of kWGroup token tiles,
 // weight-tile-major inside a group
@@ -296,6 +304,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
   tc_fence_after();
   const uint32_t tmem = misc[0];
   pdl_launch_dependents();
+  if (threadIdx.x == 0) wide_stamp(t, 0);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -321,6 +330,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
           tma_load_2d(st + kWABytes, &tx, kb * kTcBK, tt * kWBN, full + s);
         }
       }
+      wide_stamp(t, 6);
       // every copy issued must land before the CTA exits
       const uint32_t first = it > (uint32_t)kWStages ? it - kWStages : 0u;
       for (uint32_t j = first; j < it; ++j) w_wait(full + j % kWStages, (j / kWStages) & 1, nullptr);
@@ -354,6 +364,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         }
         if (ok) tc_commit(accf + b);
       }
+      wide_stamp(t, 5);
       tc_commit(fin);  // arrives once every MMA issued above has completed
       w_wait(fin, 0, nullptr);
     }
@@ -372,6 +383,12 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
       // warp-uniform: the tcgen05.ld below needs the whole warp
       if (!__all_sync(0xffffffffu, w_wait(accf + b, (ai >> 1) & 1, abort_flag))) break;
       tc_fence_after();
+      if (warp == 2 && lane == 0) {
+        if (ai == 0) wide_stamp(t, 1);
+        // the first owned tile: the tiles other ranks own are done
+        if (xchg && tile % c.world == c.rank && (ai == 0 || wide_tile_at<EPI>(t, c, k - 1) % c.world != c.rank))
+          wide_stamp(t, 2);
+      }
       int ft, tt;
       wide_tile(t, tile, ft, tt);
       const int row0 = (ft * kWBM + 32 * q + lane) & ~1;  // this lane's row pair
@@ -436,6 +453,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         }
       }
     }
+    if (warp == 2 && lane == 0) wide_stamp(t, 3);
     if (xchg) {
       // the tiles this CTA computed for other owners: their finished rows -> h
       for (int tile = blockIdx.x; tile < t.tiles; tile += gridDim.x) {
@@ -459,6 +477,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         }
       }
     }
+    if (warp == 2 && lane == 0) wide_stamp(t, 4);
     __syncwarp();
   }
 
@@ -471,6 +490,7 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kWTmemCols)
                  : "memory");
   }
+  if (threadIdx.x == 0) wide_stamp(t, 7);
   if (EPI == EPI_ROWAR && c.world > 1 && threadIdx.x == 0) {
     // the last CTA advances the comm's call counter (the epoch of the next call)
     const uint32_t epoch = read_epoch(c);
@@ -489,6 +509,8 @@ struct WidePlan {
   size_t bytes;
 };
 
+uint64_t* tc_trace_buffer();  // tc_gemm.cu (jsx_tc_set_trace)
+
 static WidePlan wide_plan(int M, int K, int N, bool norm) {
   WidePlan p;
   p.t.M = M;
@@ -498,6 +520,7 @@ static WidePlan wide_plan(int M, int K, int N, bool norm) {
   p.t.ntt = (M + kWBN - 1) / kWBN;
   p.t.nft = (N + kWBM - 1) / kWBM;
   p.t.tiles = p.t.ntt * p.t.nft;
+  p.t.trace = tc_trace_buffer();
   const int sms = sm_count();
   p.grid = p.t.tiles < sms ? p.t.tiles : sms;
   p.bytes = kWOffXn + (norm ? (((size_t)M * K * 2 + 1023) & ~(size_t)1023) : 0);

@@ -198,7 +198,11 @@ int jsx_tc_workspace_size(int M, int K, int N, size_t* bytes);
  * jsx_tc_* launch of this process stamps %globaltimer (ns) per CTA into
  * buf[cta * 8 + k], k = 0 entry, 1 first ring of loads issued, 2 loads done,
  * 3 first stage consumed, 4 last MMA issued, 5 first accumulator read,
- * 6 epilogue done, 7 exit; buf holds 8 x (SM count) u64.  NULL turns it off. */
+ * 6 epilogue done, 7 exit; every jsx_wide_* launch as well, k = 0 entry,
+ * 1 first accumulator at the epilogue, 2 epilogue done with the tiles other
+ * ranks own, 3 with every tile, 4 finished tiles gathered, 5 last MMA commit,
+ * 6 last load issued, 7 exit.  buf holds 8 x (SM count) u64.  NULL turns it
+ * off. */
 int jsx_tc_set_trace(uint64_t* buf);
 int jsx_tc_linear(const void* x, const void* gamma, float eps, const void* w_nk, const void* bias,
                   void* y, int M, int K, int N, void* workspace, size_t workspace_bytes,
