@@ -22,7 +22,6 @@
 // (jsx_device_error) and the kernel runs on to its end without waiting.
 #include <stdio.h>
 #include <stdlib.h>
-#include <string.h>
 
 #include "attn_core.cuh"
 #include "comm.cuh"
@@ -105,78 +104,12 @@ __device__ __forceinline__ void trace_mark(uint64_t* trace, int& n) {
   ++n;
 }
 
-// First weight batch of this warp's first row pair of the next GEMV phase into
-// registers and, with a landing zone `wl` (this warp's kUnroll x kRows x 32
-// vectors of shared memory), the second batch by cp.async: with K <= 4096 the
-// whole row pair is in flight while the barrier completes.  Each lane copies
-// and later reads only its own vectors, so its cp.async wait is the only sync.
-__device__ __forceinline__ void prefetch(Batch& bt, const bf16* w, int K, int N, uint4* wl) {
+// First weight batch of this warp's first row pair of the next GEMV phase.
+__device__ __forceinline__ void prefetch(Batch& bt, const bf16* w, int K, int N) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = blockIdx.x + gridDim.x * warp;
   const int nvec = K >> 3;
-  if (g >= N / kRows) return;
-  const uint4* wv = reinterpret_cast<const uint4*>(w) + (size_t)g * kRows * nvec;
-  load_batch(bt, wv, nvec, 0, lane);
-  if (wl != nullptr) {
-#pragma unroll
-    for (int u = 0; u < kUnroll; ++u) {
-      const int v = 32 * kUnroll + u * 32 + lane;
-#pragma unroll
-      for (int r = 0; r < kRows; ++r)
-        if (v < nvec)
-          asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(smem_addr(wl + (u * kRows + r) * 32 + lane)),
-                       "l"(wv + (size_t)r * nvec + v)
-                       : "memory");
-    }
-  }
-}
-
-// One weight batch (vectors [base, base + 32 kUnroll) of a row pair) into this
-// warp's landing zone; `zero` is 0 and only orders the copy after the reads of
-// the zone's previous contents (it is derived from their products).
-__device__ __forceinline__ void land_batch(uint4* wl, const uint4* wv, int nvec, int base, int lane, int zero) {
-#pragma unroll
-  for (int u = 0; u < kUnroll; ++u) {
-    const int v = base + u * 32 + lane;
-#pragma unroll
-    for (int r = 0; r < kRows; ++r)
-      if (v < nvec)
-        asm volatile("cp.async.cg.shared.global.L2::256B [%0], [%1], 16;" ::"r"(smem_addr(wl + (u * kRows + r) * 32 + lane + zero)),
-                     "l"(wv + (size_t)r * nvec + v)
-                     : "memory");
-  }
-}
-
-// fma_batch with the weights read from the landing zone (the same arithmetic and order).
-template <int M>
-__device__ __forceinline__ void fma_batch_landed(const uint4* wl, const uint4* __restrict__ xv, int nvec, int base,
-                                                 int lane, float (&acc)[kRows][M]) {
-#pragma unroll
-  for (int u = 0; u < kUnroll; ++u) {
-    const int v = base + u * 32 + lane;
-    if (v < nvec) {
-      float wf[kRows][8];
-#pragma unroll
-      for (int r = 0; r < kRows; ++r) unpack8(wl[(u * kRows + r) * 32 + lane], wf[r]);
-#pragma unroll
-      for (int m = 0; m < M; ++m) {
-        float xf[8];
-        unpack8(xv[m * nvec + v], xf);
-#pragma unroll
-        for (int r = 0; r < kRows; ++r)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[r][m] = fmaf(wf[r][j], xf[j], acc[r][m]);
-      }
-    }
-  }
-}
-
-// 0, computed from two accumulators (a dependency the compiler cannot remove)
-template <int M>
-__device__ __forceinline__ int zero_after(const float (&acc)[kRows][M]) {
-  int z;
-  asm volatile("and.b32 %0, %1, 0;" : "=r"(z) : "r"(__float_as_int(acc[0][0]) ^ __float_as_int(acc[kRows - 1][M - 1])));
-  return z;
+  if (g < N / kRows) load_batch(bt, reinterpret_cast<const uint4*>(w) + (size_t)g * kRows * nvec, nvec, 0, lane);
 }
 
 // L2 prefetch of this warp's first row pairs of a later GEMV phase: bytes
@@ -212,60 +145,28 @@ __device__ __forceinline__ void trace_max(uint64_t* slot) {
 constexpr int kMergeWeights = 1024;
 constexpr size_t kMergeRecordBytes = 80 * 1024;
 
-// Phases whose second weight batch lands in shared memory during the barrier
-// before them (kernel argument wl_mask; environment JSX_STEP_LANDING on the host).
-enum { kLandQkv = 1, kLandO = 2, kLandGateUp = 4, kLandDown = 8, kLandLmHead = 16 };
-
 // One GEMV phase (bt holds the first batch of this warp's first group).
 template <int M, int EPI>
 __device__ __forceinline__ void gemv_phase(const GemvArgs& ga, const CommDev& c, bool multi, uint32_t epoch,
-                                           const bf16* xs, Batch& bt, unsigned long long (&best)[M],
-                                           uint4* wl) {
+                                           const bf16* xs, Batch& bt, unsigned long long (&best)[M]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = ga.K >> 3, ngroups = ga.N / kRows, G = gridDim.x;
   const uint4* wbase = reinterpret_cast<const uint4*>(ga.w);
   const size_t gvecs = (size_t)kRows * nvec;
   const uint4* xv = reinterpret_cast<const uint4*>(xs);
-  const int g_first = blockIdx.x + G * warp;
-  constexpr int BV = 32 * kUnroll;  // vectors per batch
-  const int nb = (nvec + BV - 1) / BV;
-  for (int g = g_first; g < ngroups; g += G * kWarps) {
+  for (int g = blockIdx.x + G * warp; g < ngroups; g += G * kWarps) {
     const uint4* wv = wbase + (size_t)g * gvecs;
-    const int gn = g + G * kWarps;
     float acc[kRows][M];
 #pragma unroll
     for (int r = 0; r < kRows; ++r)
 #pragma unroll
       for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
-    bool next_loaded = false;
-    if (wl == nullptr) {
-      for (int b = 0; b < nb; ++b) {
-        if (b > 0) load_batch(bt, wv, nvec, b * BV, lane);
-        fma_batch<M>(bt, xv, nvec, b * BV, lane, acc);
-      }
-    } else {
-      // double buffering: even batches in registers, odd ones in the landing zone; each
-      // buffer is refilled (with batch b + 2, or the next group's batch 0 / 1) as soon as
-      // it has been consumed, so two batches are in flight at any time
-      for (int b = 0; b < nb; ++b) {
-        if ((b & 1) == 0) {
-          fma_batch<M>(bt, xv, nvec, b * BV, lane, acc);
-          if (b + 2 < nb) {
-            load_batch(bt, wv, nvec, (b + 2) * BV, lane);
-          } else if (gn < ngroups) {
-            load_batch(bt, wbase + (size_t)gn * gvecs, nvec, 0, lane);
-            next_loaded = true;
-          }
-        } else {
-          cp_async_wait_all();
-          fma_batch_landed<M>(wl, xv, nvec, b * BV, lane, acc);
-          const int z = zero_after<M>(acc);
-          if (b + 2 < nb) land_batch(wl, wv, nvec, (b + 2) * BV, lane, z);
-          else if (gn < ngroups) land_batch(wl, wbase + (size_t)gn * gvecs, nvec, BV, lane, z);
-        }
-      }
+    for (int base = 0; base < nvec; base += 32 * kUnroll) {
+      if (base > 0) load_batch(bt, wv, nvec, base, lane);
+      fma_batch<M>(bt, xv, nvec, base, lane, acc);
     }
-    if (gn < ngroups && !next_loaded) load_batch(bt, wbase + (size_t)gn * gvecs, nvec, 0, lane);
+    const int gn = g + G * kWarps;
+    if (gn < ngroups) load_batch(bt, wbase + (size_t)gn * gvecs, nvec, 0, lane);
 #pragma unroll
     for (int r = 0; r < kRows; ++r)
 #pragma unroll
@@ -452,18 +353,10 @@ __device__ __forceinline__ void stage_attn_merge(const AttnArgs& at, bf16* xs, f
 }
 
 template <int M>
-__global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_args a, CommDev c, int wl_off,
-                                                              int wl_mask, int cmerge) {
+__global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_args a, CommDev c, int cmerge) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float cmerge_w[kMergeWeights];
   bf16* xs = reinterpret_cast<bf16*>(smem_raw);
-  // this warp's landing zone for the second weight batch (past the staged activations), used
-  // for the phases in wl_mask (kLand*), or none
-  // (computed where used, from the kernel arguments: no registers held across the phases)
-#define JSX_LAND(bit)                                                                                   \
-  ((wl_off > 0 && (wl_mask & (bit)))                                                                    \
-       ? reinterpret_cast<uint4*>(smem_raw + wl_off) + (threadIdx.x >> 5) * (kUnroll * kRows * 32)    \
-       : nullptr)
   __shared__ bool is_last;
   __shared__ unsigned long long cta_best[kWarps][M];
   __shared__ unsigned long long fin[M];
@@ -503,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
 #pragma unroll
   for (int m = 0; m < M; ++m) best[m] = 0ull;
   grid_arrive(bar, gen);
-  prefetch(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows, JSX_LAND(kLandQkv));
+  prefetch(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows);
   grid_wait(bar, gen);
   trace_mark(a.trace, tn);
 
@@ -544,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.nq = a.n_heads; ga.nkv = a.n_kv_heads; ga.hd = a.head_dim; ga.rot = a.rotary_dim;
       ga.max_seq = a.max_seq; ga.tps = 1;
       stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best, JSX_LAND(kLandQkv));
+      gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best);
       l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden, 0u, a.l2_next_bytes);
     }
     at.trace = a.trace ? a.trace + (2 + 5 * a.n_layers) + 8 * l : nullptr;
@@ -567,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
         attn_item_any<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
     }
     grid_arrive(bar, gen);
-    prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden, JSX_LAND(kLandO));
+    prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden);
     grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- o_proj + all-reduce + residual (layers/attention.py:159, models/glm4.py:124) ----
@@ -580,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       const uint32_t ep = epoch0 + 2u * l;
       if (cmerge) stage_attn_merge<M>(at, xs, cmerge_w);
       else stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best, JSX_LAND(kLandO));
+      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
       uint64_t* ar = a.trace_ar ? a.trace_ar + 4 * l : nullptr;
       trace_max(ar);
       l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter, a.l2_attn_bytes,
@@ -589,7 +482,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       trace_max(ar ? ar + 1 : nullptr);
     }
     grid_arrive(bar, gen);
-    prefetch(bt, reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter, JSX_LAND(kLandGateUp));
+    prefetch(bt, reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter);
     grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- post-attention norm + gate/up + SwiGLU (models/glm4.py:128, :46-48) ----
@@ -602,11 +495,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.M = M; ga.K = a.hidden; ga.N = 2 * a.inter;
       ga.y = reinterpret_cast<bf16*>(a.act);
       stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0u, xs, bt, best, JSX_LAND(kLandGateUp));
+      gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0u, xs, bt, best);
       l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden, 0u, a.l2_next_bytes);
     }
     grid_arrive(bar, gen);
-    prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden, JSX_LAND(kLandDown));
+    prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden);
     grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- down_proj + all-reduce + residual (models/glm4.py:49, :130) ----
@@ -618,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.h = reinterpret_cast<bf16*>(a.h);
       const uint32_t ep = epoch0 + 2u * l + 1u;
       stage_x<M, false, true>(ga, xs);
-      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best, JSX_LAND(kLandDown));
+      gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
       uint64_t* ar = a.trace_ar ? a.trace_ar + 4 * l + 2 : nullptr;
       trace_max(ar);
       if (l + 1 < a.n_layers)
@@ -632,9 +525,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     }
     grid_arrive(bar, gen);
     if (l + 1 < a.n_layers)
-      prefetch(bt, reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows, JSX_LAND(kLandQkv));
+      prefetch(bt, reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows);
     else if (a.head)
-      prefetch(bt, reinterpret_cast<const bf16*>(a.lm_head), a.hidden, a.vocab_local, JSX_LAND(kLandLmHead));
+      prefetch(bt, reinterpret_cast<const bf16*>(a.lm_head), a.hidden, a.vocab_local);
     grid_wait(bar, gen);
   trace_mark(a.trace, tn);
   }
@@ -662,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     ga.y = reinterpret_cast<bf16*>(a.logits);
     ga.vocab_offset = a.vocab_offset;
     stage_x<M, false, true>(ga, xs);
-    gemv_phase<M, EPI_LMHEAD>(ga, c, multi, 0u, xs, bt, best, JSX_LAND(kLandLmHead));
+    gemv_phase<M, EPI_LMHEAD>(ga, c, multi, 0u, xs, bt, best);
   }
   if (lane == 0) {
 #pragma unroll
@@ -715,37 +608,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   }
 }
 
-#undef JSX_LAND
-
-// Shared memory of the whole-step kernel: staged activations [M][kmax], the
-// weight landing zones of the 8 warps when they fit next to them within the
-// two-CTAs-per-SM budget (wl_off > 0), or the attention items' tiles, whichever
-// is larger.
-constexpr size_t kLandingBytes = (size_t)kWarps * kUnroll * kRows * 32 * sizeof(uint4);
-
-// Phases using the landing zone: JSX_STEP_LANDING (a kLand* mask), default none.  At
-// TP=1, batch 1, every mask measured no faster (3.65 ms with and without the q/k/v
-// phase's, 3.69 with the down projection's, 4.7 ms with all phases double-buffered):
-// the bytes the landing zone puts in flight at a barrier slow the previous phase's
-// last warps, and the cp.async stream of the bandwidth-bound phases is slower than
-// the register stream.
-static int landing_mask() {
-  const char* env = getenv("JSX_STEP_LANDING");
-  return env == nullptr ? 0 : atoi(env) & 31;
-}
-
-static size_t step_smem(const jsx_decode_step_args& a, int* wl_off) {
+static size_t step_smem(const jsx_decode_step_args& a) {
   const int M = a.batch;
   int kmax = a.hidden;
   if (a.inter > kmax) kmax = a.inter;
   if (a.n_heads * a.head_dim > kmax) kmax = a.n_heads * a.head_dim;
-  size_t x = (size_t)M * kmax * sizeof(bf16);
-  const size_t off = (x + 127) & ~(size_t)127;
-  *wl_off = 0;
-  if (landing_mask() != 0 && off + kLandingBytes <= kStepMergeSmemMax) {
-    *wl_off = (int)off;
-    x = off + kLandingBytes;
-  }
+  const size_t x = (size_t)M * kmax * sizeof(bf16);
   const AttnLayout lay = attn_layout(M, a.n_heads, a.n_kv_heads, a.head_dim, a.max_seq);
   size_t at = attn_smem(lay.gi, a.head_dim, lay.splits);
   if (attn_use_mma(lay.gi, a.head_dim)) {
@@ -828,10 +696,9 @@ extern "C" int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args,
     JSX_REQUIRE(a.batch <= c.max_tokens && a.hidden <= c.hidden,
                 "batch %d / hidden %d exceed the comm buffer", a.batch, a.hidden);
   }
-  int wl_off = 0;
-  const size_t smem = step_smem(a, &wl_off);
-  const int cmerge = consumer_merge(a);
+  const size_t smem = step_smem(a);
   JSX_REQUIRE(smem <= kMaxDynSmem, "step needs %zu bytes of shared memory", smem);
+  const int cmerge = consumer_merge(a);
 #define JSX_STEP_CASE(MM)                                                                    \
   case MM: {                                                                                 \
     auto kern = k_decode_step<MM>;                                                           \
@@ -853,7 +720,7 @@ extern "C" int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args,
     attr[0].val.cooperative = 1;                                                             \
     cfg.attrs = attr;                                                                        \
     cfg.numAttrs = 1;                                                                        \
-    JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, a, c, wl_off, landing_mask(), cmerge));          \
+    JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, a, c, cmerge));                                  \
     return JSX_OK;                                                                           \
   }
   switch (a.batch) {

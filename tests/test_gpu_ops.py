@@ -140,6 +140,10 @@ def test_gate_up_swiglu(jsx, ref, cuda, rng, M, H, I):
     (1, 32, 2, 128, 1100, [1024]),
     (2, 4, 1, 128, 64, [31, 32]),
     (1, 20, 20, 256, 100, [63]),
+    # 16-head groups of many sequences: the records do not fit shared memory and the
+    # splits are merged by the separate merge launch
+    (32, 32, 2, 128, 1100, [1024 - 31 * i for i in range(32)]),
+    (8, 16, 1, 128, 600, [599, 0, 64, 63, 300, 1, 128, 511]),
 ])
 def test_attn_decode(jsx, ref, cuda, rng, B, nq, nkv, hd, L, pos):
     q = rand_bf16(ref, rng, (B, nq, hd))
