@@ -193,25 +193,35 @@ __device__ __forceinline__ void wide_exchange_tile(const CommDev& c, const WideA
       for (int k = 0; k < 4; ++k)
 #pragma unroll
         for (int i = 0; i < 8; ++i) sum[k][i] = 0.f;
-      for (int src = 0; src < c.world; ++src) {
-        uint4 u[4];
-        if (src == c.rank) {
+      // four sources' slots loaded at a time, then summed in rank order
+      for (int s0 = 0; s0 < c.world; s0 += 4) {
+        uint4 u[4][4];
 #pragma unroll
-          for (int k = 0; k < 4; ++k) u[k] = part[k];
-        } else {
-          const bf16* sp = slot_ptr(c, c.rank, jo, src, q) + mlc * 32;
+        for (int sj = 0; sj < 4; ++sj) {
+          const int src = s0 + sj;
+          if (src >= c.world) continue;
+          if (src == c.rank) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            const int e = lane + 32 * k;
-            u[k] = __ldcg(reinterpret_cast<const uint4*>(sp + (e >> 2) * 32 + 8 * (e & 3)));
+            for (int k = 0; k < 4; ++k) u[sj][k] = part[k];
+          } else {
+            const bf16* sp = slot_ptr(c, c.rank, jo, src, q) + mlc * 32;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int e = lane + 32 * k;
+              u[sj][k] = __ldcg(reinterpret_cast<const uint4*>(sp + (e >> 2) * 32 + 8 * (e & 3)));
+            }
           }
         }
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          float f[8];
-          unpack8(u[k], f);
+        for (int sj = 0; sj < 4; ++sj) {
+          if (s0 + sj >= c.world) continue;
 #pragma unroll
-          for (int i = 0; i < 8; ++i) sum[k][i] += f[i];
+          for (int k = 0; k < 4; ++k) {
+            float f[8];
+            unpack8(u[sj][k], f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) sum[k][i] += f[i];
+          }
         }
       }
 #pragma unroll
@@ -404,6 +414,18 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
                            acce + b, stg + (warp - 2) * (32 * 32));
         continue;
       }
+      // row-parallel: this lane's residual pairs of 16 tokens per 32-token chunk, loaded one
+      // chunk ahead (the next chunk's loads are issued before this chunk's stores: the
+      // compiler cannot prove the stores do not alias later loads, so loads issued after
+      // them would each wait for a round trip)
+      uint32_t hv[16];
+      if constexpr (EPI == EPI_ROWAR) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = tt * kWBN + 16 * odd + j;
+          hv[j] = (live && m < t.M) ? *reinterpret_cast<const uint32_t*>(a.h + (size_t)m * a.N + row0) : 0u;
+        }
+      }
 #pragma unroll 1
       for (int ch = 0; ch < kWBN / 32; ++ch) {
         float v[32];
@@ -415,15 +437,13 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
         }
         const int m0 = tt * kWBN + 32 * ch + 16 * odd;
         if constexpr (EPI == EPI_ROWAR) {
-          // residual (and addend) pairs of the 16 tokens loaded before any store: the
-          // compiler cannot prove the stores do not alias the next loads, so loads
-          // issued between them would each wait for a round trip
-          uint32_t hv[16], ad[16];
+          uint32_t hn[16], ad[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
-            const int m = m0 + j;
+            const int m = m0 + j, mn = m + 32;
             const bool ok = live && m < t.M;
-            hv[j] = ok ? *reinterpret_cast<const uint32_t*>(a.h + (size_t)m * a.N + row0) : 0u;
+            hn[j] = (ch + 1 < kWBN / 32 && live && mn < t.M)
+                        ? *reinterpret_cast<const uint32_t*>(a.h + (size_t)mn * a.N + row0) : 0u;
             ad[j] = (ok && a.addend) ? *reinterpret_cast<const uint32_t*>(a.addend + (size_t)m * a.N + row0) : 0u;
           }
 #pragma unroll
@@ -441,6 +461,8 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
                   pack2(__uint_as_float(hv[j] << 16) + rbf(v0), __uint_as_float(hv[j] & 0xffff0000u) + rbf(v1));
             }
           }
+#pragma unroll
+          for (int j = 0; j < 16; ++j) hv[j] = hn[j];
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
