@@ -28,56 +28,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_decode(AttnArgs a) {
   attn_item_any<kAttnThreads, false, false>(a, blockIdx.x, blockIdx.y, smem_raw);
 }
 
-// Split merge as its own launch, one CTA per (item group, head), when a group's
-// records do not fit the items' shared memory (large batches: 16-head groups of
-// many sequences).  The last-arriving split would otherwise merge them from L2
-// with one dependent round trip per few splits and output vectors, ~20 us at
-// 32 sequences; here each thread owns one output dimension and has all its
-// splits' loads in flight.  Same arithmetic and order as attn_finish's L2 form:
-// M = max over splits, L = sum of l_t exp(m_t - M) in split order,
-// out = sum_t fma(acc_t, exp(m_t - M) / L) in split order.
-__global__ void __launch_bounds__(kAttnThreads) k_attn_merge(AttnArgs a) {
-  pdl_wait();
-  const int vb = blockIdx.y, h = blockIdx.x;  // group, head inside the group
-  const int gi = a.gi, hd = a.hd, stride = split_stride(gi, hd);
-  const int b = vb / (a.nkv * a.hg);
-  const int kvh = (vb / a.hg) % a.nkv, j = vb % a.hg;
-  const int head = kvh * (a.nq / a.nkv) + j * gi + h;
-  int cur = a.pos[b];
-  if (cur > a.max_seq - 1) cur = a.max_seq - 1;
-  if (cur < 0) cur = 0;
-  const int used = (cur + kChunk) / kChunk;
-  const float* pb = a.part + (size_t)vb * a.splits * stride;
-  __shared__ float w[1024];
-  if (threadIdx.x == 0) {
-    float M = -INFINITY;
-    for (int t = 0; t < used; ++t) M = fmaxf(M, __ldcg(pb + (size_t)t * stride + gi * hd + h));
-    float L = 0.f;
-    for (int t = 0; t < used; ++t) {
-      const float e = expf(__ldcg(pb + (size_t)t * stride + gi * hd + h) - M);
-      w[t] = e;
-      L = fmaf(__ldcg(pb + (size_t)t * stride + gi * hd + gi + h), e, L);
-    }
-    for (int t = 0; t < used; ++t) w[t] = expf(__ldcg(pb + (size_t)t * stride + gi * hd + h) - M) / L;
-  }
-  __syncthreads();
-  bf16* ob = a.out + ((size_t)b * a.nq + head) * hd;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float o = 0.f;
-    for (int t0 = 0; t0 < used; t0 += 16) {
-      float v[16];
-#pragma unroll
-      for (int u = 0; u < 16; ++u)
-        v[u] = t0 + u < used ? __ldcg(pb + (size_t)(t0 + u) * stride + (size_t)h * hd + d) : 0.f;
-#pragma unroll
-      for (int u = 0; u < 16; ++u)
-        if (t0 + u < used) o = fmaf(v[u], w[t0 + u], o);
-    }
-    ob[d] = __float2bfloat16_rn(o);
-  }
-  pdl_launch_dependents();
-}
-
 }  // namespace jsx
 
 using namespace jsx;
@@ -132,20 +82,12 @@ extern "C" int jsx_attn_decode(const void* q, const void* k_cache, const void* v
   a.max_seq = max_seq; a.splits = splits; a.scale = scale;
   a.gi = lay.gi; a.hg = lay.hg;
   a.trace = nullptr;
+  a.no_merge = 0;
   a.cnt = (uint32_t*)((char*)workspace + 256);
   a.part = (float*)((char*)workspace + lay.counter_bytes);
-  // the last split merges its group from shared memory when the records fit there
-  // (attn_finish); otherwise a merge launch does it (k_attn_merge)
-  const size_t merge_need = (size_t)lay.splits * (lay.stride + lay.gi) * 4;
-  const size_t scratch_off = attn_use_mma(lay.gi, head_dim) ? (size_t)kMmaHeads * kRowPad * 2
-                                                             : (size_t)lay.gi * head_dim * 4 + (size_t)lay.gi * kChunk * 4;
-  a.no_merge = (scratch_off + merge_need > smem && lay.splits <= 1024) ? 1 : 0;
   auto kern = k_attn_decode;
   JSX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   JSX_CUDA(launch_kernel(kern, dim3(a.splits, B * nkv * lay.hg), dim3(kAttnThreads), smem,
                          (cudaStream_t)stream, a));
-  if (a.no_merge)
-    JSX_CUDA(launch_kernel(k_attn_merge, dim3(lay.gi, B * nkv * lay.hg), dim3(kAttnThreads), 0, (cudaStream_t)stream,
-                           a));
   return JSX_OK;
 }

