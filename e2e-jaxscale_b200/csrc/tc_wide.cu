@@ -133,6 +133,66 @@ __device__ __forceinline__ void pack8(const float (&f)[8], uint4& u) {
 }
 
 // One epilogue warp's quarter (32 rows x 256 tokens) of a tile in the
+// single-rank row-parallel product (h += bf16(partial)): per 32-token chunk the
+// bf16-rounded partials are transposed through shared memory into
+// [token][32 rows], so the residual is read and written with 16-byte accesses
+// (4 per lane and chunk instead of 16 four-byte ones: the load/store issue rate,
+// not the tensor cores, bounded this epilogue at small K), the next chunk's
+// residual loaded ahead of this chunk's stores.  Same arithmetic as wide_pair:
+// h + bf16(v) in fp32, rounded once.
+__device__ __forceinline__ void wide_rowar_tile(const WideArgs& t, const GemvArgs& a, int ft, int tt, int q, int lane,
+                                                uint32_t tacc, uint64_t* acc_empty, bf16* stg) {
+  const int r0 = ft * kWBM + 32 * q;
+  uint4 hv[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int e = lane + 32 * k;
+    const int m = tt * kWBN + (e >> 2), row = r0 + 8 * (e & 3);
+    hv[k] = (m < t.M && row < t.N) ? *reinterpret_cast<const uint4*>(a.h + (size_t)m * t.N + row)
+                                   : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll 1
+  for (int ch = 0; ch < kWBN / 32; ++ch) {
+    float v[32];
+    tc_ld32(tacc + 32 * ch, v);
+    if (ch == kWBN / 32 - 1) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc_arrive(acc_empty);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = __float2bfloat16_rn(v[j]);
+    __syncwarp();
+    uint4 hn[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = lane + 32 * k;
+      const int m = tt * kWBN + 32 * (ch + 1) + (e >> 2), row = r0 + 8 * (e & 3);
+      hn[k] = (ch + 1 < kWBN / 32 && m < t.M && row < t.N)
+                  ? *reinterpret_cast<const uint4*>(a.h + (size_t)m * t.N + row)
+                  : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = lane + 32 * k;
+      const int m = tt * kWBN + 32 * ch + (e >> 2), row = r0 + 8 * (e & 3);
+      if (m >= t.M || row >= t.N) continue;
+      float hf[8], pf[8];
+      unpack8(hv[k], hf);
+      unpack8(*reinterpret_cast<const uint4*>(stg + (e >> 2) * 32 + 8 * (e & 3)), pf);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) hf[i] += pf[i];
+      uint4 o;
+      pack8(hf, o);
+      *reinterpret_cast<uint4*>(a.h + (size_t)m * t.N + row) = o;
+    }
+    __syncwarp();  // the staging buffer is refilled by the next chunk
+#pragma unroll
+    for (int k = 0; k < 4; ++k) hv[k] = hn[k];
+  }
+}
+
+// One epilogue warp's quarter (32 rows x 256 tokens) of a tile in the
 // row-parallel product across ranks.  Per 32-token chunk the accumulator is
 // rounded to bf16 (this rank's partial, the reference's per-rank result) and
 // transposed through shared memory into [token][32 rows], so that every
@@ -412,6 +472,11 @@ __global__ void __launch_bounds__(kWThreads, 1) k_wide_gemm(const __grid_constan
       if (xchg) {
         wide_exchange_tile(c, t, a, tile, ft, tt, q, lane, epoch, tmem + ((uint32_t)(32 * q) << 16) + b * kWBN,
                            acce + b, stg + (warp - 2) * (32 * 32));
+        continue;
+      }
+      if (EPI == EPI_ROWAR && a.addend == nullptr && (t.N & 7) == 0) {
+        wide_rowar_tile(t, a, ft, tt, q, lane, tmem + ((uint32_t)(32 * q) << 16) + b * kWBN, acce + b,
+                        stg + (warp - 2) * (32 * 32));
         continue;
       }
       // row-parallel: this lane's residual pairs of 16 tokens per 32-token chunk, loaded one
