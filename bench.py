@@ -541,16 +541,27 @@ def run_gpu(args) -> None:
             nl = c.num_hidden_layers
             tr = torch.zeros(2 + 13 * nl, dtype=torch.int64, device=dev)
             tar = torch.zeros(4 * nl, dtype=torch.int64, device=dev)
+            tph = torch.zeros(15 * nl, dtype=torch.int64, device=dev)
             st.step_args.trace = tr.data_ptr()
             st.step_args.trace_ar = tar.data_ptr()
-            acc, sub, exp_ = None, None, None
-            for _ in range(8):
+            acc, sub, exp_, pts = None, None, None, None
+            for i in range(12):
+                # steps 8-11 add the per-phase points (a block synchronisation each) and
+                # feed only the points
                 tar.zero_()
+                tph.zero_()
+                st.step_args.trace_phase = tph.data_ptr() if i >= 8 else None
                 model.step(st, head=True)
+                t = tr.cpu().numpy().astype(np.float64)
+                if i >= 8:
+                    # latest CTA at each point of each phase, from the phase's start
+                    pstart = t[:5 * nl].reshape(nl, 5)
+                    pp = (tph.cpu().numpy().astype(np.float64).reshape(nl, 5, 3) - pstart[:, :, None]) / 1e3
+                    pts = pp if pts is None else pts + pp
+                    continue
                 ta = tar.cpu().numpy().astype(np.float64).reshape(nl, 2, 2)
                 e_ = (ta[:, :, 1] - ta[:, :, 0]) / 1e3  # [layer][o_proj, down]
                 exp_ = e_ if exp_ is None else exp_ + e_
-                t = tr.cpu().numpy().astype(np.float64)
                 d = np.diff(t[:2 + 5 * nl]) / 1e3
                 acc = d if acc is None else acc + d
                 # attention of head group 0, relative to the start of the attention phase
@@ -559,9 +570,11 @@ def run_gpu(args) -> None:
                 sub = s5 if sub is None else sub + s5
             st.step_args.trace = None
             st.step_args.trace_ar = None
+            st.step_args.trace_phase = None
             acc /= 8
             sub /= 8
             exp_ /= 8
+            pts /= 4
             exposed = {"per_layer_us": max_over_ranks(float(exp_.sum(axis=1).mean())),
                        "o_proj_us": max_over_ranks(float(exp_[:, 0].mean())),
                        "down_us": max_over_ranks(float(exp_[:, 1].mean())),
@@ -574,6 +587,9 @@ def run_gpu(args) -> None:
             names = ["qkv", "attention", "o_proj_allreduce", "gate_up", "down_allreduce"]
             phase_us = {n: float(per[:, i].mean()) for i, n in enumerate(names)}
             phase_us["lm_head"] = float(acc[5 * nl])
+            # from 4 further steps (the points' block synchronisations stay out of the times above)
+            phase_us["points_us"] = {n: [round(float(pts[:, i, k].mean()), 2) for k in range(3)]
+                                     for i, n in enumerate(names)}
             # stamps an item never writes (the split merge runs in the o_proj staging when the
             # records are small) stay zero and are left out
             phase_us["attention_group0_us"] = {k: float(sub[:, i].mean()) for i, k in enumerate(
@@ -581,7 +597,10 @@ def run_gpu(args) -> None:
                  "split0_counted", "merge_done", "merge_start"]) if np.all(t[2 + 5 * nl:].reshape(nl, 8)[:, i] > 0)}
             phase_us["note"] = ("mean us per layer (lm_head: once per step) between grid barriers, each "
                                 "phase including its barrier; CTA 0 %globaltimer over 8 eager steps; "
-                                "attention_group0_us: head group 0 from the start of the attention phase")
+                                "attention_group0_us: head group 0 from the start of the attention phase; "
+                                "points_us: per phase, from its start, the latest CTA to have staged its "
+                                "input, finished its product (row-parallel: pushed its partials) and "
+                                "finished the phase; 4 more traced steps")
         else:
             # the tensor-core chain: the step is one CUDA graph of its launches; its algorithmic
             # bytes over its time

@@ -422,6 +422,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
 
   for (int l = 0; l < a.n_layers; ++l) {
     const jsx_layer_weights L = layers[l];
+    uint64_t* tp = a.trace_phase ? a.trace_phase + 15 * l : nullptr;  // [phase][point]
+#define JSX_TP(ph, pt) trace_max(tp ? tp + 3 * (ph) + (pt) : nullptr)
     // ---- q/k/v + bias + RoPE + KV write (models/glm4.py:118-120) ----
     {
       GemvArgs ga = {};
@@ -437,8 +439,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.nq = a.n_heads; ga.nkv = a.n_kv_heads; ga.hd = a.head_dim; ga.rot = a.rotary_dim;
       ga.max_seq = a.max_seq; ga.tps = 1;
       stage_x<M, false, true>(ga, xs);
+      JSX_TP(0, 0);
       gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best);
+      JSX_TP(0, 1);
       l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden, 0u, a.l2_next_bytes);
+      JSX_TP(0, 2);
     }
     at.trace = a.trace ? a.trace + (2 + 5 * a.n_layers) + 8 * l : nullptr;
     at.kc = reinterpret_cast<const bf16*>(L.k_cache);
@@ -453,12 +458,15 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     // ---- attention over cache rows [0, pos] (layers/attention.py:148-153) ----
     // HBM is idle while the attention's short dependency chain runs: gate/up rows go to L2
     l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter, 0u, a.l2_attn_bytes);
+    JSX_TP(1, 0);
     for (int it = blockIdx.x; it < attn_items; it += gridDim.x) {
       if (attn_pre && it == (int)blockIdx.x)
         attn_item_mma<kThreads, true, true, true>(at, it % at.splits, it / at.splits, smem_raw, pre_cur);
       else
         attn_item_any<kThreads, true, true>(at, it % at.splits, it / at.splits, smem_raw);
     }
+    JSX_TP(1, 1);
+    JSX_TP(1, 2);
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden);
     grid_wait(bar, gen);
@@ -473,13 +481,16 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       const uint32_t ep = epoch0 + 2u * l;
       if (cmerge) stage_attn_merge<M>(at, xs, cmerge_w);
       else stage_x<M, false, true>(ga, xs);
+      JSX_TP(2, 0);
       gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
       uint64_t* ar = a.trace_ar ? a.trace_ar + 4 * l : nullptr;
       trace_max(ar);
+      JSX_TP(2, 1);
       l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter, a.l2_attn_bytes,
                          a.l2_next_bytes);
       if (multi) allreduce_rows<M>(ga, c, ep);
       trace_max(ar ? ar + 1 : nullptr);
+      JSX_TP(2, 2);
     }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_gu), a.hidden, 2 * a.inter);
@@ -495,8 +506,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.M = M; ga.K = a.hidden; ga.N = 2 * a.inter;
       ga.y = reinterpret_cast<bf16*>(a.act);
       stage_x<M, false, true>(ga, xs);
+      JSX_TP(3, 0);
       gemv_phase<M, EPI_SWIGLU>(ga, c, multi, 0u, xs, bt, best);
+      JSX_TP(3, 1);
       l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden, 0u, a.l2_next_bytes);
+      JSX_TP(3, 2);
     }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden);
@@ -511,9 +525,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.h = reinterpret_cast<bf16*>(a.h);
       const uint32_t ep = epoch0 + 2u * l + 1u;
       stage_x<M, false, true>(ga, xs);
+      JSX_TP(4, 0);
       gemv_phase<M, EPI_ROWAR>(ga, c, multi, ep, xs, bt, best);
       uint64_t* ar = a.trace_ar ? a.trace_ar + 4 * l + 2 : nullptr;
       trace_max(ar);
+      JSX_TP(4, 1);
       if (l + 1 < a.n_layers)
         l2_prefetch_groups(reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows, 0u,
                            a.l2_next_bytes);
@@ -522,7 +538,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
                            a.l2_next_bytes);
       if (multi) allreduce_rows<M>(ga, c, ep);
       trace_max(ar ? ar + 1 : nullptr);
+      JSX_TP(4, 2);
     }
+#undef JSX_TP
     grid_arrive(bar, gen);
     if (l + 1 < a.n_layers)
       prefetch(bt, reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows);
@@ -626,15 +644,18 @@ static size_t step_smem(const jsx_decode_step_args& a) {
 }
 
 // Whether the o_proj staging merges the attention splits (stage_attn_merge):
-// JSX_STEP_CMERGE=0/1 forces it; by default when every group's records together
-// are at most kMergeRecordBytes.
+// only when JSX_STEP_CMERGE=1 and every group's records together fit
+// kMergeWeights weights and kMergeRecordBytes bytes.  Off by default: at GLM-4
+// shapes, tensor parallelism 4, context 1024 it takes the attention phase from
+// 7.9 to 4.1 us but o_proj from 8.8 to 15.8 us (every o_proj CTA reads all
+// 66 KB of records), 536 -> 495 tokens/s.
 static int consumer_merge(const jsx_decode_step_args& a) {
   const AttnLayout lay = attn_layout(a.batch, a.n_heads, a.n_kv_heads, a.head_dim, a.max_seq);
   const size_t groups = (size_t)a.batch * a.n_kv_heads * lay.hg;
-  const bool fits = groups * lay.splits * lay.gi <= (size_t)kMergeWeights;
+  const bool fits = groups * lay.splits * lay.gi <= (size_t)kMergeWeights &&
+                    groups * lay.splits * lay.stride * sizeof(float) <= kMergeRecordBytes;
   const char* env = getenv("JSX_STEP_CMERGE");
-  if (env != nullptr) return (atoi(env) != 0 && fits) ? 1 : 0;
-  return (fits && groups * lay.splits * lay.stride * sizeof(float) <= kMergeRecordBytes) ? 1 : 0;
+  return (env != nullptr && atoi(env) != 0 && fits) ? 1 : 0;
 }
 
 static size_t step_workspace(const jsx_decode_step_args& a) {

@@ -520,7 +520,7 @@ class StepArgs(ctypes.Structure):
                 + [(n, ctypes.c_void_p) for n in ("h", "q", "attn", "act", "logits", "workspace")]
                 + [("workspace_bytes", ctypes.c_size_t), ("trace", ctypes.c_void_p),
                    ("trace_ar", ctypes.c_void_p), ("l2_next_bytes", ctypes.c_uint32),
-                   ("l2_attn_bytes", ctypes.c_uint32)])
+                   ("l2_attn_bytes", ctypes.c_uint32), ("trace_phase", ctypes.c_void_p)])
 
 
 def layer_table(layers, caches, device) -> torch.Tensor:

@@ -334,6 +334,12 @@ typedef struct {
                                       of the current one; 0 = none */
   uint32_t l2_attn_bytes;          /* per warp: bytes of its first gate/up row pairs requested into
                                       L2 while the attention runs; 0 = none */
+  uint64_t* trace_phase;           /* NULL, or [n_layers][5][3] u64, zero before the call: for each
+                                      phase (qkv, attention, o_proj, gate/up, down) the latest
+                                      %globaltimer over CTAs at which a CTA had (0) staged its input
+                                      (attention: begun its items), (1) finished its product and
+                                      epilogue (row-parallel: pushed its partials), (2) finished the
+                                      phase before its barrier arrival */
 } jsx_decode_step_args;
 
 int jsx_decode_step_workspace_size(const jsx_decode_step_args* args, size_t* bytes);

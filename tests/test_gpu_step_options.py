@@ -1,7 +1,7 @@
 """Options of the whole-step decode kernel that change how it moves data, not
 what it computes: the attention's split merge done by the o_proj staging
 (JSX_STEP_CMERGE), the L2 prefetch of the next projection's rows
-(l2_next_bytes / l2_attn_bytes) and the exchange trace (trace_ar).  Each must
+(l2_next_bytes / l2_attn_bytes) and the traces (trace_ar, trace_phase).  Each must
 give bit-identical logits and ids to the default kernel on the same inputs.
 The options are read per launch, so one process compares them."""
 
@@ -46,11 +46,13 @@ def test_step_options_bit_identical(jsx, cuda, glm_2layer, B):
     L = 80
     base = _run(jsx, model, prompt, 6, L)
     tar = torch.zeros(4 * nl, dtype=torch.int64, device=cuda)
+    tph = torch.zeros(15 * nl, dtype=torch.int64, device=cuda)
 
     def with_l2_and_trace(st):
         st.step_args.l2_next_bytes = 16384
         st.step_args.l2_attn_bytes = 16384
         st.step_args.trace_ar = tar.data_ptr()
+        st.step_args.trace_phase = tph.data_ptr()
 
     variants = [("JSX_STEP_CMERGE", "1", None), (None, None, with_l2_and_trace)]
     for env, val, setup in variants:
@@ -67,3 +69,7 @@ def test_step_options_bit_identical(jsx, cuda, glm_2layer, B):
     # the exchange stamps were written (one rank: the exchange part is empty, so both
     # stamps of a phase come from the same barrier-free point)
     assert int(tar.cpu().numpy().min()) > 0
+    # every phase point of every layer was stamped, in order within each phase
+    pts = tph.cpu().numpy().reshape(nl, 5, 3)
+    assert int(pts.min()) > 0
+    assert np.all(np.diff(pts, axis=2) >= 0)
