@@ -671,7 +671,8 @@ def run_gpu(args) -> None:
         # last and compact, so they stay in view at the end of the line
         if r["phase_us"] is not None:
             line["phase_us"] = {k: (round(v, 2) if isinstance(v, float) else
-                                    {kk: round(vv, 2) for kk, vv in v.items()} if isinstance(v, dict) else v)
+                                    {kk: (round(vv, 2) if isinstance(vv, float) else vv) for kk, vv in v.items()}
+                                    if isinstance(v, dict) else v)
                                 for k, v in r["phase_us"].items() if k != "note"}
         if r["exposed"] is not None:
             line["exposed_comm_us"] = {k: round(v, 2) for k, v in r["exposed"].items() if k != "definition"}
