@@ -132,6 +132,17 @@ __device__ __forceinline__ void l2_prefetch_groups(const bf16* w, int K, int N, 
   }
 }
 
+// L2 prefetch of a small vector that a later phase reads once per step (norm
+// weights, the q/k/v bias): one bulk request from thread 0 of CTA `cta`, so the
+// later phase's first read of it is an L2 hit rather than an HBM round trip on
+// its critical path.  Skipped for a pointer that is not 16-byte aligned.
+__device__ __forceinline__ void l2_prefetch_vec(const void* p, uint32_t bytes, int cta) {
+  if (p == nullptr || bytes < 16u || (reinterpret_cast<uintptr_t>(p) & 15u) != 0 || (int)blockIdx.x != cta ||
+      threadIdx.x != 0)
+    return;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes & ~15u) : "memory");
+}
+
 // Latest %globaltimer of any CTA at this point (trace of the exchange phases).
 __device__ __forceinline__ void trace_max(uint64_t* slot) {
   if (slot == nullptr) return;
@@ -397,6 +408,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   for (int m = 0; m < M; ++m) best[m] = 0ull;
   grid_arrive(bar, gen);
   prefetch(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows);
+  l2_prefetch_vec(layers[0].ln1, 2u * a.hidden, 0);
+  l2_prefetch_vec(layers[0].b_qkv, 2u * qkv_rows, 1);
   grid_wait(bar, gen);
   trace_mark(a.trace, tn);
 
@@ -469,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     JSX_TP(1, 2);
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden);
+    l2_prefetch_vec(L.ln2, 2u * a.hidden, (int)gridDim.x - 1);
     grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- o_proj + all-reduce + residual (layers/attention.py:159, models/glm4.py:124) ----
@@ -514,6 +528,12 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     }
     grid_arrive(bar, gen);
     prefetch(bt, reinterpret_cast<const bf16*>(L.w_d), a.inter, a.hidden);
+    if (l + 1 < a.n_layers) {
+      l2_prefetch_vec(layers[l + 1].ln1, 2u * a.hidden, (int)gridDim.x - 1);
+      l2_prefetch_vec(layers[l + 1].b_qkv, 2u * qkv_rows, (int)gridDim.x - 2);
+    } else if (a.head) {
+      l2_prefetch_vec(a.final_norm, 2u * a.hidden, (int)gridDim.x - 1);
+    }
     grid_wait(bar, gen);
   trace_mark(a.trace, tn);
     // ---- down_proj + all-reduce + residual (models/glm4.py:49, :130) ----

@@ -80,9 +80,11 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
   if constexpr (M <= 2) {
     // one pass: every vector a thread needs (at most 2 per token, K <= 16 * NT)
     // is held in registers between the sum of squares and the scaling; same
-    // summation order and arithmetic as the two-pass form below
+    // summation order and arithmetic as the two-pass form below.  The weights
+    // are loaded with the activations, so their latency (HBM, for a norm read
+    // once per step) overlaps the reduction instead of following it.
     if (nvec <= 2 * NT) {
-      uint4 xr[M][2];
+      uint4 xr[M][2], gr[2];
       float ss[M];
 #pragma unroll
       for (int jj = 0; jj < 2; ++jj) {
@@ -90,6 +92,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
 #pragma unroll
         for (int m = 0; m < M; ++m)
           xr[m][jj] = v < nvec ? ld_act(xv + m * nvec + v, kCoherent) : make_uint4(0, 0, 0, 0);
+        gr[jj] = v < nvec ? gv[v] : make_uint4(0, 0, 0, 0);
       }
 #pragma unroll
       for (int m = 0; m < M; ++m) ss[m] = 0.f;
@@ -123,7 +126,7 @@ __device__ __forceinline__ void stage_x(const GemvArgs& a, bf16* xs) {
         const int v = threadIdx.x + jj * NT;
         if (v < nvec) {
           float g[8];
-          unpack8(gv[v], g);
+          unpack8(gr[jj], g);
 #pragma unroll
           for (int m = 0; m < M; ++m) {
             float f[8];
