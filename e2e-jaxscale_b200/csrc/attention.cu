@@ -83,6 +83,7 @@ extern "C" int jsx_attn_decode(const void* q, const void* k_cache, const void* v
   a.gi = lay.gi; a.hg = lay.hg;
   a.trace = nullptr;
   a.no_merge = 0;
+  a.dist_err = nullptr;  // splits of a group may not be co-resident: the last one merges
   a.cnt = (uint32_t*)((char*)workspace + 256);
   a.part = (float*)((char*)workspace + lay.counter_bytes);
   auto kern = k_attn_decode;

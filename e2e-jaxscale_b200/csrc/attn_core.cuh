@@ -33,7 +33,13 @@ struct AttnArgs {
                    // the group's merge start (its last split counted)
   int no_merge;    // items only write their split records; the consumer merges them
                    // (whole-step kernel, small groups: the o_proj staging)
+  uint32_t* dist_err;  // null, or the distributed merge (every split item merges a share
+                       // of the group's heads once all have counted; needs every item of
+                       // the launch on its own co-resident CTA) and its error word, set
+                       // when the wait for the other splits gives up
 };
+
+constexpr long long kMergeWaitCycles = 4000000000ll;  // ~2 s at the 1965 MHz max clock
 
 __device__ __forceinline__ void attn_stamp(const AttnArgs& a, int vb, int s, int k) {
   if (a.trace != nullptr && vb == 0 && (s == 0 || k >= 6) && threadIdx.x == 0) a.trace[k] = globaltimer();
@@ -112,6 +118,95 @@ __device__ __forceinline__ uint32_t dyn_smem_bytes() {
   return r;
 }
 
+// Distributed completion (a.dist_err): every split item of group vb counts
+// itself, waits (bounded) until all have, then merges heads s, s + splits, ...
+// of the group, with the arithmetic of the shared-memory merge in attn_finish
+// (per head: warp max of m, warp sum of l * exp(m - M), weights exp(m - M) / L;
+// per output pair a sequential FMA over the splits).  While warp 0 forms a
+// head's weights, the other warps have that head's accumulators of the first
+// kSeg splits in flight to shared memory (cp.async), so the merge costs one L2
+// round trip after the wait, on every split CTA at once instead of all heads on
+// the last one.  The counter rises to splits (arrivals), then to 2 splits
+// (merges done); the last merge leaves it zero for the next use, which follows
+// a grid barrier.  Needs the tensor-core item's shared memory past `scratch`
+// (>= 41 KB): (splits + 3) / 4 * 16 + kSeg * hd * 4 bytes.
+__device__ __forceinline__ uint32_t attn_ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int kSeg = 16;  // splits of one head staged at a time by the distributed merge
+
+template <int NT>
+__device__ __forceinline__ void attn_finish_distributed(const AttnArgs& a, int vb, int s, int b, int head0,
+                                                        int cur, float* scratch) {
+  const int gi = a.gi, hd = a.hd, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int stride = split_stride(gi, hd);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    atomicAdd(a.cnt + vb, 1u);
+    const long long t0 = clock64();
+    uint32_t it = 0;
+    while (attn_ld_acquire(a.cnt + vb) < (uint32_t)a.splits) {
+      if ((++it & 63u) == 0 && clock64() - t0 > kMergeWaitCycles) {
+        atomicOr(a.dist_err, 2u);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  attn_stamp(a, vb, s, 5);
+  attn_stamp(a, vb, s, 7);
+  const int used = (cur + kChunk) / kChunk;
+  const float* pb = a.part + (size_t)vb * a.splits * stride;
+  bf16* ob = a.out + ((size_t)b * a.nq + head0) * hd;
+  float* w = scratch;                        // [used] weights of the head being merged
+  float* os = scratch + ((used + 3) & ~3);   // [kSeg][hd] its accumulators, kSeg splits at a time
+  const int d2 = tid - 32, nd2 = hd >> 1, n16 = hd >> 2;
+  for (int h = s; h < gi; h += a.splits) {
+    float2 o = make_float2(0.f, 0.f);
+    for (int t0 = 0; t0 < used; t0 += kSeg) {
+      const int nt = used - t0 < kSeg ? used - t0 : kSeg;
+      if (tid >= 32) {
+        for (int i = tid - 32; i < nt * n16; i += NT - 32) {
+          const int t = i / n16, c = i - t * n16;
+          cp_async16(os + t * hd + 4 * c, pb + (size_t)(t0 + t) * stride + h * hd + 4 * c, 16u);
+        }
+      }
+      if (t0 == 0 && warp == 0) {
+        float M = -INFINITY;
+        for (int t = lane; t < used; t += 32) M = fmaxf(M, __ldcg(pb + (size_t)t * stride + gi * hd + h));
+        M = warp_max(M);
+        float L = 0.f;
+        for (int t = lane; t < used; t += 32) {
+          const float e = expf(__ldcg(pb + (size_t)t * stride + gi * hd + h) - M);
+          w[t] = e;
+          L = fmaf(__ldcg(pb + (size_t)t * stride + gi * hd + gi + h), e, L);
+        }
+        L = warp_sum(L);
+        for (int t = lane; t < used; t += 32) w[t] = w[t] / L;
+      }
+      cp_async_wait_all();
+      __syncthreads();
+      if (d2 >= 0 && d2 < nd2) {
+        const float2* o2 = reinterpret_cast<const float2*>(os) + d2;
+        for (int t = 0; t < nt; ++t) {
+          const float wt = w[t0 + t];
+          const float2 v = o2[t * nd2];
+          o.x = fmaf(v.x, wt, o.x);
+          o.y = fmaf(v.y, wt, o.y);
+        }
+      }
+      __syncthreads();  // os (and, after the last segment, w) are reused
+    }
+    if (d2 >= 0 && d2 < nd2) *reinterpret_cast<uint32_t*>(ob + h * hd + 2 * d2) = pack2(o.x, o.y);
+  }
+  attn_stamp(a, vb, 0, 6);
+  if (tid == 0 && atomicAdd(a.cnt + vb, 1u) == 2u * (uint32_t)a.splits - 1u) a.cnt[vb] = 0u;
+}
+
 // Completion of one item: the item that completes the set of splits of group
 // vb merges them (flash-decoding combine).  Weights w_t[h] = exp(m_t - M) / L
 // are formed once in shared memory (`scratch`, free once the item's own work is
@@ -131,6 +226,10 @@ __device__ __forceinline__ void attn_finish(const AttnArgs& a, int vb, int s, in
   // the merges remain), not earlier: its CTAs would take SMs from later items
   pdl_launch_dependents();
   if (a.no_merge) return;  // the records are merged by their consumer after a grid barrier
+  if (a.dist_err != nullptr) {
+    attn_finish_distributed<NT>(a, vb, s, b, head0, cur, scratch);
+    return;
+  }
   __threadfence();
   __syncthreads();
   if (tid == 0) is_last = atomicAdd(a.cnt + vb, 1u) == (uint32_t)(a.splits - 1);

@@ -363,8 +363,13 @@ __device__ __forceinline__ void stage_attn_merge(const AttnArgs& at, bf16* xs, f
   __syncthreads();
 }
 
+// opts: kOptConsumerMerge, kOptLastMerge (host-selected variants; same results)
+constexpr int kOptConsumerMerge = 1;  // the o_proj staging merges the attention splits
+constexpr int kOptLastMerge = 2;      // the last split of a group merges it (not every split)
+
 template <int M>
-__global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_args a, CommDev c, int cmerge) {
+__global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_args a, CommDev c, int opts) {
+  const int cmerge = opts & kOptConsumerMerge;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   __shared__ float cmerge_w[kMergeWeights];
   bf16* xs = reinterpret_cast<bf16*>(smem_raw);
@@ -431,6 +436,13 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   at.cnt = reinterpret_cast<uint32_t*>(ws + kWsAttn + 256);
   at.part = reinterpret_cast<float*>(ws + kWsAttn + lay.counter_bytes);
   const int attn_items = M * a.n_kv_heads * lay.hg * lay.splits;
+  // distributed split merge: every item on its own CTA (all co-resident: the
+  // split CTAs of a group wait for one another), the tensor-core item (its
+  // shared memory holds the merge's weights and kSeg staged accumulators)
+  at.dist_err = (!cmerge && !(opts & kOptLastMerge) && attn_items <= (int)gridDim.x &&
+                 attn_use_mma(lay.gi, a.head_dim) && lay.splits <= 4096)
+                    ? &g_step_error
+                    : nullptr;
   const bool attn_pre = attn_use_mma(lay.gi, a.head_dim) && (int)blockIdx.x < attn_items;
 
   for (int l = 0; l < a.n_layers; ++l) {
@@ -739,7 +751,10 @@ extern "C" int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args,
   }
   const size_t smem = step_smem(a);
   JSX_REQUIRE(smem <= kMaxDynSmem, "step needs %zu bytes of shared memory", smem);
-  const int cmerge = consumer_merge(a);
+  // JSX_STEP_DMERGE=0: the attention's last split merges its group (the
+  // per-op kernel's form) instead of every split merging a share
+  const char* dm = getenv("JSX_STEP_DMERGE");
+  const int opts = (consumer_merge(a) ? kOptConsumerMerge : 0) | ((dm && atoi(dm) == 0) ? kOptLastMerge : 0);
 #define JSX_STEP_CASE(MM)                                                                    \
   case MM: {                                                                                 \
     auto kern = k_decode_step<MM>;                                                           \
@@ -761,7 +776,7 @@ extern "C" int jsx_decode_step(jsx_comm* comm, const jsx_decode_step_args* args,
     attr[0].val.cooperative = 1;                                                             \
     cfg.attrs = attr;                                                                        \
     cfg.numAttrs = 1;                                                                        \
-    JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, a, c, cmerge));                                  \
+    JSX_CUDA(cudaLaunchKernelEx(&cfg, kern, a, c, opts));                                    \
     return JSX_OK;                                                                           \
   }
   switch (a.batch) {
