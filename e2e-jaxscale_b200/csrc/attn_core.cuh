@@ -129,7 +129,7 @@ __device__ __forceinline__ uint32_t dyn_smem_bytes() {
 // the last one.  The counter rises to splits (arrivals), then to 2 splits
 // (merges done); the last merge leaves it zero for the next use, which follows
 // a grid barrier.  Needs the tensor-core item's shared memory past `scratch`
-// (>= 41 KB): (splits + 3) / 4 * 16 + kSeg * hd * 4 bytes.
+// (>= 41 KB): (splits + 3) / 4 * 16 + kSeg * hd * 4 + splits * 4 bytes.
 __device__ __forceinline__ uint32_t attn_ld_acquire(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -145,8 +145,7 @@ __device__ __forceinline__ void attn_finish_distributed(const AttnArgs& a, int v
   const int stride = split_stride(gi, hd);
   __threadfence();
   __syncthreads();
-  if (tid == 0) {
-    atomicAdd(a.cnt + vb, 1u);
+  if (tid == 0 && atomicAdd(a.cnt + vb, 1u) != (uint32_t)a.splits - 1u) {  // the last arrival does not wait
     const long long t0 = clock64();
     uint32_t it = 0;
     while (attn_ld_acquire(a.cnt + vb) < (uint32_t)a.splits) {
@@ -156,14 +155,16 @@ __device__ __forceinline__ void attn_finish_distributed(const AttnArgs& a, int v
       }
     }
   }
+  if (tid == 0) __threadfence();  // the other splits' records are read after this point
   __syncthreads();
   attn_stamp(a, vb, s, 5);
   attn_stamp(a, vb, s, 7);
   const int used = (cur + kChunk) / kChunk;
   const float* pb = a.part + (size_t)vb * a.splits * stride;
   bf16* ob = a.out + ((size_t)b * a.nq + head0) * hd;
-  float* w = scratch;                        // [used] weights of the head being merged
+  float* w = scratch;                        // [used] m, then the weights of the head being merged
   float* os = scratch + ((used + 3) & ~3);   // [kSeg][hd] its accumulators, kSeg splits at a time
+  float* lw = os + kSeg * hd;                // [used] l
   const int d2 = tid - 32, nd2 = hd >> 1, n16 = hd >> 2;
   for (int h = s; h < gi; h += a.splits) {
     float2 o = make_float2(0.f, 0.f);
@@ -176,14 +177,20 @@ __device__ __forceinline__ void attn_finish_distributed(const AttnArgs& a, int v
         }
       }
       if (t0 == 0 && warp == 0) {
+        // m and l of every split in one round trip, then as in the shared-memory merge
         float M = -INFINITY;
-        for (int t = lane; t < used; t += 32) M = fmaxf(M, __ldcg(pb + (size_t)t * stride + gi * hd + h));
+        for (int t = lane; t < used; t += 32) {
+          const float m = __ldcg(pb + (size_t)t * stride + gi * hd + h);
+          lw[t] = __ldcg(pb + (size_t)t * stride + gi * hd + gi + h);
+          w[t] = m;
+          M = fmaxf(M, m);
+        }
         M = warp_max(M);
         float L = 0.f;
         for (int t = lane; t < used; t += 32) {
-          const float e = expf(__ldcg(pb + (size_t)t * stride + gi * hd + h) - M);
+          const float e = expf(w[t] - M);
           w[t] = e;
-          L = fmaf(__ldcg(pb + (size_t)t * stride + gi * hd + gi + h), e, L);
+          L = fmaf(lw[t], e, L);
         }
         L = warp_sum(L);
         for (int t = lane; t < used; t += 32) w[t] = w[t] / L;

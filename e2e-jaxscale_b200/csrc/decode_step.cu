@@ -112,6 +112,61 @@ __device__ __forceinline__ void prefetch(Batch& bt, const bf16* w, int K, int N)
   if (g < N / kRows) load_batch(bt, reinterpret_cast<const uint4*>(w) + (size_t)g * kRows * nvec, nvec, 0, lane);
 }
 
+// The q/k/v projection with K split over warp pairs: when the row pairs are few
+// (tensor parallelism >= 2) and K spans two weight batches (2048 < K <= 4096),
+// warps 2j and 2j + 1 of CTA c take the two K halves of row pair c + j * grid,
+// so every weight byte of the phase is in registers (prefetch_qkv_split) before
+// the phase starts.  The halves are warp-reduced separately and added (first +
+// second) before the epilogue.
+__device__ __forceinline__ bool qkv_split_ok(int K, int N) {
+  const int nvec = K >> 3, batch = 32 * kUnroll;
+  return nvec > batch && nvec <= 2 * batch && N / kRows <= (kWarps / 2) * (int)gridDim.x;
+}
+
+__device__ __forceinline__ void prefetch_qkv_split(Batch& bt, const bf16* w, int K, int N) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = blockIdx.x + gridDim.x * (warp >> 1);
+  const int nvec = K >> 3;
+  if (g < N / kRows)
+    load_batch(bt, reinterpret_cast<const uint4*>(w) + (size_t)g * kRows * nvec, nvec, (warp & 1) * 32 * kUnroll,
+               lane);
+}
+
+template <int M>
+__device__ __forceinline__ void gemv_qkv_split(const GemvArgs& ga, const bf16* xs, const Batch& bt) {
+  __shared__ float half2[kWarps / 2][kRows][M];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = blockIdx.x + gridDim.x * (warp >> 1);
+  const int nvec = ga.K >> 3;
+  const bool mine = g < ga.N / kRows;
+  float acc[kRows][M];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r)
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[r][m] = 0.f;
+  if (mine) {
+    fma_batch<M>(bt, reinterpret_cast<const uint4*>(xs), nvec, (warp & 1) * 32 * kUnroll, lane, acc);
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] = warp_sum(acc[r][m]);
+    if ((warp & 1) && lane == 0) {
+#pragma unroll
+      for (int r = 0; r < kRows; ++r)
+#pragma unroll
+        for (int m = 0; m < M; ++m) half2[warp >> 1][r][m] = acc[r][m];
+    }
+  }
+  __syncthreads();
+  if (mine && !(warp & 1)) {
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m) acc[r][m] += half2[warp >> 1][r][m];
+    epi_qkv<M>(ga, g, acc, lane);
+  }
+}
+
 // L2 prefetch of this warp's first row pairs of a later GEMV phase: bytes
 // [from, to) of the concatenation of the groups gemv_phase will hand it
 // (g = block + grid * warp + k * grid * warps); from and to are multiples of 16.
@@ -411,8 +466,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   unsigned long long best[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) best[m] = 0ull;
+  const bool qkv_split = qkv_split_ok(a.hidden, qkv_rows);
   grid_arrive(bar, gen);
-  prefetch(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows);
+  if (qkv_split) prefetch_qkv_split(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows);
+  else prefetch(bt, reinterpret_cast<const bf16*>(layers[0].w_qkv), a.hidden, qkv_rows);
   l2_prefetch_vec(layers[0].ln1, 2u * a.hidden, 0);
   l2_prefetch_vec(layers[0].b_qkv, 2u * qkv_rows, 1);
   grid_wait(bar, gen);
@@ -465,7 +522,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
       ga.max_seq = a.max_seq; ga.tps = 1;
       stage_x<M, false, true>(ga, xs);
       JSX_TP(0, 0);
-      gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best);
+      if (qkv_split) gemv_qkv_split<M>(ga, xs, bt);
+      else gemv_phase<M, EPI_QKV>(ga, c, multi, 0u, xs, bt, best);
       JSX_TP(0, 1);
       l2_prefetch_groups(reinterpret_cast<const bf16*>(L.w_o), qdim, a.hidden, 0u, a.l2_next_bytes);
       JSX_TP(0, 2);
@@ -574,7 +632,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
     }
 #undef JSX_TP
     grid_arrive(bar, gen);
-    if (l + 1 < a.n_layers)
+    if (l + 1 < a.n_layers && qkv_split)
+      prefetch_qkv_split(bt, reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows);
+    else if (l + 1 < a.n_layers)
       prefetch(bt, reinterpret_cast<const bf16*>(layers[l + 1].w_qkv), a.hidden, qkv_rows);
     else if (a.head)
       prefetch(bt, reinterpret_cast<const bf16*>(a.lm_head), a.hidden, a.vocab_local);

@@ -74,3 +74,37 @@ def test_step_options_bit_identical(jsx, cuda, glm_2layer, B):
     pts = tph.cpu().numpy().reshape(nl, 5, 3)
     assert int(pts.min()) > 0
     assert np.all(np.diff(pts, axis=2) >= 0)
+
+
+def test_qkv_split_matches_per_op(jsx, cuda):
+    """hidden 4096 with 8 query heads: 768 q/k/v rows are few enough that the
+    whole-step kernel splits their K over warp pairs (both halves prefetched at
+    the barrier), as it does at tensor parallelism >= 2 with the GLM-4-9B shape;
+    the per-op GEMV keeps one warp per row pair.  The two differ only in the fp32
+    summation order of the projection, so teacher-forced logits agree to within
+    bf16 rounding."""
+    cfg = jsx.ModelConfig(hidden_size=4096, num_hidden_layers=2, num_attention_heads=8, num_key_value_heads=2,
+                          head_dim=128, intermediate_size=2048, vocab_size=4096)
+    model = jsx.GLM4ForCausalLM(cfg, jsx.create_mesh(1))
+    model.load_state(jsx.weights.random_reference_params(cfg, seed=5))
+    prompt = np.random.default_rng(9).integers(0, cfg.vocab_size, (1, 12))
+    logits = {}
+    for fused in (False, True):
+        model.fused_step = fused
+        st = jsx.DecodeState(model, 1, 16, want_logits=True)
+        out = []
+        for s in range(prompt.shape[1]):
+            st.ids.copy_(torch.from_numpy(prompt[:, s].astype(np.int32)))
+            model.step(st, head=True)
+            out.append(st.logits.float().cpu().numpy().copy())
+        logits[fused] = np.stack(out)
+    model.fused_step = True
+    a, b = logits[False], logits[True]
+    assert np.all(np.isfinite(b))
+    scale = float(np.abs(a).max())
+    assert float(np.abs(a - b).max()) <= 0.02 * scale
+    cos = (a * b).sum(-1) / (np.linalg.norm(a, axis=-1) * np.linalg.norm(b, axis=-1))
+    assert float(cos.min()) > 0.9999
+    status = __import__("ctypes").c_int(-1)
+    jsx._lib.call("jsx_device_error", __import__("ctypes").byref(status))
+    assert status.value == 0
