@@ -153,29 +153,40 @@ __device__ __forceinline__ float ll_get(const CommDev& c, const unsigned long lo
   }
 }
 
-// Slow path of ll_sum_ranks: every slot polled in rank order (bounded by the
-// comm timeout; on timeout the error word is set and the slot counts as 0).
+// Slow path of ll_sum_ranks (bounded by the comm timeout; on timeout the error
+// word is set and a slot without the epoch counts as 0).
 static __device__ __noinline__ float ll_sum_ranks_poll(const unsigned long long* p0, size_t sstride, int world,
                                                 uint32_t* state, unsigned long long timeout_ns, uint32_t epoch) {
-  float s = 0.f;
+  // every slot still without the epoch is reloaded, all in flight together (one
+  // round trip per pass), until all carry it; then the rank-ordered sum
+  unsigned long long w[kMaxRanks];
+#pragma unroll
+  for (int src = 0; src < kMaxRanks; ++src) w[src] = 0ull;
   const uint64_t t0 = globaltimer();
-  for (int src = 0; src < world; ++src) {
-    const unsigned long long* p = p0 + src * sstride;
-    unsigned long long w;
-    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
-    for (uint32_t it = 1; (uint32_t)(w >> 32) != epoch; ++it) {
+  bool all = false;
+#pragma unroll 1
+  for (uint32_t it = 1; !all; ++it) {
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src)
+      if (src < world && (uint32_t)(w[src] >> 32) != epoch)
+        asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w[src]) : "l"(p0 + src * sstride) : "memory");
+    all = true;
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src)
+      if (src < world) all = all && (uint32_t)(w[src] >> 32) == epoch;
+    if (!all && (it & 15u) == 0) {
       if (*reinterpret_cast<volatile uint32_t*>(state + kError)) break;
-      if ((it & 15u) == 0) {
-        if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
-          atomicOr(state + kError, 1u);
-          break;
-        }
-        __nanosleep(20);
+      if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
+        atomicOr(state + kError, 1u);
+        break;
       }
-      asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+      __nanosleep(20);
     }
-    s += (uint32_t)(w >> 32) == epoch ? __uint_as_float((uint32_t)w) : 0.f;
   }
+  float s = 0.f;
+#pragma unroll
+  for (int src = 0; src < kMaxRanks; ++src)
+    if (src < world) s += (uint32_t)(w[src] >> 32) == epoch ? __uint_as_float((uint32_t)w[src]) : 0.f;
   return s;
 }
 

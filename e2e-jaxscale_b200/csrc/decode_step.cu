@@ -319,26 +319,32 @@ __device__ __noinline__ void allreduce_rows_impl(bf16* h, int n, const unsigned 
       }
     }
     if (!all) {
-      // some push has not landed yet: poll every slot in rank order (bounded by the comm timeout)
-      s = 0.f;
+      // some push has not landed yet: reload every slot still without the
+      // epoch, all in flight together (one round trip per pass), until all
+      // carry it; bounded by the comm timeout and the error word
       const uint64_t t0 = globaltimer();
 #pragma unroll 1
-      for (int src = 0; src < world; ++src) {
-        const unsigned long long* p = p0 + src * sstride;
-        unsigned long long v = ll_load(p);
-        for (uint32_t it = 1; (uint32_t)(v >> 32) != epoch; ++it) {
+      for (uint32_t it = 1; !all; ++it) {
+#pragma unroll
+        for (int src = 0; src < kMaxRanks; ++src)
+          if (src < world && (uint32_t)(w[src] >> 32) != epoch) w[src] = ll_load(p0 + src * sstride);
+        all = true;
+#pragma unroll
+        for (int src = 0; src < kMaxRanks; ++src)
+          if (src < world) all = all && (uint32_t)(w[src] >> 32) == epoch;
+        if (!all && (it & 15u) == 0) {
           if (*reinterpret_cast<volatile uint32_t*>(state + kError)) break;
-          if ((it & 15u) == 0) {
-            if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
-              atomicOr(state + kError, 1u);
-              break;
-            }
-            __nanosleep(20);
+          if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
+            atomicOr(state + kError, 1u);
+            break;
           }
-          v = ll_load(p);
+          __nanosleep(20);
         }
-        s += (uint32_t)(v >> 32) == epoch ? __uint_as_float((uint32_t)v) : 0.f;
       }
+      s = 0.f;
+#pragma unroll
+      for (int src = 0; src < kMaxRanks; ++src)
+        if (src < world) s += (uint32_t)(w[src] >> 32) == epoch ? __uint_as_float((uint32_t)w[src]) : 0.f;
     }
     *hp = __float2bfloat16_rn(h0 + rbf(s));
   }

@@ -451,6 +451,49 @@ __device__ __noinline__ uint32_t ll_wait_raw(uint32_t* state, unsigned long long
   }
 }
 
+// Rank-ordered sums of one bf16 pair's LL slots (source src at p0 + src *
+// sstride) once all carry `epoch`: every slot still without it is reloaded,
+// all in flight together (one round trip per pass).  Bounded: on timeout (or
+// when an earlier wait of this rank gave up) the error word is set and the
+// missing slots count as 0.
+__device__ __noinline__ float2 ll_sum_pairs_poll(uint32_t* state, unsigned long long timeout_ns,
+                                                 const unsigned long long* p0, size_t sstride, int W,
+                                                 uint32_t epoch) {
+  unsigned long long w[kMaxRanks];
+#pragma unroll
+  for (int src = 0; src < kMaxRanks; ++src) w[src] = 0ull;
+  const uint64_t t0 = globaltimer();
+  bool all = false;
+#pragma unroll 1
+  for (uint32_t it = 1; !all; ++it) {
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src)
+      if (src < W && (uint32_t)(w[src] >> 32) != epoch) w[src] = ll_load_raw(p0 + src * sstride);
+    all = true;
+#pragma unroll
+    for (int src = 0; src < kMaxRanks; ++src)
+      if (src < W) all = all && (uint32_t)(w[src] >> 32) == epoch;
+    if (!all && (it & 15u) == 0) {
+      if (*reinterpret_cast<volatile uint32_t*>(state + kError)) break;
+      if (globaltimer() - t0 > timeout_ns || it > (1u << 28)) {
+        atomicOr(state + kError, 1u);
+        break;
+      }
+      __nanosleep(20);
+    }
+  }
+  float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+  for (int src = 0; src < kMaxRanks; ++src) {
+    if (src < W) {
+      const uint32_t pv = (uint32_t)(w[src] >> 32) == epoch ? (uint32_t)w[src] : 0u;
+      s0 += __uint_as_float(pv << 16);
+      s1 += __uint_as_float(pv & 0xffff0000u);
+    }
+  }
+  return make_float2(s0, s1);
+}
+
 __global__ void __launch_bounds__(256) k_tc_rows_allreduce(GemvArgs a, const float* __restrict__ part, CommDev c) {
   pdl_wait();
   pdl_launch_dependents();
@@ -480,16 +523,20 @@ __global__ void __launch_bounds__(256) k_tc_rows_allreduce(GemvArgs a, const flo
     for (int src = 0; src < kMaxRanks; ++src)
       if (src < W) w[src] = ll_load_raw(mine + ((size_t)src * c.max_tokens + m) * ppr + pl);
     float s0 = 0.f, s1 = 0.f;
+    bool all = true;
 #pragma unroll
     for (int src = 0; src < kMaxRanks; ++src) {
       if (src < W) {
-        const uint32_t pv = (uint32_t)(w[src] >> 32) == epoch
-                                ? (uint32_t)w[src]
-                                : ll_wait_raw(c.state, c.timeout_ns, mine + ((size_t)src * c.max_tokens + m) * ppr + pl,
-                                              epoch);
-        s0 += __uint_as_float(pv << 16);
-        s1 += __uint_as_float(pv & 0xffff0000u);
+        all = all && (uint32_t)(w[src] >> 32) == epoch;
+        s0 += __uint_as_float((uint32_t)w[src] << 16);
+        s1 += __uint_as_float((uint32_t)w[src] & 0xffff0000u);
       }
+    }
+    if (!all) {
+      const float2 sp = ll_sum_pairs_poll(c.state, c.timeout_ns, mine + (size_t)m * ppr + pl,
+                                          (size_t)c.max_tokens * ppr, W, epoch);
+      s0 = sp.x;
+      s1 = sp.y;
     }
     const uint32_t hn = pack2(__uint_as_float(hv << 16) + rbf(s0), __uint_as_float(hv & 0xffff0000u) + rbf(s1));
     *hp = hn;
