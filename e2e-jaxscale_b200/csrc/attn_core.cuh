@@ -136,7 +136,7 @@ __device__ __forceinline__ uint32_t attn_ld_acquire(const uint32_t* p) {
   return v;
 }
 
-constexpr int kSeg = 16;  // splits of one head staged at a time by the distributed merge
+constexpr int kSeg = 32;  // splits of one head staged at a time by the distributed merge
 
 template <int NT>
 __device__ __forceinline__ void attn_finish_distributed(const AttnArgs& a, int vb, int s, int b, int head0,

@@ -503,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_decode_step(jsx_decode_step_arg
   // split CTAs of a group wait for one another), the tensor-core item (its
   // shared memory holds the merge's weights and kSeg staged accumulators)
   at.dist_err = (!cmerge && !(opts & kOptLastMerge) && attn_items <= (int)gridDim.x &&
-                 attn_use_mma(lay.gi, a.head_dim) && lay.splits <= 4096)
+                 attn_use_mma(lay.gi, a.head_dim) && lay.splits <= 2048)
                     ? &g_step_error
                     : nullptr;
   const bool attn_pre = attn_use_mma(lay.gi, a.head_dim) && (int)blockIdx.x < attn_items;
