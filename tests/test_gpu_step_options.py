@@ -1,7 +1,7 @@
 """Options of the whole-step decode kernel that change how it moves data, not
 what it computes: the attention's split merge done by the o_proj staging
-(JSX_STEP_CMERGE) or by the last split alone (JSX_STEP_DMERGE=0, instead of
-every split merging a share of the heads), the L2 prefetch of the next projection's rows
+(JSX_STEP_CMERGE) or by every split merging a share of the heads
+(JSX_STEP_DMERGE=1, instead of the last split merging them all), the L2 prefetch of the next projection's rows
 (l2_next_bytes / l2_attn_bytes) and the traces (trace_ar, trace_phase).  Each must
 give bit-identical logits and ids to the default kernel on the same inputs.
 The options are read per launch, so one process compares them."""
@@ -55,7 +55,7 @@ def test_step_options_bit_identical(jsx, cuda, glm_2layer, B):
         st.step_args.trace_ar = tar.data_ptr()
         st.step_args.trace_phase = tph.data_ptr()
 
-    variants = [("JSX_STEP_CMERGE", "1", None), ("JSX_STEP_DMERGE", "0", None), (None, None, with_l2_and_trace)]
+    variants = [("JSX_STEP_CMERGE", "1", None), ("JSX_STEP_DMERGE", "1", None), (None, None, with_l2_and_trace)]
     for env, val, setup in variants:
         if env:
             os.environ[env] = val
