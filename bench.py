@@ -791,31 +791,57 @@ def measure_rowpar(jsx, mesh, dev, world: int, rank: int, steps: int, warmup: in
 def run_configs(jsx, model, mesh, dev, world: int, rank: int, args) -> dict:
     """Short runs of configurations 2, 3 and 4 at this GPU count after the decode
     measurement (same processes, same mesh for 2 and 3; TP = min(2, N) x EP = N / TP for
-    4), summarised compactly for the JSON line."""
+    4), summarised compactly for the JSON line.  A configuration that raises is recorded
+    as `<name>_error` and the ones after it are skipped (every rank agrees first); the
+    decode measurement, already taken, stands."""
     import torch
+    import torch.distributed as dist
 
     out = {}
-    rp = measure_rowpar(jsx, mesh, dev, world, rank, steps=20, warmup=3)
-    out["rowpar_us"] = {f"{r['op']}_M{r['M']}": [round(r["fused_us"], 1), round(r["gemm_nccl_us"], 1)]
-                        + ([round(r["gemm_only_us"], 1), round(r["nccl_allreduce_us"], 1)] if "gemm_only_us" in r
-                           else []) for r in rp}
-    out["rowpar_note"] = ("[fused, cuBLAS+NCCL(, fused product without the exchange, NCCL all-reduce alone)] "
-                          "us per call, configuration 2, K split over the N ranks")
-    hid = {f"{r['op']}_M{r['M']}": round(r["hidden_frac"], 3) for r in rp if "hidden_frac" in r}
-    if hid:
-        out["allreduce_hidden_frac"] = hid
-    out["rowpar_max_rel_err"] = round(max(r["rel_err"] for r in rp), 5)
-    pf = measure_prefill(jsx, model, dev, world, 32, 1024, steps=2, warmup=1)
-    out["prefill_32x1024"] = {"tok_s": round(pf["value"], 1), "ms": round(pf["ms_per_prefill"], 2),
-                              "mfu": round(pf["mfu"], 4), "tflops_per_gpu": round(pf["achieved_tflops_per_gpu"], 1)}
-    torch.cuda.empty_cache()
-    tp = min(2, world)
-    fmesh = jsx.create_mesh(tp=tp, ep=world // tp)
-    fl = measure_flash(jsx, fmesh, dev, world, args.ctx, steps=20, warmup=3, seed=args.seed, vocab=args.vocab)
-    fmesh.close()
-    out["flash_tok_s"] = {k: round(v["value"], 1) for k, v in fl.items()}
-    out["flash_mesh"] = f"tp{tp}xep{world // tp}"
-    torch.cuda.empty_cache()
+
+    def rowpar():
+        rp = measure_rowpar(jsx, mesh, dev, world, rank, steps=20, warmup=3)
+        out["rowpar_us"] = {f"{r['op']}_M{r['M']}": [round(r["fused_us"], 1), round(r["gemm_nccl_us"], 1)]
+                            + ([round(r["gemm_only_us"], 1), round(r["nccl_allreduce_us"], 1)]
+                               if "gemm_only_us" in r else []) for r in rp}
+        out["rowpar_note"] = ("[fused, cuBLAS+NCCL(, fused product without the exchange, NCCL all-reduce "
+                              "alone)] us per call, configuration 2, K split over the N ranks")
+        hid = {f"{r['op']}_M{r['M']}": round(r["hidden_frac"], 3) for r in rp if "hidden_frac" in r}
+        if hid:
+            out["allreduce_hidden_frac"] = hid
+        out["rowpar_max_rel_err"] = round(max(r["rel_err"] for r in rp), 5)
+
+    def prefill():
+        pf = measure_prefill(jsx, model, dev, world, 32, 1024, steps=2, warmup=1)
+        out["prefill_32x1024"] = {"tok_s": round(pf["value"], 1), "ms": round(pf["ms_per_prefill"], 2),
+                                  "mfu": round(pf["mfu"], 4), "tflops_per_gpu": round(pf["achieved_tflops_per_gpu"], 1)}
+
+    def flash():
+        tp = min(2, world)
+        out["flash_mesh"] = f"tp{tp}xep{world // tp}"
+        fmesh = jsx.create_mesh(tp=tp, ep=world // tp)
+        try:
+            fl = measure_flash(jsx, fmesh, dev, world, args.ctx, steps=20, warmup=3, seed=args.seed,
+                               vocab=args.vocab)
+        finally:
+            fmesh.close()
+        out["flash_tok_s"] = {k: round(v["value"], 1) for k, v in fl.items()}
+
+    for name, fn in (("rowpar", rowpar), ("prefill", prefill), ("flash", flash)):
+        err = None
+        try:
+            fn()
+        except Exception as e:  # noqa: BLE001 - reported in the line; the decode numbers stand
+            err = f"{type(e).__name__}: {e}"[:300]
+            out[f"{name}_error"] = err
+        torch.cuda.empty_cache()
+        failed = torch.tensor([1.0 if err else 0.0], device=dev)
+        if world > 1:
+            dist.all_reduce(failed)
+        if failed.item() > 0:
+            if err is None:
+                out[f"{name}_error"] = "failed on another rank"
+            break
     return out
 
 
