@@ -242,27 +242,52 @@ __device__ __forceinline__ float pick(const float (&acc)[kRows][M], int r, int m
 // qkv packing (jsx_pack_qkv): per head hd/2 groups; group j < rot/2 holds rows
 // (j, j + rot/2) (a neox rotary pair), group j >= rot/2 holds the pass-through
 // pair (rot + 2(j - rot/2), +1).  Heads: q (nq), then k (nkv), then v (nkv).
-__device__ __forceinline__ void qkv_store(const GemvArgs& a, int g, int m, float acc0, float acc1) {
-  const int gph = a.hd >> 1;
-  const int head = g / gph, j = g - head * gph;
-  const int rh = a.rot >> 1;
-  int d0, d1;
+// Columns (in q | k | v order) of packed row pair g: its head and the two
+// dimensions d0, d1; rotary pairs first.
+struct QkvCols {
+  int head, j, d0, d1;
   bool rotary;
-  if (j < rh) { d0 = j; d1 = j + rh; rotary = true; }
-  else { d0 = a.rot + 2 * (j - rh); d1 = d0 + 1; rotary = false; }
-  const int col0 = head * a.hd + d0, col1 = head * a.hd + d1;  // index into q|k|v
+};
+__device__ __forceinline__ QkvCols qkv_cols(const GemvArgs& a, int g) {
+  QkvCols q;
+  const int gph = a.hd >> 1;
+  q.head = g / gph;
+  q.j = g - q.head * gph;
+  const int rh = a.rot >> 1;
+  if (q.j < rh) { q.d0 = q.j; q.d1 = q.j + rh; q.rotary = true; }
+  else { q.d0 = a.rot + 2 * (q.j - rh); q.d1 = q.d0 + 1; q.rotary = false; }
+  return q;
+}
+
+// The bias pair of packed row pair g (0 without a bias).
+__device__ __forceinline__ void qkv_bias_pair(const GemvArgs& a, int g, float& b0, float& b1) {
+  b0 = b1 = 0.f;
+  if (a.bias) {
+    const QkvCols q = qkv_cols(a, g);
+    b0 = ldbf(a.bias + q.head * a.hd + q.d0);
+    b1 = ldbf(a.bias + q.head * a.hd + q.d1);
+  }
+}
+
+// Epilogue of row pair g for token m with its bias pair already loaded (b0, b1
+// are read only when a.bias is set); positions and rotary frequencies from
+// `pos` / `inv_freq` (a.pos / a.inv_freq, or copies of them in shared memory).
+__device__ __forceinline__ void qkv_store_b(const GemvArgs& a, int g, int m, float acc0, float acc1, float b0,
+                                            float b1, const int32_t* pos, const float* inv_freq) {
+  const QkvCols q = qkv_cols(a, g);
+  const int head = q.head, j = q.j, d0 = q.d0, d1 = q.d1;
   float x1 = rbf(acc0);
   float x2 = rbf(acc1);
   if (a.bias) {
-    x1 = rbf(x1 + ldbf(a.bias + col0));
-    x2 = rbf(x2 + ldbf(a.bias + col1));
+    x1 = rbf(x1 + b0);
+    x2 = rbf(x2 + b1);
   }
-  const int p = a.pos[m];
+  const int p = pos[m];
   const bool is_v = head >= a.nq + a.nkv;
-  if (rotary && !is_v) {
+  if (q.rotary && !is_v) {
     // layers/rotary.py:56-58 (fp32 angle, bf16 cos/sin) and :88-91 (half split)
     float s, c;
-    sincosf((float)p * a.inv_freq[j], &s, &c);
+    sincosf((float)p * inv_freq[j], &s, &c);
     c = rbf(c);
     s = rbf(s);
     const float o1 = rbf(rbf(x1 * c) - rbf(x2 * s));
@@ -271,9 +296,9 @@ __device__ __forceinline__ void qkv_store(const GemvArgs& a, int g, int m, float
     x2 = o2;
   }
   if (head < a.nq) {
-    bf16* q = a.y + (size_t)m * a.nq * a.hd + head * a.hd;
-    q[d0] = __float2bfloat16_rn(x1);
-    q[d1] = __float2bfloat16_rn(x2);
+    bf16* qo = a.y + (size_t)m * a.nq * a.hd + head * a.hd;
+    qo[d0] = __float2bfloat16_rn(x1);
+    qo[d1] = __float2bfloat16_rn(x2);
   } else {
     const int kvh = is_v ? head - a.nq - a.nkv : head - a.nq;
     const int b = m / a.tps;
@@ -283,6 +308,12 @@ __device__ __forceinline__ void qkv_store(const GemvArgs& a, int g, int m, float
     dst[d0] = __float2bfloat16_rn(x1);
     dst[d1] = __float2bfloat16_rn(x2);
   }
+}
+
+__device__ __forceinline__ void qkv_store(const GemvArgs& a, int g, int m, float acc0, float acc1) {
+  float b0, b1;
+  qkv_bias_pair(a, g, b0, b1);
+  qkv_store_b(a, g, m, acc0, acc1, b0, b1, a.pos, a.inv_freq);
 }
 
 // gate/up packing (jsx_pack_gate_up): group j holds rows (gate_j, up_j).

@@ -59,6 +59,7 @@ constexpr int kTcStages = 8;
 constexpr int kTcThreads = 192;
 constexpr int kTcMaxM = 32;
 constexpr int kTcMaxCluster = 8;
+constexpr int kTcMaxInvFreq = 128;  // rotary frequencies staged in shared memory by the q/k/v epilogue
 constexpr uint32_t kTcABytes = kTcBM * kTcBK * 2;
 constexpr uint32_t kTcBBytes = kTcBN * kTcBK * 2;
 constexpr uint32_t kTcStageBytes = kTcABytes + kTcBBytes;
@@ -247,6 +248,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
     const int r = 32 * q + lane;  // tile row held after tcgen05.ld
     const int pp0 = (int)(rank * 64 / S), np = (int)((rank + 1) * 64 / S) - pp0;  // row pairs finished here
     pdl_wait();  // the epilogue reads and writes what earlier kernels use
+    // q/k/v: the positions and rotary frequencies every entry reads, copied to
+    // shared memory once
+    const int32_t* pos_e = a.pos;
+    const float* invf_e = a.inv_freq;
+    if constexpr (EPI == EPI_QKV) {
+      __shared__ int32_t s_pos[kTcMaxM];
+      __shared__ float s_invf[kTcMaxInvFreq];
+      if (!t.store_only) {
+        if (et < t.M) s_pos[et] = a.pos[et];
+        const int nf = a.rot >> 1;
+        if (nf <= kTcMaxInvFreq)
+          for (int i = et; i < nf; i += 128) s_invf[i] = a.inv_freq[i];
+        epi_sync();
+        pos_e = s_pos;
+        if (nf <= kTcMaxInvFreq) invf_e = s_invf;
+      }
+    }
     uint32_t ai = 0;
     for (int tile = cid; tile < t.tiles; tile += ncl, ++ai) {
       const uint32_t b = ai & 1;
@@ -322,27 +340,51 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_tc_gemm(const __grid_constant
                 pack2(__uint_as_float(hv[u] << 16) + rbf(w0), __uint_as_float(hv[u] & 0xffff0000u) + rbf(w1));
           }
         }
-      } else
-      for (int e = et; e < np * t.M; e += 128) {
-        const int m = e / np, p = pp0 + (e - m * np);
-        const uint32_t off = (uint32_t)(m * kTcBM + 2 * p) * 4u;
-        float v0 = 0.f, v1 = 0.f;
+      } else {
+        // four entries at a time: their partial sums (and q/k/v bias pairs) are
+        // all loaded before any entry's epilogue, so the loads of one batch
+        // share a round trip instead of one per entry
+        for (int e0 = et; e0 < np * t.M; e0 += 4 * 128) {
+          float v0[4], v1[4], b0[4], b1[4];
+          int mm[4], rr[4];
 #pragma unroll
-        for (int s = 0; s < kTcMaxCluster; ++s) {
-          if (s < S) {
-            const float2 f = cl_ld2(src[s] + off);
-            v0 += f.x;
-            v1 += f.y;
+          for (int u = 0; u < 4; ++u) {
+            const int e = e0 + 128 * u;
+            v0[u] = v1[u] = b0[u] = b1[u] = 0.f;
+            mm[u] = 0;
+            rr[u] = -1;
+            if (e < np * t.M) {
+              const int m = e / np, p = pp0 + (e - m * np);
+              const uint32_t off = (uint32_t)(m * kTcBM + 2 * p) * 4u;
+#pragma unroll
+              for (int s = 0; s < kTcMaxCluster; ++s) {
+                if (s < S) {
+                  const float2 f = cl_ld2(src[s] + off);
+                  v0[u] += f.x;
+                  v1[u] += f.y;
+                }
+              }
+              const int row0 = tile * kTcBM + 2 * p;
+              if (row0 < t.N) {
+                rr[u] = row0;
+                mm[u] = m;
+                if (EPI == EPI_QKV && !t.store_only) qkv_bias_pair(a, row0 >> 1, b0[u], b1[u]);
+              }
+            }
           }
-        }
-        const int row0 = tile * kTcBM + 2 * p;
-        if (row0 < t.N) {
-          if (t.store_only) {
-            t.part[(size_t)m * t.N + row0] = v0;
-            t.part[(size_t)m * t.N + row0 + 1] = v1;
-          } else {
-            const unsigned long long key = epi_pair<EPI>(a, c, false, 0u, row0 >> 1, m, v0, v1);
-            if (EPI == EPI_LMHEAD && key) atomicMax(best + m, key);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (rr[u] < 0) continue;
+            const int m = mm[u], row0 = rr[u];
+            if (t.store_only) {
+              t.part[(size_t)m * t.N + row0] = v0[u];
+              t.part[(size_t)m * t.N + row0 + 1] = v1[u];
+            } else if constexpr (EPI == EPI_QKV) {
+              qkv_store_b(a, row0 >> 1, m, v0[u], v1[u], b0[u], b1[u], pos_e, invf_e);
+            } else {
+              const unsigned long long key = epi_pair<EPI>(a, c, false, 0u, row0 >> 1, m, v0[u], v1[u]);
+              if (EPI == EPI_LMHEAD && key) atomicMax(best + m, key);
+            }
           }
         }
       }
